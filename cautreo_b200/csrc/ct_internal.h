@@ -1,0 +1,161 @@
+/*
+ * ct_internal.h -- internal interface between the C11 host layer
+ * (cautreo_b200/host) and the CUDA kernels (cautreo_b200/csrc).
+ * Plain C declarations; device helpers only when compiled by nvcc.
+ */
+#ifndef CT_INTERNAL_H
+#define CT_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- bookkeeping shared by every launcher (host/runtime.c) ------------- */
+/* Records a CUDA error (code from cudaError_t) with a location; returns
+ * CT_ERR_CUDA (or CT_OK when code == 0). */
+int  ct__cuda_status(int code, const char *where);
+void ct__count_launches(uint32_t n);
+/* Sets the last-error message without a CUDA code. */
+void ct__set_error(const char *msg);
+
+/* ---- MLA decode work plan (shared by host/attention.c and the kernels) -- */
+typedef struct {
+    int32_t seq;         /* output row */
+    int32_t row;         /* block-table row */
+    int32_t page_begin;  /* first logical page of the chunk */
+    int32_t page_end;    /* one past the last */
+    int32_t part;        /* partial-result slot, or -1: write the final output */
+    int32_t pad[3];
+} ct_mla_chunk_t;
+
+typedef struct {
+    int32_t seq;         /* output row */
+    int32_t first_part;  /* first partial-result slot */
+    int32_t n_parts;
+    int32_t pad;
+} ct_mla_combine_t;
+
+typedef struct {
+    uint32_t n_heads, entry_dim, v_dim, page_tokens, max_pages_per_seq, kv_dtype;
+    float    scale;
+} ct_mla_dims_t;
+
+/* ---- launchers (csrc); all return a ct_status_t ------------------------- */
+int ct__launch_kv_gather(const void *pool, const float *scales, uint32_t pool_dtype,
+                         const int32_t *bt_row, uint32_t page_tokens, uint32_t dim,
+                         uint32_t start, uint32_t n, void *out, uint32_t out_dtype,
+                         void *stream);
+int ct__launch_kv_compress(float *k, float *v, float *scratch, uint32_t n_layers,
+                           uint32_t max_ctx, uint32_t stride, uint32_t new_len,
+                           uint32_t step, void *stream);
+
+int ct__launch_q_blocks(int type, const float *x, void *blocks, int64_t n, void *stream);
+int ct__launch_deq_blocks(int type, const void *blocks, float *x, int64_t n, void *stream);
+
+int ct__launch_attn_shared(const float *q, const float *k, const float *v, uint32_t n_tokens,
+                           uint32_t n_heads, uint32_t head_dim, float scale, float *out,
+                           float *scratch_scores, void *stream);
+int ct__launch_softmax(float *x, uint32_t n, void *stream);
+
+int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks,
+                          uint32_t n_chunks, const int32_t *worker_begin, uint32_t n_workers,
+                          const ct_mla_combine_t *combines,
+                          uint32_t n_combines, const void *q, const void *pool,
+                          const float *scales, const int32_t *block_table,
+                          const int32_t *seq_lens, void *out, float *lse, float *part_o,
+                          float *part_ml, void *stream, uint32_t *n_launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+/* ------------------------------------------------------------------------ */
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#define CT_DEV __device__ __forceinline__
+
+/* bf16 bits -> fp32 (exact). */
+CT_DEV float ct_bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+/* fp32 -> bf16 bits, round to nearest even on the dropped 16 bits; the same
+ * integer rule as the reference's f32_to_bf16 (ds4_forward.c:60-66). */
+CT_DEV uint16_t ct_f32_to_bf16(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+/* The reference fp16 scale encoder (quant.c:16-45), including its
+ * truncation and the unsigned exponent wrap that turns |x| < 2^-15 into Inf. */
+CT_DEV uint16_t ct_ref_f32_to_fp16(float f) {
+    uint32_t u = __float_as_uint(f);
+    uint32_t sgn = (u >> 31) & 1u, e = (u >> 23) & 0xFFu, m = u & 0x7FFFFFu;
+    if (e == 0) return (uint16_t)(sgn << 15);
+    if (e == 0xFF) return (uint16_t)((sgn << 15) | 0x7C00u | (m >> 13));
+    uint32_t ne = e - 112u;
+    if (ne >= 31u) return (uint16_t)((sgn << 15) | 0x7C00u);
+    if (ne == 0u) return (uint16_t)((sgn << 15) | (((m | 0x800000u) >> 1) >> 13));
+    return (uint16_t)((sgn << 15) | (ne << 10) | (m >> 13));
+}
+
+/* The reference fp16 decoder (quant.c:47-75), subnormal rule included. */
+CT_DEV float ct_ref_fp16_to_f32(uint16_t h) {
+    uint32_t sgn = (h >> 15) & 1u, e = (h >> 10) & 0x1Fu, m = h & 0x3FFu, u;
+    if (e == 0) {
+        if (m == 0) u = sgn << 31;
+        else {
+            uint32_t ex = 112u;
+            while (!(m & 0x400u)) { m <<= 1; ex--; }
+            u = (sgn << 31) | (ex << 23) | ((m & 0x3FFu) << 13);
+        }
+    } else if (e == 31) {
+        u = (sgn << 31) | 0x7F800000u | (m << 13);
+    } else {
+        u = (sgn << 31) | ((e + 112u) << 23) | (m << 13);
+    }
+    return __uint_as_float(u);
+}
+
+/* int8 code with the Q8_0 rounding: floor(x*id + 0.5), clamp +/-127, every
+ * operation individually rounded (no FMA contraction). */
+CT_DEV int ct_q8_code(float x, float id) {
+    int q = (int)floorf(__fadd_rn(__fmul_rn(x, id), 0.5f));
+    return q > 127 ? 127 : (q < -127 ? -127 : q);
+}
+
+/* e4m3 code of x * id, round-to-nearest-even, saturating to +/-448. */
+CT_DEV uint8_t ct_e4m3_code(float x, float id) {
+    return (uint8_t)__nv_cvt_float_to_fp8(__fmul_rn(x, id), __NV_SATFINITE, __NV_E4M3);
+}
+
+CT_DEV float ct_e4m3_to_f32(uint8_t v) {
+    __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)v, __NV_E4M3);
+    return __half2float(__half(hr));
+}
+
+CT_DEV float ct_warp_max(float v) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+
+CT_DEV float ct_warp_sum(float v) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+static inline int ct__grid_for(size_t items, int per_block, int cap) {
+    size_t g = (items + per_block - 1) / per_block;
+    if (g < 1) g = 1;
+    if ((size_t)cap < g) g = cap;
+    return (int)g;
+}
+#endif /* __CUDACC__ */
+
+#endif /* CT_INTERNAL_H */

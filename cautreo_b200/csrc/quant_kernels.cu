@@ -1,0 +1,213 @@
+/*
+ * quant_kernels.cu -- block codecs of src/quant/quant.c on the device, and
+ * the per-token KV codecs.
+ *
+ * Block codecs (Q8_0 / Q4_0 / Q2_0 / Q1_0, 32 values per block): one thread
+ * per block, the reference's arithmetic step for step (quant.c:77-249):
+ * d = amax / qmax in fp32, the fp16 scale from the reference's truncating
+ * encoder, codes from the fp32 d via floor(x * (1/d) + 0.5) with every
+ * operation individually rounded, and decode with the fp16-rounded scale.
+ * Block layout: u16 scale followed by the packed codes (34 / 18 / 10 / 6 B).
+ *
+ * Per-token codecs: one warp per token, absmax by warp shuffle.
+ */
+#include "../../include/hal.h"
+#include "../../include/quant.h"
+#include "ct_internal.h"
+
+namespace {
+
+__device__ __forceinline__ float block_amax(const float *x) {
+    float amax = 0.0f;
+    #pragma unroll 8
+    for (int i = 0; i < 32; i++) { float a = fabsf(x[i]); if (a > amax) amax = a; }
+    return amax;
+}
+
+__device__ __forceinline__ int qround(float x, float id, int lim) {
+    int q = (int)floorf(__fadd_rn(__fmul_rn(x, id), 0.5f));
+    return q > lim ? lim : (q < -lim ? -lim : q);
+}
+
+__device__ __forceinline__ void put_scale(uint8_t *blk, uint16_t h) { blk[0] = (uint8_t)h; blk[1] = (uint8_t)(h >> 8); }
+__device__ __forceinline__ float get_scale(const uint8_t *blk) {
+    return ct_ref_fp16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+}
+
+template <int Type>
+__global__ void k_quant_blocks(const float *src, uint8_t *dst, int64_t nb) {
+    constexpr int kBytes = Type == CT_QUANT_Q8_0 ? 34 : Type == CT_QUANT_Q4_0 ? 18 : Type == CT_QUANT_Q2_0 ? 10 : 6;
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+        const float *x = src + b * 32;
+        uint8_t *blk = dst + b * kBytes;
+        const float amax = block_amax(x);
+        if (Type == CT_QUANT_Q1_0) {
+            put_scale(blk, ct_ref_f32_to_fp16(amax));
+            for (int i = 0; i < 32; i += 8) {
+                uint32_t byte = 0;
+                for (int j = 0; j < 8; j++) if (x[i + j] >= 0) byte |= 1u << j;
+                blk[2 + i / 8] = (uint8_t)byte;
+            }
+            continue;
+        }
+        const float qmax = Type == CT_QUANT_Q8_0 ? 127.0f : Type == CT_QUANT_Q4_0 ? 7.0f : 1.0f;
+        const float d = __fdiv_rn(amax, qmax);
+        put_scale(blk, ct_ref_f32_to_fp16(d));
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        if (Type == CT_QUANT_Q8_0) {
+            for (int i = 0; i < 32; i++) blk[2 + i] = (uint8_t)(int8_t)qround(x[i], id, 127);
+        } else if (Type == CT_QUANT_Q4_0) {
+            for (int i = 0; i < 32; i += 2) {
+                int q0 = qround(x[i], id, 7), q1 = qround(x[i + 1], id, 7);
+                blk[2 + i / 2] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
+            }
+        } else {
+            for (int i = 0; i < 32; i += 4) {
+                uint32_t byte = 0;
+                for (int j = 0; j < 4; j++) byte |= (uint32_t)((qround(x[i + j], id, 1) + 1) & 3) << (2 * j);
+                blk[2 + i / 4] = (uint8_t)byte;
+            }
+        }
+    }
+}
+
+template <int Type>
+__global__ void k_dequant_blocks(const uint8_t *src, float *dst, int64_t nb) {
+    constexpr int kBytes = Type == CT_QUANT_Q8_0 ? 34 : Type == CT_QUANT_Q4_0 ? 18 : Type == CT_QUANT_Q2_0 ? 10 : 6;
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t *blk = src + b * kBytes;
+        float *x = dst + b * 32;
+        const float d = get_scale(blk);
+        for (int i = 0; i < 32; i++) {
+            int q;
+            if (Type == CT_QUANT_Q8_0) q = (int8_t)blk[2 + i];
+            else if (Type == CT_QUANT_Q4_0) { q = (blk[2 + i / 2] >> (4 * (i & 1))) & 0xF; if (q >= 8) q -= 16; }
+            else if (Type == CT_QUANT_Q2_0) q = (int)((blk[2 + i / 4] >> (2 * (i & 3))) & 3) - 1;
+            else { x[i] = (blk[2 + i / 8] >> (i & 7)) & 1 ? d : -d; continue; }
+            x[i] = __fmul_rn((float)q, d);
+        }
+    }
+}
+
+/* Per-token codecs: one warp per token, values strided by lane. */
+template <bool Int8, bool SrcBf16>
+__global__ void __launch_bounds__(256) k_quant_tokens(const void *x, uint32_t n_tok, uint32_t dim,
+                                                      uint8_t *codes, float *scales) {
+    const uint32_t t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= n_tok) return;
+    auto val = [&](uint32_t i) -> float {
+        return SrcBf16 ? ct_bf16_to_f32(static_cast<const uint16_t *>(x)[(size_t)t * dim + i])
+                       : static_cast<const float *>(x)[(size_t)t * dim + i];
+    };
+    float amax = 0.0f;
+    for (uint32_t i = lane; i < dim; i += 32) amax = fmaxf(amax, fabsf(val(i)));
+    amax = ct_warp_max(amax);
+    const float d = __fdiv_rn(amax, Int8 ? 127.0f : 448.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    for (uint32_t i = lane; i < dim; i += 32)
+        codes[(size_t)t * dim + i] = Int8 ? (uint8_t)(int8_t)ct_q8_code(val(i), id) : ct_e4m3_code(val(i), id);
+    if (lane == 0) scales[t] = d;
+}
+
+template <bool Int8>
+__global__ void k_dequant_tokens(const uint8_t *codes, const float *scales, uint32_t n_tok, uint32_t dim, float *x) {
+    const size_t total = (size_t)n_tok * dim;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const float sc = scales[i / dim];
+        const uint8_t b = codes[i];
+        x[i] = __fmul_rn(Int8 ? (float)(int8_t)b : ct_e4m3_to_f32(b), sc);
+    }
+}
+
+}  // namespace
+
+extern "C" int ct__launch_q_blocks(int type, const float *x, void *blocks, int64_t n, void *stream) {
+    if (n <= 0) return CT_OK;
+    const int64_t nb = n / 32;
+    const int grid = ct__grid_for((size_t)nb, 128, 148 * 8);
+    cudaStream_t st = (cudaStream_t)stream;
+    uint8_t *dst = static_cast<uint8_t *>(blocks);
+    switch (type) {
+        case CT_QUANT_Q8_0: k_quant_blocks<CT_QUANT_Q8_0><<<grid, 128, 0, st>>>(x, dst, nb); break;
+        case CT_QUANT_Q4_0: k_quant_blocks<CT_QUANT_Q4_0><<<grid, 128, 0, st>>>(x, dst, nb); break;
+        case CT_QUANT_Q2_0: k_quant_blocks<CT_QUANT_Q2_0><<<grid, 128, 0, st>>>(x, dst, nb); break;
+        case CT_QUANT_Q1_0: k_quant_blocks<CT_QUANT_Q1_0><<<grid, 128, 0, st>>>(x, dst, nb); break;
+        default: return CT_ERR_ARG;
+    }
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "quant_blocks");
+}
+
+extern "C" int ct__launch_deq_blocks(int type, const void *blocks, float *x, int64_t n, void *stream) {
+    if (n <= 0) return CT_OK;
+    const int64_t nb = n / 32;
+    const int grid = ct__grid_for((size_t)nb, 128, 148 * 8);
+    cudaStream_t st = (cudaStream_t)stream;
+    const uint8_t *src = static_cast<const uint8_t *>(blocks);
+    switch (type) {
+        case CT_QUANT_Q8_0: k_dequant_blocks<CT_QUANT_Q8_0><<<grid, 128, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q4_0: k_dequant_blocks<CT_QUANT_Q4_0><<<grid, 128, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q2_0: k_dequant_blocks<CT_QUANT_Q2_0><<<grid, 128, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q1_0: k_dequant_blocks<CT_QUANT_Q1_0><<<grid, 128, 0, st>>>(src, x, nb); break;
+        default: return CT_ERR_ARG;
+    }
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "dequant_blocks");
+}
+
+extern "C" int ct_quant_q8_0_dev(const float *x, void *blocks, int64_t n, void *stream) {
+    if (!x || !blocks || n < 0 || n % 32 != 0) return CT_ERR_ARG;
+    return ct__launch_q_blocks(CT_QUANT_Q8_0, x, blocks, n, stream);
+}
+
+extern "C" int ct_dequant_q8_0_dev(const void *blocks, float *x, int64_t n, void *stream) {
+    if (!x || !blocks || n < 0 || n % 32 != 0) return CT_ERR_ARG;
+    return ct__launch_deq_blocks(CT_QUANT_Q8_0, blocks, x, n, stream);
+}
+
+static int quant_tokens(bool int8, const void *x, int src_is_bf16, uint32_t n_tok, uint32_t dim,
+                        uint8_t *codes, float *scales, void *stream) {
+    if (!x || !codes || !scales || dim == 0) return CT_ERR_ARG;
+    if (n_tok == 0) return CT_OK;
+    const int grid = (int)((n_tok + 7) / 8);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (int8) {
+        if (src_is_bf16) k_quant_tokens<true, true><<<grid, 256, 0, st>>>(x, n_tok, dim, codes, scales);
+        else k_quant_tokens<true, false><<<grid, 256, 0, st>>>(x, n_tok, dim, codes, scales);
+    } else {
+        if (src_is_bf16) k_quant_tokens<false, true><<<grid, 256, 0, st>>>(x, n_tok, dim, codes, scales);
+        else k_quant_tokens<false, false><<<grid, 256, 0, st>>>(x, n_tok, dim, codes, scales);
+    }
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "quant_tokens");
+}
+
+extern "C" int ct_quant_kv_int8(const void *x, int src_is_bf16, uint32_t n_tok, uint32_t dim,
+                                int8_t *codes, float *scales, void *stream) {
+    return quant_tokens(true, x, src_is_bf16, n_tok, dim, reinterpret_cast<uint8_t *>(codes), scales, stream);
+}
+
+extern "C" int ct_quant_kv_e4m3(const void *x, int src_is_bf16, uint32_t n_tok, uint32_t dim,
+                                uint8_t *codes, float *scales, void *stream) {
+    return quant_tokens(false, x, src_is_bf16, n_tok, dim, codes, scales, stream);
+}
+
+extern "C" int ct_dequant_kv_int8(const int8_t *codes, const float *scales, uint32_t n_tok, uint32_t dim,
+                                  float *x, void *stream) {
+    if (!codes || !scales || !x) return CT_ERR_ARG;
+    if ((size_t)n_tok * dim == 0) return CT_OK;
+    const int grid = ct__grid_for((size_t)n_tok * dim, 256, 148 * 8);
+    k_dequant_tokens<true><<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint8_t *>(codes), scales, n_tok, dim, x);
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "dequant_int8");
+}
+
+extern "C" int ct_dequant_kv_e4m3(const uint8_t *codes, const float *scales, uint32_t n_tok, uint32_t dim,
+                                  float *x, void *stream) {
+    if (!codes || !scales || !x) return CT_ERR_ARG;
+    if ((size_t)n_tok * dim == 0) return CT_OK;
+    const int grid = ct__grid_for((size_t)n_tok * dim, 256, 148 * 8);
+    k_dequant_tokens<false><<<grid, 256, 0, (cudaStream_t)stream>>>(codes, scales, n_tok, dim, x);
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "dequant_e4m3");
+}

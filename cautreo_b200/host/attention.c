@@ -1,0 +1,223 @@
+/*
+ * attention.c -- attention.h on the device.
+ *
+ * Part 1: the reference's ct_attn_forward / ct_attn_forward_kv /
+ * ct_attn_softmax (src/attention/attention.c:11-59) with the same
+ * arguments, defaults and return values; inputs are copied to the device, the
+ * kernels of attn_plain.cu run, the result is copied back.
+ *
+ * Part 2: MLA decode plans.  A plan splits every sequence's pages into
+ * chunks so that each worker (a pair of SMs for the tensor-core kernel, one
+ * block per chunk and head group for the CUDA-core kernel) gets the same
+ * number of KV tokens: the sequences are laid end to end, cut into n_workers
+ * equal token ranges at page boundaries, and every range becomes the chunks
+ * of the sequences it covers.  Chunks of a split sequence write partial
+ * (o, m, l) to the plan's scratch; one combine launch merges them.
+ */
+#include "../../include/attention.h"
+#include "../../include/hal.h"
+#include "../../include/kv_cache.h"
+#include "../csrc/ct_internal.h"
+
+#include <cuda_runtime_api.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- Part 1 --------------------------------------------------------------- */
+
+bool ct_attn_forward(const float *q, const float *k, const float *v, uint32_t n_tokens, uint32_t n_kv_heads,
+                     uint32_t head_dim, float scale, float *out) {
+    if (!q || !k || !v || !out || n_tokens == 0) return false;
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)head_dim);
+    if (n_kv_heads == 0 || head_dim == 0) return true;
+    const size_t qb = (size_t)n_kv_heads * head_dim * sizeof(float);
+    const size_t kb = (size_t)n_tokens * head_dim * sizeof(float);
+    const size_t sb = (size_t)n_kv_heads * n_tokens * sizeof(float);
+    char *buf = NULL;
+    const size_t total = 2 * qb + 2 * kb + sb;
+    if (ct__cuda_status(cudaMallocAsync((void **)&buf, total, 0), "ct_attn_forward")) return false;
+    float *dq = (float *)buf, *dout = (float *)(buf + qb), *dk = (float *)(buf + 2 * qb);
+    float *dv = (float *)(buf + 2 * qb + kb), *dsc = (float *)(buf + 2 * qb + 2 * kb);
+    int rc = ct__cuda_status(cudaMemcpyAsync(dq, q, qb, cudaMemcpyHostToDevice, 0), "ct_attn_forward");
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(dk, k, kb, cudaMemcpyHostToDevice, 0), "ct_attn_forward");
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(dv, v, kb, cudaMemcpyHostToDevice, 0), "ct_attn_forward");
+    if (!rc) rc = ct__launch_attn_shared(dq, dk, dv, n_tokens, n_kv_heads, head_dim, scale, dout, dsc, NULL);
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, 0), "ct_attn_forward");
+    cudaFreeAsync(buf, 0);
+    if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(0), "ct_attn_forward");
+    return rc == CT_OK;
+}
+
+bool ct_attn_forward_kv(const float *q, const float *kv_k, const float *kv_v, uint32_t n_tokens,
+                        uint32_t n_kv_heads, uint32_t head_dim, float scale, float *out) {
+    return ct_attn_forward(q, kv_k, kv_v, n_tokens, n_kv_heads, head_dim, scale, out);
+}
+
+void ct_attn_softmax(float *x, uint32_t n) {
+    if (!x || n == 0) return;
+    float *d = NULL;
+    const size_t b = (size_t)n * sizeof(float);
+    if (ct__cuda_status(cudaMallocAsync((void **)&d, b, 0), "ct_attn_softmax")) return;
+    int rc = ct__cuda_status(cudaMemcpyAsync(d, x, b, cudaMemcpyHostToDevice, 0), "ct_attn_softmax");
+    if (!rc) rc = ct__launch_softmax(d, n, NULL);
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(x, d, b, cudaMemcpyDeviceToHost, 0), "ct_attn_softmax");
+    cudaFreeAsync(d, 0);
+    cudaStreamSynchronize(0);
+}
+
+/* ---- Part 2: MLA plans ---------------------------------------------------- */
+
+struct ct_mla_plan {
+    ct_mla_dims_t dims;
+    uint32_t n_seq, n_workers, n_chunks, n_combines, n_parts;
+    int device;
+    ct_mla_chunk_t *chunks;      /* device [n_chunks], worker-major */
+    int32_t *worker_begin;       /* device [n_workers + 1] */
+    ct_mla_combine_t *combines;  /* device [n_combines] */
+    float *part_o, *part_ml;     /* device scratch */
+    size_t scratch_bytes;
+    uint32_t last_launches;
+};
+
+/* Declared in mla_tc.cu: whether the tensor-core kernel takes these dims on
+ * this device, and the number of workers it runs. */
+int ct__mla_tc_workers(const ct_mla_dims_t *dims, int device);
+
+void ct_mla_plan_destroy(ct_mla_plan_t *p) {
+    if (!p) return;
+    cudaFree(p->chunks); cudaFree(p->worker_begin); cudaFree(p->combines);
+    cudaFree(p->part_o); cudaFree(p->part_ml);
+    free(p);
+}
+
+ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *seq_rows,
+                                  const int32_t *seq_lens, uint32_t n_seq, int device) {
+    if (!shape || !seq_lens || shape->n_heads == 0 || shape->page_tokens == 0 || shape->v_dim > shape->entry_dim ||
+        shape->entry_dim == 0 || shape->max_pages_per_seq == 0) {
+        ct__set_error("ct_mla_plan_create: bad shape");
+        return NULL;
+    }
+    ct_mla_plan_t *p = (ct_mla_plan_t *)calloc(1, sizeof *p);
+    if (!p) return NULL;
+    p->dims.n_heads = shape->n_heads;
+    p->dims.entry_dim = shape->entry_dim;
+    p->dims.v_dim = shape->v_dim;
+    p->dims.page_tokens = shape->page_tokens;
+    p->dims.max_pages_per_seq = shape->max_pages_per_seq;
+    p->dims.kv_dtype = shape->kv_dtype;
+    p->dims.scale = shape->scale;
+    p->n_seq = n_seq;
+    p->device = device;
+    const uint32_t P = shape->page_tokens;
+
+    int n_sms = 148;
+    if (cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+        cudaGetLastError();
+        n_sms = 148;
+    }
+    int tc_workers = ct__mla_tc_workers(&p->dims, device);
+    p->n_workers = tc_workers > 0 ? (uint32_t)tc_workers : (uint32_t)n_sms;
+
+    /* Token quota per worker; cuts fall on page boundaries. */
+    uint64_t total = 0;
+    for (uint32_t s = 0; s < n_seq; s++) {
+        if (seq_lens[s] < 0 || (uint64_t)(seq_lens[s] + P - 1) / P > shape->max_pages_per_seq) {
+            ct__set_error("ct_mla_plan_create: sequence longer than its block-table row");
+            free(p);
+            return NULL;
+        }
+        total += (uint64_t)seq_lens[s];
+    }
+    const uint32_t W = p->n_workers;
+    const uint64_t quota = total / W + 1;
+    const size_t cap = (size_t)n_seq + 2 * (size_t)W + 8;
+    ct_mla_chunk_t *ch = (ct_mla_chunk_t *)calloc(cap, sizeof *ch);
+    int32_t *wb = (int32_t *)calloc((size_t)W + 1, sizeof(int32_t));
+    int32_t *first_chunk = (int32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(int32_t));
+    int32_t *n_of = (int32_t *)calloc((size_t)(n_seq ? n_seq : 1), sizeof(int32_t));
+    if (!ch || !wb || !first_chunk || !n_of) goto fail;
+
+    uint32_t nc = 0, w = 0;
+    uint64_t filled = 0;                 /* tokens given to worker w */
+    wb[0] = 0;
+    for (uint32_t s = 0; s < n_seq; s++) {
+        const int32_t row = seq_rows ? (int32_t)seq_rows[s] : (int32_t)s;
+        const uint32_t pages = ((uint32_t)seq_lens[s] + P - 1) / P;
+        first_chunk[s] = (int32_t)nc;
+        if (pages == 0) {                /* empty sequence: one chunk that writes zeros */
+            ch[nc++] = (ct_mla_chunk_t){ (int32_t)s, row, 0, 0, -1, {0, 0, 0} };
+            n_of[s] = 1;
+            continue;
+        }
+        uint32_t pg = 0;
+        while (pg < pages) {
+            uint64_t room = quota > filled ? quota - filled : 0;
+            uint32_t take = (uint32_t)((room + P / 2) / P);          /* nearest page count */
+            if (take == 0) take = 1;
+            if (w + 1 >= W || take > pages - pg) take = pages - pg;   /* last worker takes the rest */
+            ch[nc++] = (ct_mla_chunk_t){ (int32_t)s, row, (int32_t)pg, (int32_t)(pg + take), 0, {0, 0, 0} };
+            n_of[s]++;
+            uint64_t tok = (uint64_t)take * P;
+            if (pg + take == pages) tok = (uint64_t)seq_lens[s] - (uint64_t)pg * P;
+            pg += take;
+            filled += tok;
+            if (filled + P / 2 >= quota && w + 1 < W) { wb[++w] = (int32_t)nc; filled = 0; }
+            if (nc + 2 >= cap) goto fail;
+        }
+    }
+    while (w < W) wb[++w] = (int32_t)nc;
+    p->n_chunks = nc;
+
+    /* Partial slots for split sequences, and their combine items. */
+    ct_mla_combine_t *cb = (ct_mla_combine_t *)calloc((size_t)(n_seq ? n_seq : 1), sizeof *cb);
+    if (!cb) goto fail;
+    uint32_t parts = 0, ncb = 0;
+    for (uint32_t s = 0; s < n_seq; s++) {
+        if (n_of[s] <= 1) { ch[first_chunk[s]].part = -1; continue; }
+        cb[ncb++] = (ct_mla_combine_t){ (int32_t)s, (int32_t)parts, n_of[s], 0 };
+        for (int32_t i = 0; i < n_of[s]; i++) ch[first_chunk[s] + i].part = (int32_t)(parts++);
+    }
+    p->n_combines = ncb;
+    p->n_parts = parts;
+
+    int rc = ct__cuda_status(cudaSetDevice(device), "ct_mla_plan_create");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->chunks, (size_t)(nc ? nc : 1) * sizeof *ch), "plan chunks");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->worker_begin, ((size_t)W + 1) * sizeof(int32_t)), "plan workers");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->combines, (size_t)(ncb ? ncb : 1) * sizeof *cb), "plan combines");
+    const size_t po = (size_t)(parts ? parts : 1) * shape->n_heads * shape->v_dim * sizeof(float);
+    const size_t pm = (size_t)(parts ? parts : 1) * shape->n_heads * 2 * sizeof(float);
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->part_o, po), "plan scratch");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->part_ml, pm), "plan scratch");
+    p->scratch_bytes = po + pm;
+    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->chunks, ch, (size_t)(nc ? nc : 1) * sizeof *ch, cudaMemcpyHostToDevice), "plan upload");
+    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->worker_begin, wb, ((size_t)W + 1) * sizeof(int32_t), cudaMemcpyHostToDevice), "plan upload");
+    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->combines, cb, (size_t)(ncb ? ncb : 1) * sizeof *cb, cudaMemcpyHostToDevice), "plan upload");
+    free(cb);
+    free(ch); free(wb); free(first_chunk); free(n_of);
+    if (rc) { ct_mla_plan_destroy(p); return NULL; }
+    return p;
+fail:
+    ct__set_error("ct_mla_plan_create: out of memory");
+    free(ch); free(wb); free(first_chunk); free(n_of);
+    free(p);
+    return NULL;
+}
+
+uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p) { return p ? p->n_chunks : 0; }
+size_t ct_mla_plan_scratch_bytes(const ct_mla_plan_t *p) { return p ? p->scratch_bytes : 0; }
+uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p) { return p ? p->last_launches : 0; }
+
+int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const void *pool, const float *scales,
+                             const int32_t *block_table, const int32_t *seq_lens, void *out, float *lse,
+                             void *stream) {
+    if (!plan || !q || !pool || !block_table || !seq_lens || !out) return CT_ERR_ARG;
+    if ((plan->dims.kv_dtype == CT_KV_INT8 || plan->dims.kv_dtype == CT_KV_E4M3) && !scales) return CT_ERR_ARG;
+    ct_mla_plan_t *p = (ct_mla_plan_t *)plan;
+    uint32_t launches = 0;
+    int rc = ct__launch_mla_decode(&p->dims, p->chunks, p->n_chunks, p->worker_begin, p->n_workers, p->combines,
+                                   p->n_combines, q, pool, scales, block_table, seq_lens, out, lse, p->part_o,
+                                   p->part_ml, stream, &launches);
+    p->last_launches = launches;
+    return rc;
+}

@@ -1,0 +1,542 @@
+/*
+ * kv_paged.c -- paged KV cache handle (kv_cache.h Part 2).
+ *
+ * Host side: block tables, free list, sliding window and LRU eviction, the
+ * eviction log.  Device side (kv_kernels.cu): token writes with
+ * quantise-on-append, gathers with dequantise-on-gather, page moves for
+ * compaction.  The reference has no paged cache; its precedents are
+ * ct_kv_compress for moving tokens down (src/kv_cache/kv_cache.c:113-137)
+ * and the streamer's LRU, which picks the minimum last-access time with the
+ * lowest index winning ties (src/streaming/streaming.c:86-96).
+ *
+ * Event order for each appended token (rounds across the sequences of one
+ * call, see ct_kv_paged_append):
+ *   1. a token at position r with r % P == 0 opens logical page r / P; if no
+ *      page is free, the least recently used FULL page is evicted first,
+ *      minimising (last_access[seq], seq, lpage);
+ *   2. the free page of lowest rank is taken (rank = position in the free
+ *      order, ascending ids by default);
+ *   3. the token goes to slot r % P;
+ *   4. last_access[seq] = the allocator clock of this round;
+ *   5. pages lying wholly below len - window are freed.
+ * A sequence's mapped pages form one run [lo, hi) of logical pages: new
+ * pages open at hi; the window and LRU free from lo.
+ *
+ * Device mirrors (block table, lengths) are updated by scattering only the
+ * changed entries, staged with the token slots in one pinned buffer.
+ */
+#include "../../include/hal.h"
+#include "../../include/kv_cache.h"
+#include "../csrc/ct_internal.h"
+
+#include <cuda_runtime_api.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* Device helper in kv_kernels.cu: dst[idx[i]] = val[i]. */
+int ct__launch_scatter_i32(int32_t *dst, const int32_t *pairs, uint32_t n_pairs, void *stream);
+
+struct ct_kv_paged {
+    ct_kv_paged_config_t cfg;
+    int host_only;              /* device < 0: tables only, no device memory */
+    cudaStream_t stream;
+    size_t elt;                 /* bytes per value in the pool */
+    size_t page_bytes;          /* page_tokens * entry_dim * elt */
+    /* device */
+    void *pool;
+    float *scales;
+    int32_t *bt_dev;
+    int32_t *len_dev;
+    int32_t *stage_dev;         /* staged dest slots + (index, value) pairs */
+    size_t stage_cap;           /* int32 elements */
+    /* pinned staging and the event guarding its reuse */
+    int32_t *stage_host;
+    cudaEvent_t stage_ev;
+    int stage_pending;
+    /* host state */
+    int32_t *bt;                /* [n_seqs][max_pages] */
+    uint32_t *len, *lo, *hi;
+    uint64_t *last_access;
+    uint32_t *rank;             /* free-order rank of each physical page */
+    int32_t *heap;              /* free pages, min-heap by rank */
+    uint32_t heap_n;
+    ct_kv_evict_event_t *log;
+    uint32_t log_n, log_cap;
+    uint8_t *claimed;           /* per-call slot bitmap for last-writer-wins */
+    ct_kv_paged_stats_t st;
+    /* pending device updates of this call */
+    int32_t *pairs;             /* (index, value) for bt_dev then len_dev */
+    uint32_t n_bt_pairs, n_len_pairs, pairs_cap;
+};
+
+/* ---- free list ----------------------------------------------------------- */
+
+static int heap_less(const ct_kv_paged_t *h, int32_t a, int32_t b) { return h->rank[a] < h->rank[b]; }
+
+static void heap_push(ct_kv_paged_t *h, int32_t p) {
+    uint32_t i = h->heap_n++;
+    h->heap[i] = p;
+    while (i > 0) {
+        uint32_t up = (i - 1) / 2;
+        if (!heap_less(h, h->heap[i], h->heap[up])) break;
+        int32_t t = h->heap[up]; h->heap[up] = h->heap[i]; h->heap[i] = t; i = up;
+    }
+}
+
+static int32_t heap_pop(ct_kv_paged_t *h) {
+    int32_t top = h->heap[0];
+    h->heap[0] = h->heap[--h->heap_n];
+    uint32_t i = 0;
+    for (;;) {
+        uint32_t l = 2 * i + 1, r = l + 1, m = i;
+        if (l < h->heap_n && heap_less(h, h->heap[l], h->heap[m])) m = l;
+        if (r < h->heap_n && heap_less(h, h->heap[r], h->heap[m])) m = r;
+        if (m == i) break;
+        int32_t t = h->heap[m]; h->heap[m] = h->heap[i]; h->heap[i] = t; i = m;
+    }
+    return top;
+}
+
+static void heap_rebuild(ct_kv_paged_t *h, int32_t *pages, uint32_t n) {
+    h->heap_n = 0;
+    for (uint32_t i = 0; i < n; i++) heap_push(h, pages[i]);
+}
+
+/* ---- pending device updates ---------------------------------------------- */
+
+static int pairs_reserve(ct_kv_paged_t *h, uint32_t extra) {
+    uint32_t need = 2 * (h->n_bt_pairs + h->n_len_pairs + extra);
+    if (need <= h->pairs_cap) return CT_OK;
+    uint32_t cap = h->pairs_cap ? h->pairs_cap : 1024;
+    while (cap < need) cap *= 2;
+    int32_t *p = (int32_t *)realloc(h->pairs, (size_t)cap * sizeof(int32_t));
+    if (!p) return CT_ERR_NOMEM;
+    h->pairs = p;
+    h->pairs_cap = cap;
+    return CT_OK;
+}
+
+/* bt pairs are stored from the front, len pairs are appended after the call
+ * by flush (lengths are final only then). */
+static int set_bt(ct_kv_paged_t *h, uint32_t s, uint32_t lp, int32_t v) {
+    size_t idx = (size_t)s * h->cfg.max_pages_per_seq + lp;
+    h->bt[idx] = v;
+    if (pairs_reserve(h, 1)) return CT_ERR_NOMEM;
+    h->pairs[2 * h->n_bt_pairs] = (int32_t)idx;
+    h->pairs[2 * h->n_bt_pairs + 1] = v;
+    h->n_bt_pairs++;
+    return CT_OK;
+}
+
+static int log_event(ct_kv_paged_t *h, uint32_t s, uint32_t lp, int32_t ph, uint32_t reason) {
+    if (h->log_n == h->log_cap) {
+        uint32_t cap = h->log_cap ? 2 * h->log_cap : 1024;
+        ct_kv_evict_event_t *p = (ct_kv_evict_event_t *)realloc(h->log, (size_t)cap * sizeof *p);
+        if (!p) return CT_ERR_NOMEM;
+        h->log = p;
+        h->log_cap = cap;
+    }
+    ct_kv_evict_event_t ev = { (uint32_t)h->st.clock, s, lp, ph, reason };
+    h->log[h->log_n++] = ev;
+    if (reason == 1) h->st.n_evict_window++; else h->st.n_evict_lru++;
+    return CT_OK;
+}
+
+/* Frees logical page lo[s] of sequence s. */
+static int free_low_page(ct_kv_paged_t *h, uint32_t s, uint32_t reason) {
+    uint32_t lp = h->lo[s];
+    int32_t ph = h->bt[(size_t)s * h->cfg.max_pages_per_seq + lp];
+    if (reason && log_event(h, s, lp, ph, reason)) return CT_ERR_NOMEM;
+    if (set_bt(h, s, lp, -1)) return CT_ERR_NOMEM;
+    h->lo[s]++;
+    heap_push(h, ph);
+    h->st.n_pages_live--;
+    return CT_OK;
+}
+
+/* LRU victim: sequence with a full lowest page, minimising (last_access, seq). */
+static int64_t lru_victim(const ct_kv_paged_t *h) {
+    int64_t best = -1;
+    const uint32_t P = h->cfg.page_tokens;
+    for (uint32_t c = 0; c < h->cfg.n_seqs; c++) {
+        if (h->lo[c] >= h->hi[c]) continue;
+        if ((uint64_t)(h->lo[c] + 1) * P > h->len[c]) continue;      /* partial tail page */
+        if (best < 0 || h->last_access[c] < h->last_access[best]) best = c;
+    }
+    return best;
+}
+
+/* ---- lifecycle ------------------------------------------------------------ */
+
+void ct_kv_paged_destroy(ct_kv_paged_t *h) {
+    if (!h) return;
+    if (!h->host_only) {
+        if (h->stage_pending) cudaEventSynchronize(h->stage_ev);
+        if (h->stage_ev) cudaEventDestroy(h->stage_ev);
+        cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->bt_dev); cudaFree(h->len_dev); cudaFree(h->stage_dev);
+        if (h->stage_host) cudaFreeHost(h->stage_host);
+    }
+    free(h->bt); free(h->len); free(h->lo); free(h->hi); free(h->last_access); free(h->rank);
+    free(h->heap); free(h->log); free(h->claimed); free(h->pairs);
+    free(h);
+}
+
+ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg) {
+    if (!cfg || cfg->n_seqs == 0 || cfg->n_pages == 0 || cfg->max_pages_per_seq == 0 || cfg->dtype > CT_KV_E4M3) {
+        ct__set_error("ct_kv_paged_create: bad config");
+        return NULL;
+    }
+    ct_kv_paged_t *h = (ct_kv_paged_t *)calloc(1, sizeof *h);
+    if (!h) return NULL;
+    h->cfg = *cfg;
+    if (h->cfg.page_tokens == 0) h->cfg.page_tokens = 64;
+    if (h->cfg.entry_dim == 0) h->cfg.entry_dim = 576;
+    if (h->cfg.entry_dim % 16 != 0) { ct__set_error("ct_kv_paged_create: entry_dim % 16 != 0"); free(h); return NULL; }
+    h->host_only = cfg->device < 0;
+    if (!h->host_only && ct__cuda_status(cudaSetDevice(cfg->device), "ct_kv_paged_create")) { free(h); return NULL; }
+    const uint32_t S = h->cfg.n_seqs, MP = h->cfg.max_pages_per_seq, NP = h->cfg.n_pages, P = h->cfg.page_tokens;
+    h->elt = h->cfg.dtype == CT_KV_BF16 ? 2 : h->cfg.dtype == CT_KV_F32 ? 4 : 1;
+    h->page_bytes = (size_t)P * h->cfg.entry_dim * h->elt;
+    const size_t bt_n = (size_t)S * MP;
+    h->bt = (int32_t *)malloc(bt_n * sizeof(int32_t));
+    h->len = (uint32_t *)calloc(S, sizeof(uint32_t));
+    h->lo = (uint32_t *)calloc(S, sizeof(uint32_t));
+    h->hi = (uint32_t *)calloc(S, sizeof(uint32_t));
+    h->last_access = (uint64_t *)calloc(S, sizeof(uint64_t));
+    h->rank = (uint32_t *)malloc((size_t)NP * sizeof(uint32_t));
+    h->heap = (int32_t *)malloc((size_t)NP * sizeof(int32_t));
+    h->claimed = (uint8_t *)calloc(((size_t)NP * P + 7) / 8, 1);
+    if (!h->bt || !h->len || !h->lo || !h->hi || !h->last_access || !h->rank || !h->heap || !h->claimed) {
+        ct_kv_paged_destroy(h);
+        return NULL;
+    }
+    for (size_t i = 0; i < bt_n; i++) h->bt[i] = -1;
+    for (uint32_t p = 0; p < NP; p++) { h->rank[p] = p; h->heap[p] = (int32_t)p; }
+    h->heap_n = NP;                      /* ascending ids already form a heap */
+    h->st.n_pages_free = NP;
+    if (h->host_only) return h;
+    int rc = ct__cuda_status(cudaMalloc(&h->pool, (size_t)NP * h->page_bytes), "ct_kv_paged_create pool");
+    if (!rc && (h->cfg.dtype == CT_KV_INT8 || h->cfg.dtype == CT_KV_E4M3))
+        rc = ct__cuda_status(cudaMalloc((void **)&h->scales, (size_t)NP * P * sizeof(float)), "ct_kv_paged_create scales");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&h->bt_dev, bt_n * sizeof(int32_t)), "ct_kv_paged_create bt");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&h->len_dev, (size_t)S * sizeof(int32_t)), "ct_kv_paged_create len");
+    if (!rc) rc = ct__cuda_status(cudaMemset(h->bt_dev, 0xFF, bt_n * sizeof(int32_t)), "ct_kv_paged_create");
+    if (!rc) rc = ct__cuda_status(cudaMemset(h->len_dev, 0, (size_t)S * sizeof(int32_t)), "ct_kv_paged_create");
+    if (!rc && h->scales) rc = ct__cuda_status(cudaMemset(h->scales, 0, (size_t)NP * P * sizeof(float)), "ct_kv_paged_create");
+    if (!rc) rc = ct__cuda_status(cudaEventCreateWithFlags(&h->stage_ev, cudaEventDisableTiming), "ct_kv_paged_create");
+    if (rc) { ct_kv_paged_destroy(h); return NULL; }
+    return h;
+}
+
+int ct_kv_paged_set_stream(ct_kv_paged_t *h, void *stream) {
+    if (!h) return CT_ERR_ARG;
+    h->stream = (cudaStream_t)stream;
+    return CT_OK;
+}
+
+int ct_kv_paged_set_free_order(ct_kv_paged_t *h, const int32_t *order) {
+    if (!h || !order) return CT_ERR_ARG;
+    const uint32_t NP = h->cfg.n_pages;
+    uint8_t *seen = (uint8_t *)calloc(NP, 1);
+    if (!seen) return CT_ERR_NOMEM;
+    for (uint32_t i = 0; i < NP; i++) {
+        if (order[i] < 0 || (uint32_t)order[i] >= NP || seen[order[i]]) { free(seen); return CT_ERR_ARG; }
+        seen[order[i]] = 1;
+    }
+    free(seen);
+    for (uint32_t i = 0; i < NP; i++) h->rank[order[i]] = i;
+    int32_t *pages = (int32_t *)malloc((size_t)h->heap_n * sizeof(int32_t));
+    if (!pages) return CT_ERR_NOMEM;
+    memcpy(pages, h->heap, (size_t)h->heap_n * sizeof(int32_t));
+    heap_rebuild(h, pages, h->heap_n);
+    free(pages);
+    return CT_OK;
+}
+
+/* ---- staging to the device ------------------------------------------------ */
+
+static int stage_reserve(ct_kv_paged_t *h, size_t n) {
+    if (h->stage_pending) {
+        int rc = ct__cuda_status(cudaEventSynchronize(h->stage_ev), "stage");
+        if (rc) return rc;
+        h->stage_pending = 0;
+    }
+    if (n <= h->stage_cap) return CT_OK;
+    size_t cap = h->stage_cap ? h->stage_cap : 4096;
+    while (cap < n) cap *= 2;
+    if (h->stage_host) cudaFreeHost(h->stage_host);
+    if (h->stage_dev) cudaFree(h->stage_dev);
+    h->stage_host = NULL; h->stage_dev = NULL; h->stage_cap = 0;
+    int rc = ct__cuda_status(cudaMallocHost((void **)&h->stage_host, cap * sizeof(int32_t)), "stage host");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&h->stage_dev, cap * sizeof(int32_t)), "stage dev");
+    if (rc) return rc;
+    h->stage_cap = cap;
+    return CT_OK;
+}
+
+/* Uploads n_dest token slots plus the pending bt / len (index, value) pairs
+ * in one pinned staging copy, then runs the scatters and the token writes. */
+static int flush(ct_kv_paged_t *h, const int32_t *dest, uint32_t n_dest, const void *entries, uint32_t src_dtype) {
+    const size_t n_pairs = (size_t)h->n_bt_pairs + h->n_len_pairs;
+    const size_t total = n_dest + 2 * n_pairs;
+    if (h->host_only) {
+        h->n_bt_pairs = h->n_len_pairs = 0;
+        return entries ? CT_ERR_UNSUPPORTED : CT_OK;
+    }
+    if (total == 0) return CT_OK;
+    int rc = stage_reserve(h, total);
+    if (rc) return rc;
+    if (n_dest) memcpy(h->stage_host, dest, (size_t)n_dest * sizeof(int32_t));
+    /* Stage the final host value of every touched index: an index touched
+     * twice in one call then carries one value, and the scatter needs no order. */
+    int32_t *pr = h->stage_host + n_dest;
+    for (uint32_t i = 0; i < h->n_bt_pairs; i++) {
+        pr[2 * i] = h->pairs[2 * i];
+        pr[2 * i + 1] = h->bt[h->pairs[2 * i]];
+    }
+    for (uint32_t i = h->n_bt_pairs; i < h->n_bt_pairs + h->n_len_pairs; i++) {
+        pr[2 * i] = h->pairs[2 * i];
+        pr[2 * i + 1] = (int32_t)h->len[h->pairs[2 * i]];
+    }
+    rc = ct__cuda_status(cudaMemcpyAsync(h->stage_dev, h->stage_host, total * sizeof(int32_t),
+                                         cudaMemcpyHostToDevice, h->stream), "stage upload");
+    if (!rc) rc = ct__cuda_status(cudaEventRecord(h->stage_ev, h->stream), "stage event");
+    if (rc) return rc;
+    h->stage_pending = 1;
+    if (h->n_bt_pairs) rc = ct__launch_scatter_i32(h->bt_dev, h->stage_dev + n_dest, h->n_bt_pairs, h->stream);
+    if (!rc && h->n_len_pairs)
+        rc = ct__launch_scatter_i32(h->len_dev, h->stage_dev + n_dest + 2 * (size_t)h->n_bt_pairs, h->n_len_pairs, h->stream);
+    if (!rc && entries && n_dest)
+        rc = ct_kv_paged_write_slots(h->pool, h->scales, h->cfg.dtype, entries, src_dtype, h->stage_dev, n_dest,
+                                     h->cfg.entry_dim, h->stream);
+    h->n_bt_pairs = h->n_len_pairs = 0;
+    return rc;
+}
+
+static int push_len(ct_kv_paged_t *h, uint32_t s) {
+    if (pairs_reserve(h, 1)) return CT_ERR_NOMEM;
+    uint32_t i = h->n_bt_pairs + h->n_len_pairs;
+    h->pairs[2 * i] = (int32_t)s;
+    h->pairs[2 * i + 1] = (int32_t)h->len[s];
+    h->n_len_pairs++;
+    return CT_OK;
+}
+
+/* ---- append --------------------------------------------------------------- */
+
+int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts, uint32_t n,
+                       const void *entries, uint32_t src_dtype) {
+    if (!h || (n && (!seq_ids || !counts))) return CT_ERR_ARG;
+    if (entries && h->host_only) return CT_ERR_UNSUPPORTED;
+    if (entries && src_dtype != CT_KV_BF16 && src_dtype != CT_KV_F32) return CT_ERR_ARG;
+    const uint32_t P = h->cfg.page_tokens, MP = h->cfg.max_pages_per_seq, W = h->cfg.window_tokens;
+    size_t total = 0;
+    uint32_t maxc = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        if (seq_ids[i] >= h->cfg.n_seqs) return CT_ERR_ARG;
+        total += counts[i];
+        if (counts[i] > maxc) maxc = counts[i];
+    }
+    if (total > 0x7FFFFFFFu) return CT_ERR_ARG;
+    int rc = CT_OK;
+    size_t *off = (size_t *)malloc((n ? n : 1) * sizeof(size_t));
+    int32_t *dest = (int32_t *)malloc((total ? total : 1) * sizeof(int32_t));
+    if (!off || !dest) { free(off); free(dest); return CT_ERR_NOMEM; }
+    for (uint32_t i = 0, acc = 0; i < n; i++) { off[i] = acc; acc += counts[i]; }
+    h->n_bt_pairs = h->n_len_pairs = 0;
+
+    for (uint32_t k = 0; k < maxc && rc == CT_OK; k++) {
+        for (uint32_t i = 0; i < n; i++) {
+            if (k >= counts[i]) continue;
+            const uint32_t s = seq_ids[i];
+            const uint32_t r = h->len[s];
+            const uint32_t lp = r / P;
+            if (r % P == 0) {
+                if (lp >= MP) { rc = CT_ERR_FULL; ct__set_error("append: block table row full"); break; }
+                if (h->heap_n == 0) {
+                    int64_t c = lru_victim(h);
+                    if (c < 0) { rc = CT_ERR_FULL; ct__set_error("append: no evictable page"); break; }
+                    if ((rc = free_low_page(h, (uint32_t)c, 2))) break;
+                }
+                int32_t ph = heap_pop(h);
+                if ((rc = set_bt(h, s, lp, ph))) break;
+                if (h->lo[s] == h->hi[s]) h->lo[s] = lp;
+                h->hi[s] = lp + 1;
+                h->st.n_pages_live++;
+            }
+            const int32_t ph = h->bt[(size_t)s * MP + lp];
+            dest[off[i] + k] = ph * (int32_t)P + (int32_t)(r % P);
+            h->len[s] = r + 1;
+            h->last_access[s] = h->st.clock;
+            h->st.n_appends++;
+            if (W > 0 && r + 1 > W) {
+                const uint64_t below = (uint64_t)r + 1 - W;
+                while (h->lo[s] < h->hi[s] && (uint64_t)(h->lo[s] + 1) * P <= below)
+                    if ((rc = free_low_page(h, s, 1))) break;
+                if (rc) break;
+            }
+        }
+        h->st.clock++;
+    }
+    if (rc == CT_OK && total > 1) {
+        /* Last writer wins when a page was freed and reused inside the call:
+         * keep only the final write of each slot. */
+        for (size_t t = total; t-- > 0;) {
+            int32_t sl = dest[t];
+            if (sl < 0) continue;
+            if (h->claimed[sl >> 3] & (1u << (sl & 7))) dest[t] = -1;
+            else h->claimed[sl >> 3] |= (uint8_t)(1u << (sl & 7));
+        }
+        for (size_t t = 0; t < total; t++) {
+            int32_t sl = dest[t];
+            if (sl >= 0) h->claimed[sl >> 3] = 0;
+        }
+        /* the clearing above zeroes whole bytes; bytes holding a discarded
+         * duplicate were already set by its winner and are cleared with it */
+    }
+    if (rc == CT_OK)
+        for (uint32_t i = 0; i < n; i++) if ((rc = push_len(h, seq_ids[i]))) break;
+    free(off);
+    h->st.n_pages_free = h->heap_n;
+    if (rc != CT_OK) {
+        /* Host state already advanced: publish what changed so the device
+         * mirrors stay consistent, but write no token data. */
+        flush(h, NULL, 0, NULL, 0);
+        free(dest);
+        return rc;
+    }
+    rc = flush(h, dest, (uint32_t)total, entries, src_dtype);
+    free(dest);
+    return rc;
+}
+
+int ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t s) {
+    if (!h || s >= h->cfg.n_seqs) return CT_ERR_ARG;
+    int rc = CT_OK;
+    while (h->lo[s] < h->hi[s]) if ((rc = free_low_page(h, s, 0))) return rc;
+    h->lo[s] = h->hi[s] = 0;
+    h->len[s] = 0;
+    if ((rc = push_len(h, s))) return rc;
+    h->st.n_pages_free = h->heap_n;
+    return flush(h, NULL, 0, NULL, 0);
+}
+
+int ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n) {
+    if (!h) return CT_ERR_ARG;
+    int rc = CT_OK;
+    uint32_t done = 0;
+    for (; done < n; done++) {
+        int64_t c = lru_victim(h);
+        if (c < 0) break;
+        if ((rc = free_low_page(h, (uint32_t)c, 2))) return rc;
+    }
+    h->st.n_pages_free = h->heap_n;
+    rc = flush(h, NULL, 0, NULL, 0);
+    return rc ? rc : (int)done;
+}
+
+/* ---- compaction ----------------------------------------------------------- */
+
+int ct_kv_paged_compact(ct_kv_paged_t *h) {
+    if (!h) return CT_ERR_ARG;
+    const uint32_t S = h->cfg.n_seqs, MP = h->cfg.max_pages_per_seq, NP = h->cfg.n_pages, P = h->cfg.page_tokens;
+    int32_t *map;
+    int rc = CT_OK;
+    if (h->host_only) {
+        map = h->heap;                            /* scratch: rebuilt below */
+    } else {
+        rc = stage_reserve(h, (size_t)S * MP + NP + 64);
+        if (rc) return rc;
+        map = h->stage_host;                      /* [n_live] new -> old, then the bt image */
+    }
+    uint32_t n_live = 0;
+    for (uint32_t s = 0; s < S; s++)
+        for (uint32_t lp = h->lo[s]; lp < h->hi[s]; lp++) {
+            int32_t *e = h->bt + (size_t)s * MP + lp;
+            map[n_live] = *e;
+            *e = (int32_t)n_live++;
+        }
+    if (h->host_only) goto renumbered;
+    void *new_pool = NULL;
+    float *new_scales = NULL;
+    rc = ct__cuda_status(cudaMalloc(&new_pool, (size_t)NP * h->page_bytes), "compact pool");
+    if (!rc && h->scales) rc = ct__cuda_status(cudaMalloc((void **)&new_scales, (size_t)NP * P * sizeof(float)), "compact scales");
+    if (!rc && new_scales) rc = ct__cuda_status(cudaMemsetAsync(new_scales, 0, (size_t)NP * P * sizeof(float), h->stream), "compact");
+    /* bt image follows the map in the staging buffer */
+    memcpy(map + n_live, h->bt, (size_t)S * MP * sizeof(int32_t));
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(h->stage_dev, map, ((size_t)n_live + (size_t)S * MP) * sizeof(int32_t),
+                                                  cudaMemcpyHostToDevice, h->stream), "compact upload");
+    if (!rc) rc = ct_kv_paged_move_pages(h->pool, h->scales, new_pool, new_scales, h->stage_dev, n_live,
+                                         h->page_bytes, P, h->stream);
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(h->bt_dev, h->stage_dev + n_live, (size_t)S * MP * sizeof(int32_t),
+                                                  cudaMemcpyDeviceToDevice, h->stream), "compact bt");
+    if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(h->stream), "compact sync");
+    if (rc) { cudaFree(new_pool); cudaFree(new_scales); return rc; }
+    cudaFree(h->pool);
+    cudaFree(h->scales);
+    h->pool = new_pool;
+    h->scales = new_scales;
+renumbered:
+    /* Free pages are now n_live..NP-1, handed out in ascending order. */
+    for (uint32_t p = 0; p < NP; p++) h->rank[p] = p;
+    h->heap_n = 0;
+    for (uint32_t p = n_live; p < NP; p++) h->heap[h->heap_n++] = (int32_t)p;
+    h->st.n_pages_free = h->heap_n;
+    h->st.n_compactions++;
+    h->st.bytes_compacted += 2ull * n_live * h->page_bytes;
+    return CT_OK;
+}
+
+/* ---- reads ------------------------------------------------------------------ */
+
+int ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t n, void *out, uint32_t out_dtype) {
+    if (!h || !out || seq >= h->cfg.n_seqs) return CT_ERR_ARG;
+    if (h->host_only) return CT_ERR_UNSUPPORTED;
+    if (out_dtype != CT_KV_BF16 && out_dtype != CT_KV_F32) return CT_ERR_ARG;
+    if ((uint64_t)start + n > h->len[seq]) return CT_ERR_ARG;
+    if (n == 0) return CT_OK;
+    const uint32_t P = h->cfg.page_tokens;
+    for (uint32_t lp = start / P; lp <= (start + n - 1) / P; lp++)
+        if (h->bt[(size_t)seq * h->cfg.max_pages_per_seq + lp] < 0) return CT_ERR_UNMAPPED;
+    return ct__launch_kv_gather(h->pool, h->scales, h->cfg.dtype, h->bt_dev + (size_t)seq * h->cfg.max_pages_per_seq,
+                                P, h->cfg.entry_dim, start, n, out, out_dtype, h->stream);
+}
+
+int ct_kv_paged_block_table(const ct_kv_paged_t *h, int32_t *out) {
+    if (!h || !out) return CT_ERR_ARG;
+    memcpy(out, h->bt, (size_t)h->cfg.n_seqs * h->cfg.max_pages_per_seq * sizeof(int32_t));
+    return CT_OK;
+}
+
+int ct_kv_paged_seq_lens(const ct_kv_paged_t *h, uint32_t *out) {
+    if (!h || !out) return CT_ERR_ARG;
+    memcpy(out, h->len, (size_t)h->cfg.n_seqs * sizeof(uint32_t));
+    return CT_OK;
+}
+
+int ct_kv_paged_last_access(const ct_kv_paged_t *h, uint64_t *out) {
+    if (!h || !out) return CT_ERR_ARG;
+    memcpy(out, h->last_access, (size_t)h->cfg.n_seqs * sizeof(uint64_t));
+    return CT_OK;
+}
+
+uint32_t ct_kv_paged_evict_log(const ct_kv_paged_t *h, ct_kv_evict_event_t *out, uint32_t max) {
+    if (!h) return 0;
+    if (!out) return h->log_n;
+    uint32_t n = h->log_n < max ? h->log_n : max;
+    memcpy(out, h->log, (size_t)n * sizeof *out);
+    return n;
+}
+
+ct_kv_paged_stats_t ct_kv_paged_stats(const ct_kv_paged_t *h) {
+    ct_kv_paged_stats_t s;
+    memset(&s, 0, sizeof s);
+    if (h) s = h->st;
+    return s;
+}
+
+const ct_kv_paged_config_t *ct_kv_paged_config(const ct_kv_paged_t *h) { return h ? &h->cfg : NULL; }
+void *ct_kv_paged_pool(ct_kv_paged_t *h) { return h ? h->pool : NULL; }
+float *ct_kv_paged_scales(ct_kv_paged_t *h) { return h ? h->scales : NULL; }
+const int32_t *ct_kv_paged_block_table_dev(const ct_kv_paged_t *h) { return h ? h->bt_dev : NULL; }
+const int32_t *ct_kv_paged_seq_lens_dev(const ct_kv_paged_t *h) { return h ? h->len_dev : NULL; }

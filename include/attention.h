@@ -1,0 +1,113 @@
+#ifndef CAUTREO_ATTENTION_H
+#define CAUTREO_ATTENTION_H
+
+/*
+ * attention.h -- decode attention on B200.
+ *
+ * Part 1 keeps the reference interface of src/attention/attention.h:22-32
+ * unchanged (host pointers, bool / void returns).  Each call copies its
+ * inputs to the device, runs a CUDA kernel and copies the result back.
+ *
+ * Part 2 adds device-pointer entry points: plain decode over a contiguous
+ * cache (the loop of src/transformer/transformer.c:185-214) and paged
+ * absorbed-MLA decode (the latent cache of src/transformer/ds4_forward.c:
+ * 1567-1636 extended with a 64-d RoPE key, paging and split-KV).
+ */
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ======================================================================== */
+/* Part 1 -- reference interface (src/attention/attention.h:22-32)          */
+/* ======================================================================== */
+
+/* attention.h:22 -- single-query scaled dot-product attention.  q and out are
+ * [n_kv_heads][head_dim]; k and v are ONE [n_tokens][head_dim] block that
+ * every head reads (attention.c:37,47).  scale 0 selects 1/sqrt(head_dim).
+ * false on NULL pointers, n_tokens == 0 or a CUDA failure. */
+bool ct_attn_forward(const float *q, const float *k, const float *v,
+                     uint32_t n_tokens, uint32_t n_kv_heads, uint32_t head_dim,
+                     float scale, float *out);
+
+/* attention.h:26 -- same as ct_attn_forward. */
+bool ct_attn_forward_kv(const float *q, const float *kv_k, const float *kv_v,
+                        uint32_t n_tokens, uint32_t n_kv_heads, uint32_t head_dim,
+                        float scale, float *out);
+
+/* attention.h:31 -- in-place softmax of n floats (fp32 max, exp, double sum). */
+void ct_attn_softmax(float *x, uint32_t n);
+
+/* ======================================================================== */
+/* Part 2 -- device entry points (new; no reference counterpart)            */
+/* ======================================================================== */
+
+/* Plain decode over a contiguous fp32 cache laid out as ct_kv_cache_t
+ * ([n_layers][max_ctx][n_kv_heads*head_dim]), for n_layers layers at once.
+ * q, out: device [n_layers][n_q_heads][head_dim]; query head h reads KV head
+ * h % n_kv_heads (transformer.c:187); scores = q.k * scale, scale 0 selects
+ * 1/sqrt(head_dim).  Attends tokens [0, n_tokens). */
+int ct_attn_decode_contig(const float *q, const float *k_cache, const float *v_cache,
+                          uint32_t n_layers, uint32_t max_ctx, uint32_t n_kv_heads,
+                          uint32_t n_q_heads, uint32_t head_dim, uint32_t n_tokens,
+                          float scale, float *out, void *stream);
+
+/* One decode step of the same cache: writes k_new / v_new (device
+ * [n_layers][n_kv_heads*head_dim]) at token pos, then attends [0, pos].
+ * One launch for all layers and heads. */
+int ct_attn_decode_step_contig(const float *q, const float *k_new, const float *v_new,
+                               float *k_cache, float *v_cache, uint32_t n_layers,
+                               uint32_t max_ctx, uint32_t n_kv_heads, uint32_t n_q_heads,
+                               uint32_t head_dim, uint32_t pos, float scale, float *out,
+                               void *stream);
+
+/* ---- paged absorbed-MLA decode ------------------------------------------ */
+
+/* Shape of one MLA decode problem. */
+typedef struct {
+    uint32_t n_heads;        /* query heads sharing one latent entry (128) */
+    uint32_t entry_dim;      /* latent + rope values per token (576) */
+    uint32_t v_dim;          /* leading values of an entry used as V (512) */
+    uint32_t page_tokens;    /* 64 */
+    uint32_t max_pages_per_seq;
+    uint32_t kv_dtype;       /* ct_kv_dtype_t of the pool */
+    float    scale;          /* softmax scale, e.g. 1/sqrt(192) */
+} ct_mla_shape_t;
+
+/* A work plan: the split of every sequence's pages into chunks, the chunk
+ * order across SMs, and the device scratch for partial results.  Built on
+ * the host from the sequence lengths; stays valid while no sequence's page
+ * count changes (a token appended inside the last page keeps it valid). */
+typedef struct ct_mla_plan ct_mla_plan_t;
+
+/* seq_rows (host, may be NULL = 0..n_seq-1): block-table row of each output
+ * sequence.  seq_lens_host: tokens each sequence attends. */
+ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *seq_rows,
+                                  const int32_t *seq_lens_host, uint32_t n_seq, int device);
+void   ct_mla_plan_destroy(ct_mla_plan_t *p);
+/* Number of work chunks and the split-KV scratch bytes the plan holds. */
+uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p);
+size_t   ct_mla_plan_scratch_bytes(const ct_mla_plan_t *p);
+
+/* out[s][h][0:v_dim] = sum_t softmax_t(scale * q[s][h] . e_t) * e_t[0:v_dim]
+ * over the entries e_t of sequence s in mapped pages (t < seq_lens[row]).
+ * q: device [n_seq][n_heads][entry_dim] bf16.  pool / scales / block_table /
+ * seq_lens: device, as held by ct_kv_paged_t.  out: device
+ * [n_seq][n_heads][v_dim] bf16.  lse (optional, device [n_seq][n_heads] fp32)
+ * receives the natural-log softmax normaliser.  Sequences of length 0 give 0. */
+int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const void *pool,
+                             const float *scales, const int32_t *block_table,
+                             const int32_t *seq_lens, void *out, float *lse, void *stream);
+
+/* Number of kernel launches the last ct_attn_mla_decode_paged issued. */
+uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAUTREO_ATTENTION_H */

@@ -1,0 +1,204 @@
+#ifndef CAUTREO_KV_CACHE_H
+#define CAUTREO_KV_CACHE_H
+
+/*
+ * kv_cache.h -- KV cache, backed by B200 device memory.
+ *
+ * Part 1 keeps the reference interface of src/kv_cache/kv_cache.h:22-66
+ * byte-for-byte (same struct layouts, same signatures, same return
+ * conventions), so src/transformer/transformer.c and src/engine link against
+ * this library unchanged.  The K/V arrays live in HBM; every call copies
+ * between the caller's host buffers and the device.
+ *
+ * Part 2 adds the paged cache the reference does not have: a pool of
+ * fixed-size pages, per-sequence block tables, a sliding window, LRU
+ * eviction, per-token int8 / fp8-e4m3 codecs applied on append, and
+ * defragmenting compaction.  Device pointers, status codes (0 = success,
+ * negative = error, see ct_status_t in hal.h), one handle per host thread.
+ */
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ======================================================================== */
+/* Part 1 -- reference interface (src/kv_cache/kv_cache.h:22-66)            */
+/* ======================================================================== */
+
+/* Replaces src/kv_cache/kv_cache.h:22-28; 20 bytes, same field order. */
+typedef struct {
+    uint32_t n_layers;
+    uint32_t n_kv_heads;
+    uint32_t head_dim;
+    uint32_t max_ctx;         /* token capacity; 0 selects 2048 */
+    float    compress_ratio;  /* 1.0 = none; 0 selects 1.0 */
+} ct_kv_config_t;
+
+typedef struct ct_kv_cache ct_kv_cache_t;
+
+/* kv_cache.h:33 -- allocates zeroed [n_layers][max_ctx][n_kv_heads*head_dim]
+ * fp32 K and V in device memory; NULL on failure. */
+ct_kv_cache_t *ct_kv_create(const ct_kv_config_t *cfg);
+/* kv_cache.h:34 */
+void           ct_kv_destroy(ct_kv_cache_t *c);
+
+/* kv_cache.h:37 -- copies one token's K and V row (n_kv_heads*head_dim fp32
+ * each, host pointers) into (layer, token_pos).  false on NULL, layer out of
+ * range or token_pos >= max_ctx.  len becomes max(len, token_pos + 1). */
+bool ct_kv_append(ct_kv_cache_t *c, uint32_t layer, uint32_t token_pos,
+                  const float *k, const float *v);
+
+/* kv_cache.h:41 -- copies the row back to host buffers; false if
+ * token_pos >= len.  Does not count as a read in the stats (as in the
+ * reference). */
+bool ct_kv_get(const ct_kv_cache_t *c, uint32_t layer, uint32_t token_pos,
+               float *k_out, float *v_out);
+
+/* kv_cache.h:45-46 */
+uint32_t ct_kv_len(const ct_kv_cache_t *c);
+uint32_t ct_kv_capacity(const ct_kv_cache_t *c);
+
+/* kv_cache.h:49 -- zeroes the counters, keeps the data. */
+void ct_kv_reset(ct_kv_cache_t *c);
+
+/* kv_cache.h:52-53 -- the reference's raw file format: the 20-byte config,
+ * u32 len, u32 n_compressed, then all of K and all of V (full capacity). */
+bool ct_kv_save(const ct_kv_cache_t *c, const char *path);
+bool ct_kv_load(ct_kv_cache_t *c, const char *path);
+
+/* kv_cache.h:56 -- keeps tokens 0, step, 2*step, ... (step = max(2, (int)
+ * ratio)) packed to the front of every layer, on the device. */
+bool ct_kv_compress(ct_kv_cache_t *c, float ratio);
+
+/* kv_cache.h:59-66 */
+typedef struct {
+    uint64_t n_appends;
+    uint64_t n_reads;
+    uint64_t bytes_used;
+    uint32_t n_tokens;
+} ct_kv_stats_t;
+
+ct_kv_stats_t ct_kv_stats(const ct_kv_cache_t *c);
+
+/* Device addresses of the K / V arrays (for kernels that read the cache in
+ * place, e.g. ct_attn_decode_contig in attention.h).  New; no reference
+ * counterpart. */
+float *ct_kv_device_k(ct_kv_cache_t *c);
+float *ct_kv_device_v(ct_kv_cache_t *c);
+
+/* ======================================================================== */
+/* Part 2 -- paged cache (new; no reference counterpart)                    */
+/* ======================================================================== */
+
+/* Storage type of the page pool. */
+typedef enum {
+    CT_KV_BF16 = 0,   /* 2 B per value */
+    CT_KV_F32  = 1,   /* 4 B per value */
+    CT_KV_INT8 = 2,   /* int8 codes + one fp32 scale per token (amax/127) */
+    CT_KV_E4M3 = 3,   /* fp8 e4m3 codes + one fp32 scale per token (amax/448) */
+} ct_kv_dtype_t;
+
+typedef struct {
+    uint32_t n_seqs;             /* block-table rows */
+    uint32_t max_pages_per_seq;  /* block-table columns */
+    uint32_t n_pages;            /* physical pages in the pool */
+    uint32_t page_tokens;        /* tokens per page; 0 selects 64 */
+    uint32_t entry_dim;          /* values per token; 0 selects 576 (512 latent + 64 rope) */
+    uint32_t window_tokens;      /* sliding window; 0 keeps every token */
+    uint32_t dtype;              /* ct_kv_dtype_t */
+    int32_t  device;             /* CUDA ordinal */
+} ct_kv_paged_config_t;
+
+typedef struct ct_kv_paged ct_kv_paged_t;
+
+typedef struct {
+    uint64_t n_appends;          /* tokens appended */
+    uint64_t n_evict_window;     /* pages freed by the sliding window */
+    uint64_t n_evict_lru;        /* pages taken by LRU eviction */
+    uint64_t n_compactions;
+    uint64_t bytes_compacted;    /* page bytes moved by compaction */
+    uint32_t n_pages_live;
+    uint32_t n_pages_free;
+    uint64_t clock;              /* allocator rounds so far */
+} ct_kv_paged_stats_t;
+
+typedef struct {
+    uint32_t round, seq, lpage;
+    int32_t  phys;
+    uint32_t reason;             /* 1 = sliding window, 2 = LRU */
+} ct_kv_evict_event_t;
+
+ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg);
+void           ct_kv_paged_destroy(ct_kv_paged_t *h);
+/* Stream (cudaStream_t) used by every later call on h; NULL = legacy. */
+int  ct_kv_paged_set_stream(ct_kv_paged_t *h, void *stream);
+
+/* Order in which free pages are handed out: order[i] = physical id with
+ * rank i (a permutation of 0..n_pages-1).  Default: ascending ids. */
+int  ct_kv_paged_set_free_order(ct_kv_paged_t *h, const int32_t *order_host);
+
+/* Appends counts[i] tokens to sequence seq_ids[i] (host arrays).  Tokens are
+ * taken in rounds: round k appends token k of every i with k < counts[i], in
+ * array order; each round advances the allocator clock.  Per token:
+ *   1. opening a page when the pool is empty first evicts the least recently
+ *      used full page, minimising (last_access, seq, lpage);
+ *   2. the lowest-ranked free page is taken;
+ *   3. the token is written (quantised on the way if the pool is int8/e4m3);
+ *   4. last_access[seq] = clock;
+ *   5. pages wholly outside the sliding window are freed.
+ * entries: device [sum(counts)][entry_dim] in src_dtype (CT_KV_BF16 or
+ * CT_KV_F32), ordered sequence by sequence (all tokens of seq_ids[0] first);
+ * NULL reserves the slots and writes nothing. */
+int  ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts,
+                        uint32_t n, const void *entries, uint32_t src_dtype);
+
+/* Releases every page of a sequence and sets its length to 0. */
+int  ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t seq);
+/* Frees up to n pages by LRU order; returns the number freed (>= 0). */
+int  ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n);
+/* Renumbers live pages to 0..n_live-1 in (seq, lpage) order and moves their
+ * bytes to match (device gather into a fresh pool). */
+int  ct_kv_paged_compact(ct_kv_paged_t *h);
+
+/* Copies n tokens [start, start+n) of a sequence to out (device) as
+ * contiguous [n][entry_dim] values of out_dtype (CT_KV_BF16 or CT_KV_F32),
+ * dequantising int8/e4m3 pages.  Fails if a page in the range is unmapped. */
+int  ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t n,
+                        void *out, uint32_t out_dtype);
+
+/* Host mirrors / device views. */
+int  ct_kv_paged_block_table(const ct_kv_paged_t *h, int32_t *out_host);  /* [n_seqs][max_pages] */
+int  ct_kv_paged_seq_lens(const ct_kv_paged_t *h, uint32_t *out_host);    /* [n_seqs] */
+int  ct_kv_paged_last_access(const ct_kv_paged_t *h, uint64_t *out_host); /* [n_seqs] */
+uint32_t ct_kv_paged_evict_log(const ct_kv_paged_t *h, ct_kv_evict_event_t *out_host, uint32_t max);
+ct_kv_paged_stats_t ct_kv_paged_stats(const ct_kv_paged_t *h);
+const ct_kv_paged_config_t *ct_kv_paged_config(const ct_kv_paged_t *h);
+void          *ct_kv_paged_pool(ct_kv_paged_t *h);          /* [n_pages][page_tokens][entry_dim] */
+float         *ct_kv_paged_scales(ct_kv_paged_t *h);        /* [n_pages][page_tokens], NULL for bf16/f32 */
+const int32_t *ct_kv_paged_block_table_dev(const ct_kv_paged_t *h);
+const int32_t *ct_kv_paged_seq_lens_dev(const ct_kv_paged_t *h);
+
+/* ---- stateless device kernels under the paged API ----------------------- */
+
+/* Writes n token entries (device [n][dim], src_dtype BF16 or F32) to
+ * dest_slot[i] = phys_page*page_tokens + slot (device int32; < 0 skips),
+ * converting / quantising into the pool's dtype. */
+int ct_kv_paged_write_slots(void *pool, float *scales, uint32_t pool_dtype, const void *entries,
+                            uint32_t src_dtype, const int32_t *dest_slot, uint32_t n,
+                            uint32_t dim, void *stream);
+
+/* Page-level gather: dst page i <- src page map[i] (device int32), whole
+ * pages of page_bytes (codes) and page_tokens scales (if scales != NULL). */
+int ct_kv_paged_move_pages(const void *src_pool, const float *src_scales, void *dst_pool,
+                           float *dst_scales, const int32_t *map, uint32_t n_pages,
+                           size_t page_bytes, uint32_t page_tokens, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAUTREO_KV_CACHE_H */

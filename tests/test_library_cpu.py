@@ -1,0 +1,210 @@
+"""CPU: the product library loads, exports every declared entry point, and its
+host logic (paged allocator bookkeeping, LPT sharding, HAL strategy, fp16
+scalar rules, distributed context) matches the oracle / reference -- no GPU
+compute is called here."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import cautreo_b200 as ct
+import oracle
+
+ROOT = Path(__file__).resolve().parent.parent
+GOLD = ROOT / "tests" / "golden"
+
+
+def declared_functions():
+    names = set()
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"static inline[^{]*\{.*?\n\}", "", text, flags=re.S)
+        for m in re.finditer(r"\b(ct_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = ct.lib()
+    names = declared_functions()
+    assert len(names) > 90
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    # and every declared function has a ctypes signature in the Python layer
+    assert not [n for n in names if n not in ct.SIGNATURES], [n for n in names if n not in ct.SIGNATURES]
+
+
+def test_version_and_launch_counter():
+    L = ct.lib()
+    assert b"sm_100a" in L.ct_hal_version()
+    assert L.ct_hal_cuda_launch_count() >= 0
+
+
+def test_fp16_scalar_rules_match_reference_golden():
+    g = np.load(GOLD / "quant_ref.npz")
+    L = ct.lib()
+    enc = np.array([L.ct_quant_f32_to_fp16(float(v)) for v in g["f32"]], np.uint16)
+    assert np.array_equal(enc, g["f32_to_fp16"])
+    dec = np.array([L.ct_quant_fp16_to_f32(h) for h in range(65536)], np.float32)
+    assert np.array_equal(dec.view(np.uint32), g["fp16_to_f32"].view(np.uint32))
+
+
+def test_bytes_per_float_quirk():
+    # quant.h:57-66 integer division: Q8_0 -> 1 (34/32), Q4_0..Q1_0 -> 0; FP16 -> 2
+    assert {t: b // 32 for t, b in ct.QUANT_BLOCK_BYTES.items()} == {1: 1, 2: 0, 3: 0, 4: 0}
+
+
+def test_lpt_matches_oracle():
+    lens = oracle.lengths_loguniform(oracle.key(4, 0), 1024, 512, 65536)
+    for n_ranks in (1, 2, 3, 4, 8):
+        assert np.array_equal(ct.lpt_shard(lens, n_ranks), oracle.lpt(lens, n_ranks))
+    ties = np.array([5, 5, 5, 5, 9, 1], np.uint32)
+    assert np.array_equal(ct.lpt_shard(ties, 2), oracle.lpt(ties, 2))
+
+
+def test_rank_sequences():
+    L = ct.lib()
+    rank_of = np.array([1, 0, 1, 2, 0], np.int32)
+    out = np.zeros(5, np.uint32)
+    n = L.ct_dist_rank_sequences(rank_of.ctypes.data, 5, 0, out.ctypes.data)
+    assert n == 2 and out[:2].tolist() == [1, 4]
+
+
+def test_distributed_context_mirrors_reference():
+    # distributed_test.c: defaults to one device, rank 0 leads, collectives succeed
+    L = ct.lib()
+    ctx = L.ct_dist_init(None)
+    assert L.ct_dist_n_devices(ctx) == 1 and L.ct_dist_device_id(ctx) == 0 and L.ct_dist_is_leader(ctx)
+    buf = np.ones(4, np.float32)
+    assert L.ct_dist_allreduce(ctx, buf.ctypes.data, 4)
+    assert not L.ct_dist_allreduce(ctx, None, 4)
+    assert L.ct_dist_broadcast(ctx, buf.ctypes.data, 4, 0)
+    L.ct_dist_destroy(ctx)
+
+
+def test_hal_strategy_matches_reference_rule():
+    """With the RAM budget pinned and no GPU, ct_hal_set_model follows the
+    reference's strategy rule (hal.c:285-305): resident up to 80 % of the
+    budget, otherwise stream when the SSD reads >= 500 MB/s."""
+    L = ct.lib()
+    sc = L.ct_hal_detect().contents
+    assert sc.cpu_cores_logical >= 1 and sc.ram_total_bytes > 0
+    budget = 10 << 30
+    L.ct_hal_set_ram_budget(budget)
+    assert L.ct_hal_get().contents.ram_model_budget == int(budget * 0.8)
+    assert L.ct_hal_set_model(int(budget * 0.8), 1, False) == 0            # RESIDENT
+    big = L.ct_hal_set_model(int(budget * 0.9), 1, True)
+    gpu = L.ct_hal_get().contents
+    if not gpu.gpu_present:
+        assert big == 1                                                     # STREAM (ssd 3000 MB/s)
+    if oracle.ref_available():
+        R = C.CDLL(str(oracle.REF_LIB))
+        R.ct_hal_set_ram_budget.argtypes = [C.c_uint64]
+        R.ct_hal_set_model.argtypes = [C.c_uint64, C.c_uint64, C.c_bool]
+        R.ct_hal_detect()
+        R.ct_hal_set_ram_budget(budget)
+        assert R.ct_hal_set_model(int(budget * 0.8), 1, False) == 0
+        if not gpu.gpu_present:
+            assert R.ct_hal_set_model(int(budget * 0.9), 1, True) == big
+    L.ct_hal_set_ram_budget(0)
+
+
+# ---- paged allocator bookkeeping (host-only handle) --------------------------
+
+def host_paged(S, MP, NP, P, W):
+    return ct.PagedKV(S, MP, NP, page_tokens=P, entry_dim=16, window_tokens=W, dtype=ct.CT_KV_BF16, device=-1)
+
+
+def replay_product(lens, S, P, NP, MP, W, splits=None):
+    h = host_paged(S, MP, NP, P, W)
+    lens = np.asarray(lens, np.int64)
+    edges = [0] + list(splits or []) + [int(lens.max())]
+    for a, b in zip(edges[:-1], edges[1:]):
+        ids = [s for s in range(S) if lens[s] > a]
+        cnt = [min(int(lens[s]), b) - a for s in ids]
+        ids = [s for s, c in zip(ids, cnt) if c > 0]
+        cnt = [c for c in cnt if c > 0]
+        if ids:
+            h.append(ids, cnt)
+    return h
+
+
+@pytest.mark.parametrize("splits", [None, [1, 2, 3, 17, 40, 41]])
+def test_product_allocator_matches_golden(splits):
+    g = np.load(GOLD / "alloc_ref.npz")
+    S, P, NP, MP, W = (int(v) for v in g["cfg"])
+    h = replay_product(g["lens"], S, P, NP, MP, W, splits)
+    assert np.array_equal(h.block_table(), g["bt"])
+    ev = np.array(h.evict_log(), np.int64)
+    assert np.array_equal(ev, g["events"])
+    assert np.array_equal(h.last_access().astype(np.uint32), g["last"])
+    st = h.stats()
+    assert st.n_pages_free == int(g["n_free"])
+    assert st.n_evict_window + st.n_evict_lru == len(ev)
+    assert ct.lib().ct_kv_paged_compact(h.h) == 0
+    assert np.array_equal(h.block_table(), g["compact_bt"])
+    h.close()
+
+
+@pytest.mark.parametrize("S,P,NP,W,lo,hi", [(40, 8, 60, 0, 1, 300), (64, 16, 90, 64, 16, 600),
+                                            (33, 4, 50, 20, 1, 200)])
+def test_product_allocator_matches_oracle(S, P, NP, W, lo, hi):
+    lens = oracle.lengths_loguniform(oracle.key(3, S), S, lo, hi)
+    MP = (hi + P - 1) // P + 1
+    rc, bt, owner, ev, last, nfree = oracle.alloc_replay(lens, S, P, NP, MP, W)
+    assert rc == 0
+    h = replay_product(lens, S, P, NP, MP, W)
+    assert np.array_equal(h.block_table(), bt)
+    assert h.evict_log() == ev
+    assert np.array_equal(h.seq_lens(), lens)
+    h.close()
+
+
+def test_product_allocator_eviction_compaction_full_size():
+    """The eviction + compaction workload at full size: 256 sequences with
+    log-uniform lengths 512..32768, 64-token pages, a pool of 60 % of the
+    pages demanded, sliding window 4096 -- tables and eviction log identical."""
+    S, P, W = 256, 64, 4096
+    lens = oracle.lengths_loguniform(oracle.key(3, 0), S, 512, 32768)
+    demand = int(sum((int(n) + P - 1) // P for n in lens))
+    NP = int(0.6 * demand)
+    MP = 32768 // P + 1
+    rc, bt, owner, ev, last, nfree = oracle.alloc_replay(lens, S, P, NP, MP, W)
+    assert rc == 0
+    h = replay_product(lens, S, P, NP, MP, W)
+    assert np.array_equal(h.block_table(), bt)
+    assert h.evict_log() == ev
+    cbt, cmap = oracle.compact_plan(bt)
+    assert ct.lib().ct_kv_paged_compact(h.h) == 0
+    assert np.array_equal(h.block_table(), cbt)
+    h.close()
+
+
+def test_product_allocator_full_pool_errors():
+    h = host_paged(2, 4, 1, 4, 0)
+    h.append([0], [2])                          # the only page, partly filled
+    with pytest.raises(RuntimeError):
+        h.append([1], [1])                      # only a partial tail page exists: nothing evictable
+    h.close()
+    h = host_paged(2, 4, 1, 4, 0)
+    h.append([0], [4])                          # the only page, full
+    h.append([1], [1])                          # -> LRU takes it
+    assert h.evict_log() == [(4, 0, 0, 0, 2)]
+    assert h.block_table()[0].tolist() == [-1] * 4 and h.block_table()[1, 0] == 0
+    h.close()
+
+
+def test_product_allocator_free_and_evict_api():
+    h = host_paged(3, 8, 6, 4, 0)
+    h.append([0, 1, 2], [8, 4, 6])              # 2 + 1 + 2 pages = 5 of 6
+    L = ct.lib()
+    assert L.ct_kv_paged_evict_lru(h.h, 2) == 2
+    ev = h.evict_log()
+    # all three appended in the same rounds; round of last access: seq0 -> 7, seq1 -> 3, seq2 -> 5
+    assert [(e[1], e[2]) for e in ev] == [(1, 0), (2, 0)]
+    assert L.ct_kv_paged_free_seq(h.h, 0) == 0
+    assert h.seq_lens().tolist() == [0, 4, 6] and (h.block_table()[0] < 0).all()
+    assert h.stats().n_pages_free == 6 - 1
+    h.close()
