@@ -1,0 +1,495 @@
+"""Benchmark of the paged MLA decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload sharded|mla32]
+
+Workload "sharded" (default; the configuration the headline metric is quoted
+on at 1/2/4/8 GPUs): 1024 sequences with context lengths log-uniform in
+512..65536 (seed 4), a bf16 MLA latent cache of 576-value entries (512 latent
++ 64 rope) in 64-token pages whose physical order is a random permutation,
+128 absorbed query heads, softmax scale 1/sqrt(192).  Sequences are sharded
+over the N ranks by longest-processing-time on their lengths; each rank holds
+only its sequences.  One step = append one new token to every sequence
+(quantise/convert on append) + paged MLA decode over all its tokens (split
+across the SMs, with the split-KV combine).  Total work is fixed as N grows
+("strong" scaling).  Workload "mla32": 32 sequences x 4096 tokens, seed 1.
+
+value: KV tokens attended per second over all ranks, inputs resident in HBM,
+timed with CUDA events on the launching stream (max over ranks).  e2e: the
+same step through ct_attn_mla_decode_step_host with the queries and new
+tokens in pinned host memory and the outputs copied back every step.
+roofline: the decode launch (MLA kernel + split-KV combine) against the
+measured HBM copy bandwidth; algorithmic bytes = 1152 B per attended token +
+queries + outputs.  cpu_baseline / --impl reference: the reference's own
+ct_attn_forward (oracle/_ref, compiled from the reference sources) over the
+same pages gathered to fp32, on a bounded sample of the workload, all host
+threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+E, DV, H, PAGE = 576, 512, 128, 64
+SCALE = float(1.0 / np.sqrt(192.0))
+BYTES_PER_TOKEN = E * 2
+METRIC = "decode KV tokens/s and achieved HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def workload(name):
+    """(lengths as stored in the cache before the step, description)."""
+    if name == "mla32":
+        lens = np.full(32, 4096 - 1, np.int64)
+        desc = "MLA paged decode, 32 seqs x 4096 tokens (after the appended token), seed 1"
+        seed = 1
+    else:
+        lens = lengths_loguniform(1024, 512, 65536, seed=4)
+        desc = ("sequence-sharded MLA serving: 1024 seqs, context log-uniform 512..65536 (seed 4), "
+                "one append + decode per seq")
+        seed = 4
+    return lens, desc, seed
+
+
+def lengths_loguniform(n, lo, hi, seed):
+    """Same rule as the oracle's generator (ct_oracle.c: floor(lo*(hi/lo)^u))."""
+    import cautreo_b200 as ct  # noqa: F401  (key derivation lives in the library)
+    key = ct.synth_key(seed, 0)
+    out = np.empty(n, np.int64)
+    for s in range(n):
+        z = splitmix(key + (s + 1) * 0x9E3779B97F4A7C15)
+        u = (z >> 11) * (1.0 / 9007199254740992.0)
+        t = np.floor(lo * np.exp(u * np.log(hi / lo)))
+        out[s] = int(min(max(t, lo), hi))
+    return out
+
+
+def splitmix(z):
+    m = (1 << 64) - 1
+    z &= m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    return z ^ (z >> 31)
+
+
+def physical_gpu(dev):
+    """nvidia-smi index of CUDA device `dev` (CUDA_VISIBLE_DEVICES remaps)."""
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if cvd:
+        ids = [x.strip() for x in cvd.split(",") if x.strip()]
+        if dev < len(ids) and ids[dev].isdigit():
+            return int(ids[dev])
+    return dev
+
+
+def measured_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(workload_name):
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "mla_decode_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload_name)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import cautreo_b200 as ct
+
+    torch.cuda.set_device(local_rank)
+    dev = local_rank
+    L = ct.lib()
+    lens_all, desc, seed = workload(args.workload)
+    n_all = len(lens_all)
+    rank_of = ct.lpt_shard(lens_all.astype(np.uint32), world) if world > 1 else np.zeros(n_all, np.int32)
+    mine = np.nonzero(rank_of == rank)[0]
+    lens = lens_all[mine]                               # tokens cached before the step
+    n = len(mine)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    # ---- cache: pages for len+1 tokens, physical order permuted ----
+    pages = ((lens + 1) + PAGE - 1) // PAGE
+    n_pages = int(pages.sum())
+    max_pages = int(pages.max())
+    kv = ct.PagedKV(n, max_pages, n_pages, PAGE, E, 0, ct.CT_KV_BF16, dev, sp)
+    perm = np.random.default_rng(seed * 1000 + rank).permutation(n_pages).astype(np.int32)
+    kv.set_free_order(perm)
+    kv.append(list(range(n)), (lens + 1).tolist(), None)          # reserve slots for len + 1 tokens
+    rows = torch.arange(n, dtype=torch.int32, device="cuda")
+    lens_dev = torch.from_numpy(lens.astype(np.int32)).cuda()
+    ct.check(L.ct_synth_fill_paged(kv.pool, None, ct.CT_KV_BF16, kv.block_table_dev, max_pages, rows.data_ptr(),
+                                   lens_dev.data_ptr(), n, int(lens.max()), PAGE, E, ct.synth_key(seed, 10), 0, 1.0,
+                                   sp), "fill")
+    bt = kv.block_table()
+    dest = np.array([bt[i, lens[i] // PAGE] * PAGE + lens[i] % PAGE for i in range(n)], np.int32)
+    dest_dev = torch.from_numpy(dest).cuda()
+    # ---- step inputs ----
+    q = torch.empty(n * H * E, dtype=torch.int16, device="cuda")
+    new_tok = torch.empty(n * E, dtype=torch.int16, device="cuda")
+    ct.check(L.ct_synth_fill(q.data_ptr(), 0, ct.synth_key(seed, 11), rank << 40, n * H * E, 0, 1.0, sp))
+    ct.check(L.ct_synth_fill(new_tok.data_ptr(), 0, ct.synth_key(seed, 13), rank << 40, n * E, 0, 1.0, sp))
+    out = torch.empty(n * H * DV, dtype=torch.int16, device="cuda")
+    att = (lens + 1).astype(np.int64)
+    plan = ct.MlaPlan(att.astype(np.int32), max_pages_per_seq=max_pages, device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        ct.check(L.ct_kv_paged_write_slots(kv.pool, None, ct.CT_KV_BF16, new_tok.data_ptr(), ct.CT_KV_BF16,
+                                           dest_dev.data_ptr(), n, E, sp))
+        ct.check(L.ct_attn_mla_decode_paged(plan.h, q.data_ptr(), kv.pool, None, kv.block_table_dev,
+                                            kv.seq_lens_dev, out.data_ptr(), None, sp))
+
+    group = dist.group.WORLD if world > 1 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(physical_gpu(dev))
+    clocks.start()
+    launches0 = ct.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        ct.check(L.ct_kv_paged_write_slots(kv.pool, None, ct.CT_KV_BF16, new_tok.data_ptr(), ct.CT_KV_BF16,
+                                           dest_dev.data_ptr(), n, E, sp))
+        ev[i][1].record(stream)
+        ct.check(L.ct_attn_mla_decode_paged(plan.h, q.data_ptr(), kv.pool, None, kv.block_table_dev,
+                                            kv.seq_lens_dev, out.data_ptr(), None, sp))
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    barrier()
+    launches = ct.launch_count() - launches0
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end)
+    dec_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in ev]))
+    app_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+    tokens = float(att.sum())
+
+    # ---- e2e through the host-buffer C-ABI call ----
+    import ctypes as C
+    qh = ct.lib().ct_hal_cuda_alloc_host(n * H * E * 2)
+    eh = ct.lib().ct_hal_cuda_alloc_host(n * E * 2)
+    oh = ct.lib().ct_hal_cuda_alloc_host(n * H * DV * 2)
+    q_host, tok_host = q.cpu().numpy(), new_tok.cpu().numpy()
+    C.memmove(qh, q_host.ctypes.data, n * H * E * 2)
+    C.memmove(eh, tok_host.ctypes.data, n * E * 2)
+
+    def step_host():
+        ct.check(L.ct_attn_mla_decode_step_host(plan.h, qh, eh, dest_dev.data_ptr(), kv.pool, None,
+                                                kv.block_table_dev, kv.seq_lens_dev, oh, sp))
+
+    for _ in range(max(1, args.warmup)):
+        step_host()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_host()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    for p_ in (qh, eh, oh):
+        ct.lib().ct_hal_cuda_free_host(p_)
+
+    # ---- reduce over ranks ----
+    import torch.distributed as dist
+    vals = torch.tensor([ms, e2e_ms, dec_ms, app_ms, tokens, float(launches), float(n)], dtype=torch.float64,
+                        device="cuda")
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+    else:
+        mx = sm = vals
+    ms_max, e2e_max, dec_max = float(mx[0]), float(mx[1]), float(mx[2])
+    tok_total = float(sm[4])
+    launches_total = int(sm[5])
+
+    # ---- the one exchange: gather outputs to rank 0 (timed separately) ----
+    gather_ms = None
+    if world > 1:
+        n_max = int(mx[6])
+        pad = torch.zeros(n_max * H * DV, dtype=torch.int16, device="cuda")
+        pad[:n * H * DV] = out
+        gl = [torch.empty_like(pad) for _ in range(world)] if rank == 0 else None
+        torch.cuda.synchronize()
+        g0 = time.perf_counter()
+        dist.gather(pad, gl, dst=0)
+        torch.cuda.synchronize()
+        gather_ms = (time.perf_counter() - g0) * 1e3
+        if rank == 0:
+            full = torch.empty((n_all, H * DV), dtype=torch.int16, device="cuda")
+            for r in range(world):
+                ids = np.nonzero(rank_of == r)[0]
+                full[torch.from_numpy(ids).cuda()] = gl[r].view(n_max, H * DV)[:len(ids)]
+
+    if rank != 0:
+        return None
+    hbm, hbm_kind = measured_hbm()
+    bytes_dec = tok_total * BYTES_PER_TOKEN + n_all * H * E * 2 + n_all * H * DV * 2
+    achieved = bytes_dec / (dec_max * 1e-3) / 1e9
+    value = tok_total * args.steps / (ms_max * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "KV tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded SplitMix64/Box-Muller latents and queries, generated on the device)",
+        "config": {"workload": desc, "n_seqs": int(n_all), "heads": H, "entry_dim": E, "v_dim": DV,
+                   "page_tokens": PAGE, "kv_dtype": "bf16", "softmax_scale": "1/sqrt(192)",
+                   "kv_tokens_per_step": int(tok_total), "sharding": "LPT by length" if world > 1 else "none",
+                   "parallelism": f"sequence-sharded x{world}",
+                   "l2": "inputs larger than L2 (per-GPU KV >= 1.9 GB vs 126 MB L2); no flush"},
+        "hbm_gbs": tok_total * args.steps * BYTES_PER_TOKEN / (ms_max * 1e-3) / 1e9,
+        "gpu_launches": launches_total,
+        "e2e": {"value": tok_total * args.steps / (e2e_max * 1e-3), "unit": "KV tokens/s",
+                "h2d_bytes_per_step": int(n_all * H * E * 2 + n_all * E * 2),
+                "d2h_bytes_per_step": int(n_all * H * DV * 2),
+                "path": "ct_attn_mla_decode_step_host (pinned host q/new tokens in, outputs out)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": committed_traffic(args.workload), "peak_kind": hbm_kind,
+                     "kernel": "MLA decode + split-KV combine (one ct_attn_mla_decode_paged call)",
+                     "decode_ms": dec_max, "append_ms": float(mx[3])},
+        "clocks": clk,
+    }
+    if gather_ms is not None:
+        line["gather_ms"] = gather_ms
+    return line
+
+
+# ---------------------------------------------------------------------------
+# CPU arms: the reference's own ct_attn_forward on gathered pages
+# ---------------------------------------------------------------------------
+
+CPU_TOKEN_CAP = 8192
+
+
+def cpu_sample(lens, seed, budget_s, threads):
+    """Decode sequences of the workload (64 stratified over the lengths, in a
+    seeded order) with the reference ct_attn_forward on all host threads until
+    ~budget_s of decode time; each sequence is decoded over its first
+    min(len, 8192) tokens so one call stays a few seconds (per-token cost
+    still grows past that length, so the sample reads slightly fast).
+    Input generation is outside the timed calls.  Returns (tokens/s, tokens,
+    seconds): tokens over the busiest thread's decode time."""
+    import concurrent.futures as cf
+    import oracle
+    R = oracle.ref()
+    order = np.argsort(lens)
+    strat = order[np.linspace(0, len(order) - 1, min(len(order), 64)).astype(int)]
+    rng = np.random.default_rng(seed)
+    rng.shuffle(strat)
+    O = oracle.port()
+    key_kv = O.orc_key(seed, 10)
+    key_q = O.orc_key(seed, 11)
+    busy = {}
+    lock = threading.Lock()
+    stop = threading.Event()
+
+    def one(s):
+        if stop.is_set():
+            return 0
+        n = min(int(lens[s]) + 1, CPU_TOKEN_CAP)
+        kv = oracle.bf16_to_f32(oracle.normal_bf16(key_kv, (int(s) << 24) * E, n * E))
+        q = oracle.bf16_to_f32(oracle.normal_bf16(key_q, int(s) * H * E, H * E))
+        o = np.empty(H * E, np.float32)
+        t0 = time.perf_counter()
+        R.ct_attn_forward(q.ctypes.data, kv.ctypes.data, kv.ctypes.data, n, H, E, SCALE, o.ctypes.data)
+        dt = time.perf_counter() - t0
+        tid = threading.get_ident()
+        with lock:
+            busy[tid] = busy.get(tid, 0.0) + dt
+            if max(busy.values()) > budget_s:
+                stop.set()
+        return n
+
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        tok = sum(ex.map(one, strat))
+    t = max(busy.values()) if busy else 1e-9
+    return tok / t, tok, t
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    try:
+        import oracle
+        if not oracle.ref_available():
+            return {"impl": "reference", "unavailable": "reference objects (oracle/_ref/libctref.so) not built"}
+    except Exception as e:  # pragma: no cover
+        return {"impl": "reference", "unavailable": f"oracle import failed: {e}"}
+    lens, desc, seed = workload(args.workload)
+    threads = os.cpu_count() or 1
+    per_step = max(3.0, 60.0 / max(1, args.steps + args.warmup))
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, tok, el = cpu_sample(lens, seed + i, per_step, threads)
+        if i >= args.warmup:
+            rates.append(r)
+    value = float(np.mean(rates))
+    sample = (f"stratified sequences of the workload (first <= {CPU_TOKEN_CAP} tokens each), ~{per_step:.0f} s of "
+              f"decode per step through the reference ct_attn_forward (all 128 heads share the gathered fp32 "
+              f"[n][576] entries)")
+    return {"metric": METRIC, "value": value, "unit": "KV tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64 accumulate (f32 in/out)", "data": "synthetic",
+            "config": {"workload": desc}, "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "KV tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "KV tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="sharded", choices=["sharded", "mla32"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    if args.impl == "reference":
+        line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if line is not None and world == 1 and not args.no_cpu_baseline:
+            lens, desc, seed = workload(args.workload)
+            try:
+                import oracle
+                if oracle.ref_available():
+                    r, tok, el = cpu_sample(lens, seed, args.cpu_seconds, os.cpu_count() or 1)
+                    line["cpu_baseline"] = {"value": r, "unit": "KV tokens/s", "cores": os.cpu_count() or 1,
+                                            "kind": "reference",
+                                            "sample": f"{tok} KV tokens of stratified sequences (first <= "
+                                                      f"{CPU_TOKEN_CAP} tokens each) in {el:.1f} s of decode through "
+                                                      f"the reference ct_attn_forward on gathered fp32 pages"}
+            except Exception as e:  # pragma: no cover
+                line["cpu_baseline"] = {"value": None, "error": str(e)}
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -77,6 +77,7 @@ struct ct_mla_plan {
     ct_mla_combine_t *combines;  /* device [n_combines] */
     float *part_o, *part_ml;     /* device scratch */
     size_t scratch_bytes;
+    void *stage_q, *stage_e, *stage_o;   /* device staging of ct_attn_mla_decode_step_host */
     uint32_t last_launches;
 };
 
@@ -88,6 +89,7 @@ void ct_mla_plan_destroy(ct_mla_plan_t *p) {
     if (!p) return;
     cudaFree(p->chunks); cudaFree(p->worker_begin); cudaFree(p->combines);
     cudaFree(p->part_o); cudaFree(p->part_ml);
+    cudaFree(p->stage_q); cudaFree(p->stage_e); cudaFree(p->stage_o);
     free(p);
 }
 
@@ -219,5 +221,33 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
                                    p->n_combines, q, pool, scales, block_table, seq_lens, out, lse, p->part_o,
                                    p->part_ml, stream, &launches);
     p->last_launches = launches;
+    return rc;
+}
+
+int ct_attn_mla_decode_step_host(ct_mla_plan_t *p, const void *q_host, const void *entries_host,
+                                 const int32_t *dest_slot, void *pool, float *scales,
+                                 const int32_t *block_table, const int32_t *seq_lens, void *out_host,
+                                 void *stream) {
+    if (!p || !q_host || !out_host || !pool || !block_table || !seq_lens) return CT_ERR_ARG;
+    if (dest_slot && !entries_host) return CT_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t n = p->n_seq, H = p->dims.n_heads, E = p->dims.entry_dim, Dv = p->dims.v_dim;
+    const size_t qb = n * H * E * 2, eb = n * E * 2, ob = n * H * Dv * 2;
+    int rc = CT_OK;
+    if (!p->stage_q) {
+        rc = ct__cuda_status(cudaMalloc(&p->stage_q, qb ? qb : 16), "step_host staging");
+        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_e, eb ? eb : 16), "step_host staging");
+        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_o, ob ? ob : 16), "step_host staging");
+        if (rc) return rc;
+    }
+    rc = ct__cuda_status(cudaMemcpyAsync(p->stage_q, q_host, qb, cudaMemcpyHostToDevice, st), "step_host q");
+    if (!rc && dest_slot) {
+        rc = ct__cuda_status(cudaMemcpyAsync(p->stage_e, entries_host, eb, cudaMemcpyHostToDevice, st), "step_host e");
+        if (!rc) rc = ct_kv_paged_write_slots(pool, scales, p->dims.kv_dtype, p->stage_e, CT_KV_BF16, dest_slot,
+                                              (uint32_t)n, (uint32_t)E, stream);
+    }
+    if (!rc) rc = ct_attn_mla_decode_paged(p, p->stage_q, pool, scales, block_table, seq_lens, p->stage_o, NULL, stream);
+    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(out_host, p->stage_o, ob, cudaMemcpyDeviceToHost, st), "step_host out");
+    if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(st), "step_host sync");
     return rc;
 }

@@ -405,7 +405,8 @@ int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t
         free(dest);
         return rc;
     }
-    rc = flush(h, dest, (uint32_t)total, entries, src_dtype);
+    /* Without entries only the tables change: the slots need not travel. */
+    rc = flush(h, dest, entries ? (uint32_t)total : 0u, entries, src_dtype);
     free(dest);
     return rc;
 }

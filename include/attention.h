@@ -106,6 +106,19 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
 /* Number of kernel launches the last ct_attn_mla_decode_paged issued. */
 uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p);
 
+/* One serving step with host I/O, for callers that keep inputs and outputs
+ * in host memory: copies q_host ([n_seq][n_heads][entry_dim] bf16) and
+ * entries_host ([n_seq][entry_dim] bf16, the token appended to each sequence)
+ * to the device, writes the new tokens to dest_slot (device int32, as
+ * ct_kv_paged_write_slots; NULL skips the append), decodes, and copies
+ * out_host ([n_seq][n_heads][v_dim] bf16) back.  Returns when out_host is
+ * filled.  The plan keeps the device staging buffers between calls; pinned
+ * host buffers give the fastest copies. */
+int ct_attn_mla_decode_step_host(ct_mla_plan_t *plan, const void *q_host, const void *entries_host,
+                                 const int32_t *dest_slot, void *pool, float *scales,
+                                 const int32_t *block_table, const int32_t *seq_lens, void *out_host,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

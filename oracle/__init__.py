@@ -205,9 +205,10 @@ def mla_decode_paged(pool_bf16, bt, seq_lens, q_bf16, H, E, Dv, page_tokens, sca
     out = np.empty((n_seq, H, Dv), np.float32)
     bt = np.ascontiguousarray(bt, np.int32)
     lens = np.ascontiguousarray(seq_lens, np.int32)
-    rc = port().orc_mla_decode_paged_bf16(ptr(np.ascontiguousarray(pool_bf16)), ptr(bt), bt.shape[1], ptr(lens),
-                                          n_seq, ptr(np.ascontiguousarray(q_bf16)), H, E, Dv, page_tokens, scale,
-                                          n_threads, ptr(out))
+    pool_c = np.ascontiguousarray(pool_bf16)        # keep references for the duration of the call
+    q_c = np.ascontiguousarray(q_bf16)
+    rc = port().orc_mla_decode_paged_bf16(ptr(pool_c), ptr(bt), bt.shape[1], ptr(lens), n_seq, ptr(q_c), H, E, Dv,
+                                          page_tokens, scale, n_threads, ptr(out))
     if rc != 0:
         raise RuntimeError("oracle mla decode failed")
     return out

@@ -1,0 +1,200 @@
+"""GPU: paged absorbed-MLA decode (ct_attn_mla_decode_paged) against the
+oracle, whose MLA numerics are pinned bit-exactly to the reference's own
+ct_attn_forward (tests/test_oracle.py).  Tolerance (bf16 inputs, fp32
+accumulation): max-abs <= 2e-2 and norm-relative <= 1e-2."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cautreo_b200 as ct
+import oracle
+from gpu_util import dev, empty, host, stream
+from helpers import ATOL, MLA_DV, MLA_E, MLA_H, MLA_SCALE, PAGE, RTOL, close, mla_case
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+O = oracle.port()
+
+
+def run_decode(pool, bt, lens, q, H=MLA_H, E=MLA_E, Dv=MLA_DV, P=PAGE, dtype=ct.CT_KV_BF16, scales=None,
+               want_lse=False):
+    lens = np.asarray(lens, np.int32)
+    plan = ct.MlaPlan(lens, n_heads=H, entry_dim=E, v_dim=Dv, page_tokens=P, max_pages_per_seq=bt.shape[1],
+                      kv_dtype=dtype, scale=MLA_SCALE)
+    out = empty((len(lens), H, Dv), np.uint16)
+    lse = empty((len(lens), H), np.float32) if want_lse else None
+    pd, qd, btd, ld = dev(pool), dev(q), dev(bt), dev(lens)       # alive until the results are read
+    sd = dev(scales) if scales is not None else None
+    plan.decode(qd.data_ptr(), pd.data_ptr(), sd.data_ptr() if sd is not None else None,
+                btd.data_ptr(), ld.data_ptr(), out.data_ptr(), lse.data_ptr() if lse is not None else None,
+                stream())
+    got = oracle.bf16_to_f32(host(out, np.uint16)).reshape(len(lens), H, Dv)
+    return (got, host(lse, np.float32), plan) if want_lse else (got, plan)
+
+
+def oracle_decode_f32(poolf, bt, lens, qf, H, E, Dv, P):
+    out = np.zeros((len(lens), H, Dv), np.float32)
+    for s, n in enumerate(lens):
+        rows = [poolf[bt[s, t // P], t % P] for t in range(int(n)) if bt[s, t // P] >= 0]
+        if not rows:
+            continue
+        kv = np.ascontiguousarray(np.stack(rows), np.float32)
+        qs = np.ascontiguousarray(qf[s], np.float32)
+        assert O.orc_mla_decode(qs.ctypes.data, kv.ctypes.data, len(rows), H, E, Dv, MLA_SCALE,
+                                out[s].ctypes.data) == 0
+    return out
+
+
+@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 130, 0, 200], [4096], [1], [0, 0], [777, 1500, 64 * 17 + 3]])
+def test_mla_small_cases(lens):
+    pool, bt, q = mla_case(lens, seed=1)
+    before = ct.launch_count()
+    got, plan = run_decode(pool, bt, lens, q)
+    assert ct.launch_count() > before
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+    for s, n in enumerate(lens):
+        if n == 0:
+            assert np.all(got[s] == 0)
+
+
+def test_mla_matches_reference_golden_16_heads():
+    """16-head case of mla_ref.npz, computed by the reference's own
+    ct_attn_forward over gathered pages (runs the CUDA-core kernel)."""
+    g = np.load(GOLD / "mla_ref.npz")
+    lens = g["lens"]
+    H = int(g["heads"])
+    pool, bt, q = mla_case(lens, seed=1, H=H)
+    got, _ = run_decode(pool, bt, lens, q, H=H)
+    ok, mx, rel = close(got, g["out"])
+    assert ok, (mx, rel)
+
+
+def test_mla_lse_and_splits():
+    lens = [5000, 3, 12000]
+    pool, bt, q = mla_case(lens, seed=3)
+    got, lse, plan = run_decode(pool, bt, lens, q, want_lse=True)
+    assert plan.n_chunks > len(lens)                 # long sequences were split across workers
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+    # log-sum-exp of the scaled scores, from the oracle's fp64 scores
+    for s, n in enumerate(lens):
+        kv = np.stack([oracle.bf16_to_f32(pool[bt[s, t // PAGE], t % PAGE]) for t in range(n)]).astype(np.float64)
+        sc = (oracle.bf16_to_f32(q[s]).astype(np.float64) @ kv.T) * MLA_SCALE
+        m = sc.max(axis=1)
+        ref = m + np.log(np.exp(sc - m[:, None]).sum(axis=1))
+        np.testing.assert_allclose(lse[s], ref, rtol=1e-4, atol=1e-3)
+
+
+def test_mla_evicted_pages_are_skipped():
+    lens = [300, 300]
+    pool, bt, q = mla_case(lens, seed=4)
+    bt = bt.copy()
+    bt[0, 1] = -1                                    # an LRU-evicted page
+    bt[1, 0] = -1                                    # a window-freed head
+    got, _ = run_decode(pool, bt, lens, q)
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+
+
+@pytest.mark.parametrize("dtype", [ct.CT_KV_INT8, ct.CT_KV_E4M3])
+def test_mla_quantised_pool(dtype):
+    """Decode over int8 / e4m3 pages (dequantised on load) against the oracle
+    run on the dequantised codes and scales; latent ~N(0,1) with 1 % x20."""
+    lens = [700, 64, 2049]
+    pool16, bt, q = mla_case(lens, seed=2, outlier_bp=100, outlier_mul=20.0)
+    NP = pool16.shape[0]
+    xf = oracle.bf16_to_f32(pool16.reshape(-1)).reshape(NP * PAGE, MLA_E)
+    codes = np.zeros(NP * PAGE * MLA_E, np.uint8)
+    sc = np.zeros(NP * PAGE, np.float32)
+    back = np.zeros(NP * PAGE * MLA_E, np.float32)
+    xf = np.ascontiguousarray(xf)
+    if dtype == ct.CT_KV_INT8:
+        O.orc_kv_quant_int8(xf.ctypes.data, NP * PAGE, MLA_E, codes.ctypes.data, sc.ctypes.data)
+        O.orc_kv_dequant_int8(codes.ctypes.data, sc.ctypes.data, NP * PAGE, MLA_E, back.ctypes.data)
+    else:
+        O.orc_kv_quant_e4m3(xf.ctypes.data, NP * PAGE, MLA_E, codes.ctypes.data, sc.ctypes.data)
+        O.orc_kv_dequant_e4m3(codes.ctypes.data, sc.ctypes.data, NP * PAGE, MLA_E, back.ctypes.data)
+    got, _ = run_decode(codes, bt, lens, q, dtype=dtype, scales=sc)
+    want = oracle_decode_f32(back.reshape(NP, PAGE, MLA_E), bt, lens, oracle.bf16_to_f32(q.reshape(-1)).reshape(
+        q.shape), MLA_H, MLA_E, MLA_DV, PAGE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+
+
+def test_mla_full_size_batch32_ctx4096():
+    """The MLA paged decode configuration at full size: 32 sequences x 4096
+    tokens, 128 heads, 576-d bf16 entries, 64-token pages in one random
+    permutation of the pool.  Parity on 4 sequences against the oracle, and
+    size-independent checks on all 32: a zero query attends uniformly (output
+    = mean of the latents), and permuting the pages does not change results."""
+    S, T = 32, 4096
+    lens = [T] * S
+    pool, bt, q = mla_case(lens, seed=1)
+    got, plan = run_decode(pool, bt, lens, q)
+    assert plan.n_chunks >= S
+    sub = [0, 9, 22, 31]
+    want = oracle.mla_decode_paged(pool, bt[sub], [T] * len(sub), q[sub], MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got[sub], want)
+    assert ok, (mx, rel)
+    # zero query -> uniform softmax -> mean latent (all heads)
+    q0 = np.zeros_like(q)
+    got0, _ = run_decode(pool, bt, lens, q0)
+    pd = torch.from_numpy(pool.view(np.int16)).cuda().view(torch.bfloat16).float()
+    btd = torch.from_numpy(bt.astype(np.int64)).cuda()
+    mean = pd[btd].reshape(S, T, MLA_E)[:, :, :MLA_DV].mean(dim=1).cpu().numpy()
+    assert np.abs(got0 - mean[:, None, :]).max() < 2e-2
+    # re-permute physical pages
+    perm = oracle.permutation(oracle.key(1, 77), pool.shape[0])
+    inv = np.argsort(perm)
+    pool2 = pool[perm]
+    bt2 = inv[bt].astype(np.int32)
+    got2, _ = run_decode(pool2, bt2, lens, q)
+    assert np.array_equal(got2, got)
+
+
+def test_mla_variable_lengths_sharded_shape():
+    """Log-uniform lengths (the sequence-sharded serving shape, reduced to 48
+    sequences of 512..16384 tokens); parity on a stratified subset."""
+    lens = oracle.lengths_loguniform(oracle.key(4, 0), 48, 512, 16384).astype(np.int32)
+    pool, bt, q = mla_case(lens, seed=4)
+    got, plan = run_decode(pool, bt, lens, q)
+    order = np.argsort(lens)
+    sub = sorted(set(order[[0, 12, 24, 36, 47]].tolist()))
+    want = oracle.mla_decode_paged(pool, bt[sub], lens[sub], q[sub], MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got[sub], want)
+    assert ok, (mx, rel)
+
+
+def test_mla_through_paged_handle():
+    """Append through ct_kv_paged_append, then decode the handle's pool."""
+    S, E = 3, MLA_E
+    lens = [100, 64, 257]
+    total = sum(lens)
+    x = oracle.normal_bf16(oracle.key(6, 3), 0, total * E).reshape(total, E)
+    h = ct.PagedKV(S, 8, 20, PAGE, E, 0, ct.CT_KV_BF16, 0, stream())
+    h.set_free_order(oracle.permutation(oracle.key(6, 4), 20))
+    xd = dev(x)
+    h.append(list(range(S)), lens, xd.data_ptr(), ct.CT_KV_BF16)
+    q = oracle.normal_bf16(oracle.key(6, 5), 0, S * MLA_H * E).reshape(S, MLA_H, E)
+    plan = ct.MlaPlan(lens, max_pages_per_seq=8)
+    out = empty((S, MLA_H, MLA_DV), np.uint16)
+    qd = dev(q)
+    plan.decode(qd.data_ptr(), h.pool, None, h.block_table_dev, h.seq_lens_dev, out.data_ptr(), None, stream())
+    got = oracle.bf16_to_f32(host(out, np.uint16)).reshape(S, MLA_H, MLA_DV)
+    bt = h.block_table()
+    pool = np.zeros((20, PAGE, E), np.uint16)
+    off = 0
+    for s, n in enumerate(lens):
+        for t in range(n):
+            pool[bt[s, t // PAGE], t % PAGE] = x[off + t]
+        off += n
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+    h.close()

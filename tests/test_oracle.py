@@ -107,7 +107,8 @@ def test_q8_0_matches_golden():
     g = np.load(GOLD / "quant_ref.npz")
     x = g["x"]
     enc = np.zeros((len(x), 34), np.uint8)
-    O.orc_q8_0_quantize(oracle.ptr(np.ascontiguousarray(x)), oracle.ptr(enc), x.size)
+    xc = np.ascontiguousarray(x)
+    O.orc_q8_0_quantize(oracle.ptr(xc), oracle.ptr(enc), x.size)
     assert np.array_equal(enc, g["enc1"])
     dec = np.zeros_like(x)
     O.orc_q8_0_dequantize(oracle.ptr(enc), oracle.ptr(dec), x.size)
@@ -239,7 +240,8 @@ def test_mla_skips_unmapped_pages():
     # attending only tokens 64..199 equals decoding a sequence made of those tokens
     kv = np.stack([oracle.bf16_to_f32(pool[bt[0, t // PAGE], t % PAGE]) for t in range(64, 200)])
     o = np.zeros((4, MLA_DV), np.float32)
-    O.orc_mla_decode(oracle.ptr(np.ascontiguousarray(oracle.bf16_to_f32(q[0]))), oracle.ptr(kv), 136, 4, MLA_E,
+    q0 = np.ascontiguousarray(oracle.bf16_to_f32(q[0]))
+    O.orc_mla_decode(oracle.ptr(q0), oracle.ptr(kv), 136, 4, MLA_E,
                      MLA_DV, MLA_SCALE, oracle.ptr(o))
     assert np.array_equal(bits(part[0]), bits(o))
     assert not np.array_equal(part, full)
