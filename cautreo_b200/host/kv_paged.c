@@ -380,12 +380,17 @@ int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t
     }
     if (rc == CT_OK && total > 1) {
         /* Last writer wins when a page was freed and reused inside the call:
-         * keep only the final write of each slot. */
-        for (size_t t = total; t-- > 0;) {
-            int32_t sl = dest[t];
-            if (sl < 0) continue;
-            if (h->claimed[sl >> 3] & (1u << (sl & 7))) dest[t] = -1;
-            else h->claimed[sl >> 3] |= (uint8_t)(1u << (sl & 7));
+         * walk the writes backwards in time (rounds descending, then array
+         * order descending) and keep only the final write of each slot. */
+        for (uint32_t k = maxc; k-- > 0;) {
+            for (uint32_t i = n; i-- > 0;) {
+                if (k >= counts[i]) continue;
+                int32_t *d = &dest[off[i] + k];
+                int32_t sl = *d;
+                if (sl < 0) continue;
+                if (h->claimed[sl >> 3] & (1u << (sl & 7))) *d = -1;
+                else h->claimed[sl >> 3] |= (uint8_t)(1u << (sl & 7));
+            }
         }
         for (size_t t = 0; t < total; t++) {
             int32_t sl = dest[t];

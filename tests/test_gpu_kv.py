@@ -218,11 +218,13 @@ def test_paged_eviction_contents_and_compaction(S, P, NP, W, lo, hi, splits):
             ph = bt[s, lp]
             for j in range(P):
                 o = int(owner[ph, j])
+                if lp * P + j < int(lens[s]):              # a slot of this sequence's history
+                    assert o == (s << 32 | (lp * P + j))
                 if o == (1 << 64) - 1:
                     continue
+                # slots past the sequence's end keep the previous owner's token
                 os_, ot = o >> 32, o & 0xFFFFFFFF
-                assert os_ == s
-                assert np.array_equal(pool[ph, j], vals[s][ot])
+                assert np.array_equal(pool[ph, j], vals[os_][ot])
     cbt, cmap = oracle.compact_plan(bt)
     ct.check(ct.lib().ct_kv_paged_compact(h.h))
     assert np.array_equal(h.block_table(), cbt)
