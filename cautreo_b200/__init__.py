@@ -130,6 +130,7 @@ SIGNATURES = {
     "ct_attn_mla_decode_paged": (I, [P, P, P, P, P, P, P, P, P]),
     "ct_mla_plan_launches": (U32, [P]),
     "ct_attn_mla_decode_step_host": (I, [P, P, P, P, P, P, P, P, P, P]),
+    "ct_attn_mla_decode_paged_noalloc": (I, [C.POINTER(MlaShape), P, U32, P, P, P, P, P, P, P, P]),
     # quant.h
     "ct_quant_q8_0": (V, [P, P, I64]),
     "ct_quant_q4_0": (V, [P, P, I64]),

@@ -119,6 +119,34 @@ int ct_attn_mla_decode_step_host(ct_mla_plan_t *plan, const void *q_host, const 
                                  const int32_t *block_table, const int32_t *seq_lens, void *out_host,
                                  void *stream);
 
+/* ---- the same decode without any allocation ---------------------------- */
+
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory on their decode path -- an engine that reserved nearly all of HBM
+ * for its KV pool at start-up, where a later cudaMalloc would fail, or a
+ * latency-bound serving loop that bans allocator calls (and the
+ * synchronisation they bring) once running.  Computes what
+ * ct_mla_plan_create + ct_attn_mla_decode_paged compute, but plans on the host
+ * into static arrays and keeps its work list and split-KV partials in one
+ * fixed device array of CT_MLA_NOALLOC_SCRATCH_BYTES inside the library, which
+ * every GPU that loads the library holds until the process exits.  It calls
+ * no cudaMalloc / cudaFree and no allocating library routine.
+ *
+ * Sequence s reads block-table row s.  seq_lens_host and seq_lens (device)
+ * hold the same lengths.  Limits: n_seq <= CT_MLA_NOALLOC_MAX_SEQS, and the
+ * split-KV partials (at most 2 x 59 sequences' worth of n_heads x v_dim fp32)
+ * must fit the array; beyond either limit the call returns CT_ERR_ARG and
+ * ct_hal_cuda_last_error() says which.  The first call on each device looks
+ * up the array's device address with that device current, so make it before
+ * any stream capture.  All calls share the array and leave their contents in
+ * it; calls that overlap on the GPU race, so serialise them. */
+#define CT_MLA_NOALLOC_SCRATCH_BYTES (32u << 20)
+#define CT_MLA_NOALLOC_MAX_SEQS 4096u
+int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, const int32_t *seq_lens_host,
+                                     uint32_t n_seq, const void *q, const void *pool,
+                                     const float *scales, const int32_t *block_table,
+                                     const int32_t *seq_lens, void *out, float *lse, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
