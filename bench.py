@@ -210,7 +210,7 @@ def run_ours(args, rank, world, local_rank):
     ct.check(L.ct_synth_fill(new_tok.data_ptr(), 0, ct.synth_key(seed, 13), rank << 40, n * E, 0, 1.0, sp))
     out = torch.empty(n * H * DV, dtype=torch.int16, device="cuda")
     att = (lens + 1).astype(np.int64)
-    plan = ct.MlaPlan(att.astype(np.int32), max_pages_per_seq=max_pages, device=dev)
+    plan = ct.MlaPlan(att.astype(np.int32), n_pages, max_pages_per_seq=max_pages, device=dev)
     torch.cuda.synchronize()
 
     def step():

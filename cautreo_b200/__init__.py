@@ -61,7 +61,7 @@ class EvictEvent(C.Structure):
 class MlaShape(C.Structure):
     _fields_ = [("n_heads", C.c_uint32), ("entry_dim", C.c_uint32), ("v_dim", C.c_uint32),
                 ("page_tokens", C.c_uint32), ("max_pages_per_seq", C.c_uint32), ("kv_dtype", C.c_uint32),
-                ("scale", C.c_float)]
+                ("scale", C.c_float), ("n_pages", C.c_uint32)]
 
 
 class Scorecard(C.Structure):
@@ -129,8 +129,11 @@ SIGNATURES = {
     "ct_mla_plan_scratch_bytes": (SZ, [P]),
     "ct_attn_mla_decode_paged": (I, [P, P, P, P, P, P, P, P, P]),
     "ct_mla_plan_launches": (U32, [P]),
+    "ct_mla_plan_workers": (U32, [P]),
+    "ct_mla_plan_tensor_cores": (I, [P]),
     "ct_attn_mla_decode_step_host": (I, [P, P, P, P, P, P, P, P, P, P]),
     "ct_attn_mla_decode_paged_noalloc": (I, [C.POINTER(MlaShape), P, U32, P, P, P, P, P, P, P, P]),
+    "ct_mla_tc_error": (I, [I]),
     # quant.h
     "ct_quant_q8_0": (V, [P, P, I64]),
     "ct_quant_q4_0": (V, [P, P, I64]),
@@ -345,14 +348,14 @@ class PagedKV:
 class MlaPlan:
     """ct_mla_plan_t for a fixed set of sequence lengths."""
 
-    def __init__(self, seq_lens, n_heads=128, entry_dim=576, v_dim=512, page_tokens=64, max_pages_per_seq=None,
-                 kv_dtype=CT_KV_BF16, scale=None, seq_rows=None, device=0):
+    def __init__(self, seq_lens, n_pages, n_heads=128, entry_dim=576, v_dim=512, page_tokens=64,
+                 max_pages_per_seq=None, kv_dtype=CT_KV_BF16, scale=None, seq_rows=None, device=0):
         seq_lens = np.ascontiguousarray(seq_lens, np.int32)
         if max_pages_per_seq is None:
             max_pages_per_seq = int(max(1, (int(seq_lens.max(initial=0)) + page_tokens - 1) // page_tokens))
         if scale is None:
             scale = 1.0 / np.sqrt(192.0)
-        self.shape = MlaShape(n_heads, entry_dim, v_dim, page_tokens, max_pages_per_seq, kv_dtype, scale)
+        self.shape = MlaShape(n_heads, entry_dim, v_dim, page_tokens, max_pages_per_seq, kv_dtype, scale, n_pages)
         rows = None if seq_rows is None else np.ascontiguousarray(seq_rows, np.uint32)
         self._rows = rows
         self.n_seq = len(seq_lens)
@@ -375,6 +378,14 @@ class MlaPlan:
     @property
     def launches(self):
         return int(lib().ct_mla_plan_launches(self.h))
+
+    @property
+    def workers(self):
+        return int(lib().ct_mla_plan_workers(self.h))
+
+    @property
+    def tensor_cores(self):
+        return bool(lib().ct_mla_plan_tensor_cores(self.h))
 
     def decode(self, q, pool, scales, block_table, seq_lens, out, lse=None, stream=None):
         rc = lib().ct_attn_mla_decode_paged(self.h, ptr(q), ptr(pool), ptr(scales), ptr(block_table),

@@ -41,6 +41,8 @@ typedef struct {
 typedef struct {
     uint32_t n_heads, entry_dim, v_dim, page_tokens, max_pages_per_seq, kv_dtype;
     float    scale;
+    uint32_t n_pages;    /* pool pages: bounds every page read */
+    uint32_t n_seq;      /* rows of q / out */
 } ct_mla_dims_t;
 
 /* ---- launchers (csrc); all return a ct_status_t ------------------------- */

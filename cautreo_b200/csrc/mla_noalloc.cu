@@ -80,7 +80,7 @@ extern "C" int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, con
                                                 const int32_t *seq_lens, void *out, float *lse, void *stream) {
     if (!shape || !seq_lens_host || !q || !pool || !block_table || !seq_lens || !out) return CT_ERR_ARG;
     if (shape->n_heads == 0 || shape->page_tokens == 0 || shape->entry_dim == 0 || shape->v_dim > shape->entry_dim ||
-        shape->max_pages_per_seq == 0) {
+        shape->max_pages_per_seq == 0 || shape->n_pages == 0) {
         ct__set_error("ct_attn_mla_decode_paged_noalloc: bad shape");
         return CT_ERR_ARG;
     }
@@ -97,6 +97,8 @@ extern "C" int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, con
     dims.max_pages_per_seq = shape->max_pages_per_seq;
     dims.kv_dtype = shape->kv_dtype;
     dims.scale = shape->scale;
+    dims.n_pages = shape->n_pages;
+    dims.n_seq = n_seq;
     const uint32_t P = shape->page_tokens;
 
     void *scratch = nullptr;

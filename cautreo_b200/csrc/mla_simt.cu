@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(256) k_mla_simt(ct_mla_dims_t dims, const ct_m
     for (int32_t lp = ch.page_begin; lp < ch.page_end; lp++) {
         const int32_t pg = block_table[(size_t)ch.row * dims.max_pages_per_seq + lp];
         const int32_t ntok = min((int32_t)P, len - lp * (int32_t)P);
-        if (pg < 0 || ntok <= 0) continue;
+        if (pg < 0 || (uint32_t)pg >= dims.n_pages || ntok <= 0) continue;
         for (int32_t sub = 0; sub < ntok; sub += TT) {
             const uint32_t nt = (uint32_t)min(TT, ntok - sub);
             __syncthreads();

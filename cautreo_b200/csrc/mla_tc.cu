@@ -1,23 +1,727 @@
 /*
  * mla_tc.cu -- paged absorbed-MLA decode on the 5th-generation tensor cores
- * (tcgen05 + TMEM + TMA) for the DeepSeek shape: 128 query heads, 576-value
- * entries (512 latent + 64 rope), 512 value dims, 64-token bf16 pages.
+ * (tcgen05 + TMEM + TMA) for the DeepSeek shape: 128 query heads sharing one
+ * cache entry of 576 bf16 values (512 latent + 64 rope), V = the 512 latent
+ * values, 64-token pages.
+ *
+ * Work: the plan's chunks (sequence, page range) are split evenly over
+ * n_workers; a worker is a cluster of two CTAs on two SMs that split the
+ * entry dimension: CTA r owns latent values [256r, 256r+256) and rope values
+ * [512+32r, 544+32r).  Per 64-token page ("tile"):
+ *   GEMM1  S_r = Q[:, own 288 dims] . KV[:, own 288 dims]^T  (M=128 heads,
+ *          N=64 tokens, K=288) -> TMEM, double-buffered;
+ *   the two partial S are exchanged through distributed shared memory and
+ *   added (a + b is the same float in both CTAs, so both run the identical
+ *   softmax on identical scores);
+ *   softmax in the log2 domain with a lazily updated row maximum (O is
+ *          rescaled only when a row's maximum grows by more than 2^8);
+ *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64) -> TMEM,
+ *          reading V in MN-major form from the same shared-memory page tile.
+ * Roles per CTA (192 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+ * issues the MMAs (one elected thread), warps 2-5 (thread = head row = TMEM
+ * lane) do the exchange, softmax and epilogue.
+ *
+ * Shared memory (per CTA): Q 72 KB (4 SW128 [128x64] boxes + 1 SW64 [128x32]),
+ * 2 page stages of 36 KB, 2 P buffers of 16 KB (SW128 K-major), the partial-S
+ * exchange buffer 32 KB, barriers.  TMEM: S at columns 0/64, O at 256..511.
+ *
+ * Every wait is bounded (about two seconds of clock); on expiry the kernel
+ * records an error word, drains its own TMA loads and MMAs, frees TMEM and
+ * returns.  No load uses cluster multicast, and no CTA reads another GPU's
+ * memory.
  */
 #include "../../include/attention.h"
 #include "../../include/hal.h"
 #include "../../include/kv_cache.h"
 #include "ct_internal.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace {
+
+constexpr int kH = 128, kE = 576, kDv = 512, kP = 64;
+constexpr int kThreads = 192;
+constexpr int kStages = 2;
+constexpr uint32_t kQBytes = 4 * 16384 + 8192;          /* 73,728 */
+constexpr uint32_t kKvBytes = 4 * 8192 + 4096;          /* 36,864 per stage */
+constexpr uint32_t kPBytes = 16384;
+constexpr uint32_t kXBytes = 32768;
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffKv = kOffQ + kQBytes;
+constexpr uint32_t kOffP = kOffKv + kStages * kKvBytes;
+constexpr uint32_t kOffX = kOffP + 2 * kPBytes;
+constexpr uint32_t kOffBar = kOffX + kXBytes;
+constexpr uint32_t kNumBars = 32;
+constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
+constexpr uint32_t kSmemUsed = kOffTmem + 16;
+constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;
+constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
+
+/* barrier slots */
+enum : uint32_t {
+    B_KV_FULL = 0, B_KV_EMPTY = 2, B_Q_FULL = 4, B_Q_EMPTY = 5, B_S_FULL = 6, B_S_EMPTY = 8, B_P_FULL = 10,
+    B_P_EMPTY = 12, B_O_READY = 14, B_O_FINAL = 15, B_O_FREE = 16, B_X_FULL = 17, B_X_EMPTY = 18, B_DRAIN = 19
+};
+
+/* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ int g_mla_tc_error;                          /* 0 = ok; else the code of the first failed wait */
+
+/* ---- PTX helpers ------------------------------------------------------- */
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; "
+                 "selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
+                 ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+/* 32 consecutive TMEM columns of this thread's lane -> registers. */
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    #pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+/* Shared-memory matrix descriptor (sm_100 format, version 1). */
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(lbo & 0x3FFFu) << 16) |
+           ((uint64_t)(sbo & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t kSw128 = 2, kSw64 = 4;
+
+/* ---- shared state of one CTA ------------------------------------------- */
+
+struct Ctx {
+    uint8_t *smem;          /* 1024-aligned base */
+    uint32_t s;             /* its shared address */
+    uint32_t peer;          /* the other CTA's rank */
+    volatile int *abort;    /* set by a thread whose wait expired */
+};
+
+__device__ __forceinline__ uint32_t bar(const Ctx &c, uint32_t i) { return c.s + kOffBar + 8 * i; }
+
+/* Bounded wait; returns false (and raises the abort flag) on expiry. */
+__device__ bool wait_bar(const Ctx &c, uint32_t b, uint32_t parity, bool cluster_scope, int code) {
+    long long t0 = clock64();
+    for (;;) {
+        if (cluster_scope ? mbar_try_cluster(b, parity) : mbar_try(b, parity)) return true;
+        if (*c.abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            atomicCAS(&g_mla_tc_error, 0, code);
+            *c.abort = 1;
+            return false;
+        }
+    }
+}
+
+/* The pages of a chunk that hold tokens: page lp of row `row` with page id
+ * pg >= 0 and ntok = min(64, len - 64*lp) > 0.  Every role walks the same list. */
+struct TileIter {
+    const int32_t *bt_row;
+    int32_t len, lp, end;
+    uint32_t n_pages;
+    __device__ bool next(int32_t &pg, int32_t &ntok) {
+        while (lp < end) {
+            const int32_t cur = lp++;
+            const int32_t n = min(kP, len - cur * kP);
+            const int32_t p = bt_row[cur];
+            if (n > 0 && p >= 0 && (uint32_t)p < n_pages) { pg = p; ntok = n; return true; }
+        }
+        return false;
+    }
+};
+
+__device__ __forceinline__ TileIter tiles_of(const ct_mla_chunk_t &ch, const int32_t *bt, uint32_t maxp,
+                                             const int32_t *lens, uint32_t n_pages) {
+    TileIter it;
+    it.n_pages = n_pages;
+    it.bt_row = bt + (size_t)ch.row * maxp;
+    it.len = lens[ch.row];
+    it.lp = ch.page_begin;
+    it.end = ch.page_end;
+    return it;
+}
+
+__device__ __forceinline__ int chunk_tiles(const ct_mla_chunk_t &ch, const int32_t *bt, uint32_t maxp,
+                                           const int32_t *lens, uint32_t n_pages) {
+    TileIter it = tiles_of(ch, bt, maxp, lens, n_pages);
+    int n = 0;
+    int32_t pg, nt;
+    while (it.next(pg, nt)) n++;
+    return n;
+}
+
+struct Params {
+    const ct_mla_chunk_t *chunks;
+    const int32_t *worker_begin;
+    const int32_t *bt;
+    const int32_t *lens;
+    uint16_t *out;
+    float *lse;
+    float *part_o;
+    float *part_ml;
+    uint32_t maxp;
+    uint32_t n_pages;
+    float qk_scale;          /* scale * log2(e) */
+};
+
+/* ---- warp 0: TMA producer ------------------------------------------------ */
+
+__device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_lat, const CUtensorMap *kv_rope,
+                         const CUtensorMap *q_lat, const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
+    uint32_t g = 0, nq = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = p.chunks[ci];
+        if (chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages) == 0) continue;
+        /* Q of this chunk's sequence, once the previous chunk's GEMM1s are done */
+        if (!wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1)) { ok = false; break; }
+        mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
+        const int qy = ch.seq * kH;
+        for (int b = 0; b < 4; b++) tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + b * 64, qy, bar(c, B_Q_FULL));
+        tma_load_2d(c.s + kOffQ + 4 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
+        nq++;
+        TileIter it = tiles_of(ch, p.bt, p.maxp, p.lens, p.n_pages);
+        int32_t pg, nt;
+        while (it.next(pg, nt)) {
+            const uint32_t st = g % kStages;
+            if (!wait_bar(c, bar(c, B_KV_EMPTY + st), ((g / kStages) & 1) ^ 1, false, 2)) { ok = false; break; }
+            mbar_expect_tx(bar(c, B_KV_FULL + st), kKvBytes);
+            const uint32_t dst = c.s + kOffKv + st * kKvBytes;
+            const int y = pg * kP;
+            for (int b = 0; b < 4; b++) tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, bar(c, B_KV_FULL + st));
+            tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, bar(c, B_KV_FULL + st));
+            g++;
+        }
+    }
+    /* Drain: every issued load must have landed before the CTA may exit. */
+    for (uint32_t k = 0; k < kStages && k < g; k++) {
+        const uint32_t last = g - 1 - k;
+        const uint32_t st = last % kStages;
+        long long t0 = clock64();
+        while (!mbar_try(bar(c, B_KV_FULL + st), (last / kStages) & 1) && clock64() - t0 < kWaitCycles) {}
+    }
+    if (nq) {
+        long long t0 = clock64();
+        while (!mbar_try(bar(c, B_Q_FULL), (nq - 1) & 1) && clock64() - t0 < kWaitCycles) {}
+    }
+}
+
+/* ---- warp 1 (one thread): MMA issuer ------------------------------------ */
+
+__device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf) {
+    const uint32_t q = c.s + kOffQ, kv = c.s + kOffKv + st * kKvBytes;
+    const uint32_t d = tmem + sbuf * 64;
+    uint32_t acc = 0;
+    #pragma unroll
+    for (int b = 0; b < 4; b++)
+        #pragma unroll
+        for (int k = 0; k < 4; k++) {
+            mma_bf16(d, sdesc(q + b * 16384 + k * 32, 1, 64, kSw128), sdesc(kv + b * 8192 + k * 32, 1, 64, kSw128),
+                     kIdescS, acc);
+            acc = 1;
+        }
+    #pragma unroll
+    for (int k = 0; k < 2; k++)
+        mma_bf16(d, sdesc(q + 4 * 16384 + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64),
+                 kIdescS, 1);
+}
+
+__device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t pbuf, bool first) {
+    const uint32_t pa = c.s + kOffP + pbuf * kPBytes, v = c.s + kOffKv + st * kKvBytes;
+    #pragma unroll
+    for (int k = 0; k < 4; k++)
+        mma_bf16(tmem + kTmemO, sdesc(pa + k * 32, 1, 64, kSw128), sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
+                 (first && k == 0) ? 0u : 1u);
+}
+
+__device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    uint32_t g = 0, nchunk = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = p.chunks[ci];
+        const int nt = chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages);
+        if (nt == 0) continue;
+        if (!wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3)) { ok = false; break; }
+        tc_fence_after();
+        for (int j = 0; j <= nt && ok; j++) {
+            if (j < nt) {                                   /* GEMM1 of tile j */
+                const uint32_t gj = g + j;
+                const uint32_t st = gj % kStages, sb = gj & 1;
+                if (!wait_bar(c, bar(c, B_KV_FULL + st), (gj / kStages) & 1, false, 5)) { ok = false; break; }
+                if (!wait_bar(c, bar(c, B_S_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 6)) { ok = false; break; }
+                tc_fence_after();
+                issue_gemm1(c, tmem, st, sb);
+                mma_commit(bar(c, B_S_FULL + sb));
+                if (j == nt - 1) mma_commit(bar(c, B_Q_EMPTY));
+            }
+            if (j >= 1) {                                   /* GEMM2 of tile j-1 */
+                const uint32_t gj = g + j - 1;
+                const uint32_t st = gj % kStages, pb = gj & 1;
+                if (!wait_bar(c, bar(c, B_P_FULL + pb), (gj >> 1) & 1, false, 7)) { ok = false; break; }
+                /* the first GEMM2 overwrites O: the previous chunk's epilogue must have read it */
+                if (j == 1 && !wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 4)) { ok = false; break; }
+                tc_fence_after();
+                issue_gemm2(c, tmem, st, pb, j == 1);
+                mma_commit(bar(c, B_KV_EMPTY + st));
+                mma_commit(bar(c, B_P_EMPTY + pb));
+                mma_commit(bar(c, B_O_READY));
+                if (j == nt) mma_commit(bar(c, B_O_FINAL));
+            }
+        }
+        g += nt;
+        nchunk++;
+    }
+    /* Drain the tensor pipe before TMEM is released. */
+    mma_commit(bar(c, B_DRAIN));
+    long long t0 = clock64();
+    while (!mbar_try(bar(c, B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {}
+}
+
+/* ---- warps 2-5: exchange, softmax, epilogue ------------------------------- */
+
+/* A wait all 32 lanes of a softmax warp leave together (the tcgen05 loads
+ * and stores that follow are warp-collective). */
+__device__ __forceinline__ bool wait_warp(const Ctx &c, uint32_t b, uint32_t parity, bool cluster_scope, int code) {
+    const bool r = wait_bar(c, b, parity, cluster_scope, code);
+    return __all_sync(0xFFFFFFFFu, r);
+}
+
+/* Swizzled position of 16-byte chunk `c` (0..15) of exchange row `row`. */
+__device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
+
+__device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t quad = warp & 3;                     /* TMEM lane quadrant this warp may access */
+    const uint32_t row = quad * 32 + lane;              /* head */
+    const uint32_t lane_base = (quad * 32) << 16;
+    const uint32_t x_mine = c.s + kOffX;
+    const uint32_t x_peer = mapa(x_mine, c.peer);
+    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
+    const uint32_t xe_peer = mapa(bar(c, B_X_EMPTY), c.peer);
+    uint32_t g = 0, nchunk = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = p.chunks[ci];
+        const int nt = chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages);
+        float m_used = -INFINITY, l = 0.0f;
+        if (nt > 0) {
+            TileIter it = tiles_of(ch, p.bt, p.maxp, p.lens, p.n_pages);
+            for (int j = 0; j < nt && ok; j++) {
+                int32_t pg, ntok;
+                it.next(pg, ntok);
+                const uint32_t gj = g + j, sb = gj & 1, st = gj % kStages;
+                /* scores of this CTA's half */
+                if (!wait_warp(c, bar(c, B_S_FULL + sb), (gj >> 1) & 1, false, 8)) { ok = false; break; }
+                tc_fence_after();
+                float s[64];
+                tmem_ld32(tmem + lane_base + sb * 64, s);
+                tmem_ld32(tmem + lane_base + sb * 64 + 32, s + 32);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(bar(c, B_S_EMPTY + sb));
+                /* exchange with the other CTA: send mine, receive theirs */
+                if (!wait_warp(c, bar(c, B_X_EMPTY), (gj & 1) ^ 1, true, 9)) { ok = false; break; }
+                #pragma unroll
+                for (int q4 = 0; q4 < 16; q4++)
+                    st_cluster_v4(x_peer + xoff(row, q4), s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
+                mbar_arrive_remote(xf_peer);
+                if (!wait_warp(c, bar(c, B_X_FULL), gj & 1, true, 10)) { ok = false; break; }
+                const float4 *xr = reinterpret_cast<const float4 *>(c.smem + kOffX);
+                #pragma unroll
+                for (int q4 = 0; q4 < 16; q4++) {
+                    const float4 w = xr[xoff(row, q4) >> 4];
+                    s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
+                }
+                mbar_arrive_remote(xe_peer);
+                /* scaled scores, masked beyond the page's tokens */
+                float mx = -INFINITY;
+                #pragma unroll
+                for (int i = 0; i < 64; i++) {
+                    s[i] = (i < ntok) ? s[i] * p.qk_scale : -INFINITY;
+                    mx = fmaxf(mx, s[i]);
+                }
+                const bool grow = mx > m_used + kRescaleThreshold;   /* also true for the first tile */
+                const float m_new = grow ? mx : m_used;
+                const float alpha = exp2f(m_used - m_new);           /* 0 on the first tile, 1 if unchanged */
+                if (__any_sync(0xFFFFFFFFu, grow && j > 0)) {
+                    /* O holds tiles < j: wait for GEMM2(j-1), rescale this warp's rows */
+                    if (!wait_warp(c, bar(c, B_O_READY), (gj - 1) & 1, false, 11)) { ok = false; break; }
+                    tc_fence_after();
+                    const float a = grow ? alpha : 1.0f;
+                    #pragma unroll 1
+                    for (int cc = 0; cc < 8; cc++) {
+                        float o[32];
+                        tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
+                        tmem_wait_ld();
+                        #pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] *= a;
+                        tmem_st32(tmem + lane_base + kTmemO + cc * 32, o);
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                }
+                l *= alpha;
+                m_used = m_new;
+                /* P = bf16(2^(s - m)), row-wise into the SW128 K-major P buffer */
+                if (!wait_warp(c, bar(c, B_P_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 12)) { ok = false; break; }
+                uint8_t *pbuf = c.smem + kOffP + sb * kPBytes;
+                #pragma unroll
+                for (int ch16 = 0; ch16 < 8; ch16++) {
+                    uint32_t w[4];
+                    #pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint16_t lo = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k] - m_used));
+                        const uint16_t hi = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k + 1] - m_used));
+                        l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
+                        w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+                    }
+                    *reinterpret_cast<uint4 *>(pbuf + row * 128 + ((ch16 ^ (row & 7)) << 4)) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
+                if (ntok < kP) {
+                    uint8_t *kvs = c.smem + kOffKv + st * kKvBytes;
+                    const uint32_t tid = threadIdx.x - 64;
+                    const uint32_t n16 = (uint32_t)(kP - ntok) * 4 * 8;      /* 16-B words in 4 blocks */
+                    for (uint32_t i = tid; i < n16; i += 128) {
+                        const uint32_t blk = i / ((kP - ntok) * 8), rem = i % ((kP - ntok) * 8);
+                        const uint32_t r = ntok + rem / 8, w16 = rem % 8;
+                        *reinterpret_cast<uint4 *>(kvs + blk * 8192 + r * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                proxy_fence();
+                mbar_arrive(bar(c, B_P_FULL + sb));
+            }
+            if (!ok) break;
+            g += nt;
+            /* epilogue: O rows of this CTA's 256 value dims */
+            if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
+            tc_fence_after();
+            const size_t oh = (size_t)ch.seq * kH + row;
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            #pragma unroll 1
+            for (int cc = 0; cc < 8; cc++) {
+                float o[32];
+                tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
+                tmem_wait_ld();
+                const uint32_t d0 = rank * 256 + cc * 32;
+                if (ch.part < 0) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d0);
+                    #pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        uint32_t w[4];
+                        #pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            w[e] = (uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e] * inv) |
+                                   ((uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e + 1] * inv) << 16);
+                        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+                    float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + row) * kDv + d0);
+                    #pragma unroll
+                    for (int k = 0; k < 8; k++) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(bar(c, B_O_FREE));
+            nchunk++;
+        }
+        /* outputs and statistics that only one CTA writes */
+        if (rank == 0) {
+            const size_t oh = (size_t)ch.seq * kH + row;
+            if (ch.part < 0) {
+                if (p.lse) p.lse[oh] = l > 0.0f ? m_used * kLn2 + logf(l) : -INFINITY;
+            } else {
+                p.part_ml[2 * ((size_t)ch.part * kH + row)] = m_used;
+                p.part_ml[2 * ((size_t)ch.part * kH + row) + 1] = l;
+            }
+        }
+        if (nt == 0 && ch.part < 0) {               /* nothing readable: zero output */
+            uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)ch.seq * kH + row) * kDv + rank * 256);
+            for (int k = 0; k < 32; k++) dst[k] = make_uint4(0, 0, 0, 0);
+        } else if (nt == 0) {
+            float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + row) * kDv + rank * 256);
+            for (int k = 0; k < 64; k++) dst[k] = make_float4(0, 0, 0, 0);
+        }
+    }
+}
+
+/* ---- the kernel ----------------------------------------------------------- */
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_mla_tc(const __grid_constant__ CUtensorMap kv_lat, const __grid_constant__ CUtensorMap kv_rope,
+             const __grid_constant__ CUtensorMap q_lat, const __grid_constant__ CUtensorMap q_rope, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_abort;
+    const uint32_t raw = smem_addr(smem_raw);
+    const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+    Ctx c;
+    c.smem = smem_raw + pad;
+    c.s = raw + pad;
+    const uint32_t rank = cluster_rank();
+    c.peer = rank ^ 1u;
+    c.abort = &s_abort;
+    const uint32_t warp = threadIdx.x >> 5;
+    const int w = blockIdx.x >> 1;
+    const int wbeg = p.worker_begin[w], wend = p.worker_begin[w + 1];
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        mbar_init(bar(c, B_KV_FULL + 0), 1); mbar_init(bar(c, B_KV_FULL + 1), 1);
+        mbar_init(bar(c, B_KV_EMPTY + 0), 1); mbar_init(bar(c, B_KV_EMPTY + 1), 1);
+        mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1);
+        mbar_init(bar(c, B_S_FULL + 0), 1); mbar_init(bar(c, B_S_FULL + 1), 1);
+        mbar_init(bar(c, B_S_EMPTY + 0), 128); mbar_init(bar(c, B_S_EMPTY + 1), 128);
+        mbar_init(bar(c, B_P_FULL + 0), 128); mbar_init(bar(c, B_P_FULL + 1), 128);
+        mbar_init(bar(c, B_P_EMPTY + 0), 1); mbar_init(bar(c, B_P_EMPTY + 1), 1);
+        mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1); mbar_init(bar(c, B_O_FREE), 128);
+        mbar_init(bar(c, B_X_FULL), 128); mbar_init(bar(c, B_X_EMPTY), 128);
+        mbar_init(bar(c, B_DRAIN), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(c.s + kOffTmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                                 /* both CTAs' barriers exist before any remote arrive */
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
+
+    if (warp == 0) {
+        if ((threadIdx.x & 31) == 0) producer(c, p, &kv_lat, &kv_rope, &q_lat, &q_rope, wbeg, wend, rank);
+    } else if (warp == 1) {
+        if ((threadIdx.x & 31) == 0) mma_issuer(c, p, tmem, wbeg, wend);
+    } else {
+        softmax_warps(c, p, tmem, wbeg, wend, rank);
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    cluster_sync();                                 /* no CTA leaves while its peer may still write its smem */
+}
+
+/* ---- host side ------------------------------------------------------------ */
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+/* 2-D bf16 map over [rows][576] with a (box_cols x box_rows) box. */
+bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+              CUtensorMapSwizzle sw) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)kE, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kE * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool shape_ok(const ct_mla_dims_t *d) {
+    return d->n_heads == (uint32_t)kH && d->entry_dim == (uint32_t)kE && d->v_dim == (uint32_t)kDv &&
+           d->page_tokens == (uint32_t)kP && d->kv_dtype == CT_KV_BF16;
+}
+
+}  // namespace
+
 extern "C" int ct__mla_tc_workers(const ct_mla_dims_t *dims, int device) {
-    (void)dims; (void)device;
-    return 0;
+    if (!dims || !shape_ok(dims)) return 0;
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (major != 10 || minor != 0 || !encode_fn()) return 0;
+    /* One worker per co-resident cluster, so every worker runs in one wave. */
+    static int cached[64];
+    if (device < 0 || device >= 64) return 0;
+    if (cached[device] == 0) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        int n = 0;
+        if (cudaFuncSetAttribute(k_mla_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc) ==
+            cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = kSmemAlloc;
+            if (cudaOccupancyMaxActiveClusters(&n, (void *)k_mla_tc, &cfg) != cudaSuccess) n = 0;
+        }
+        cudaGetLastError();
+        cudaSetDevice(prev);
+        cached[device] = n > 0 ? n : -1;
+    }
+    return cached[device] > 0 ? cached[device] : 0;
+}
+
+/* Error word of the tensor-core kernel (0 = no wait expired), for tests. */
+extern "C" int ct_mla_tc_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_mla_tc_error, sizeof v) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (clear && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_mla_tc_error, &z, sizeof z);
+    }
+    return v;
 }
 
 extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks, uint32_t n_chunks,
                                  const int32_t *worker_begin, uint32_t n_workers, const void *q,
                                  const void *pool, const int32_t *block_table, const int32_t *seq_lens,
                                  void *out, float *lse, float *part_o, float *part_ml, void *stream) {
-    (void)dims; (void)chunks; (void)n_chunks; (void)worker_begin; (void)n_workers; (void)q; (void)pool;
-    (void)block_table; (void)seq_lens; (void)out; (void)lse; (void)part_o; (void)part_ml; (void)stream;
-    return CT_ERR_UNSUPPORTED;
+    (void)n_chunks;
+    if (!shape_ok(dims)) return CT_ERR_UNSUPPORTED;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (ct__mla_tc_workers(dims, dev) <= 0 || n_workers == 0) return CT_ERR_UNSUPPORTED;
+    if (((uintptr_t)pool & 15u) || ((uintptr_t)q & 15u) || ((uintptr_t)out & 15u)) return CT_ERR_UNSUPPORTED;
+    /* Rows of the pool map: pages are addressed by the block table; the map
+     * covers up to the largest page id the tables can hold (2^31 / 64). */
+    /* Maps cover exactly the pool and q: a page id beyond the pool reads
+     * zeros (TMA out-of-bounds fill) rather than foreign memory. */
+    CUtensorMap kv_lat, kv_rope, q_lat, q_rope;
+    if (dims->n_pages == 0 || dims->n_seq == 0) return CT_ERR_ARG;
+    const uint64_t pool_rows = (uint64_t)dims->n_pages * kP;
+    const uint64_t q_rows = (uint64_t)dims->n_seq * kH;
+    if (!make_map(&kv_lat, pool, pool_rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&kv_rope, pool, pool_rows, 32, 64, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&q_lat, q, q_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&q_rope, q, q_rows, 32, 128, CU_TENSOR_MAP_SWIZZLE_64B)) {
+        ct__set_error("mla_tc: cuTensorMapEncodeTiled failed");
+        return CT_ERR_CUDA;
+    }
+    Params p;
+    p.chunks = chunks;
+    p.worker_begin = worker_begin;
+    p.bt = block_table;
+    p.lens = seq_lens;
+    p.out = static_cast<uint16_t *>(out);
+    p.lse = lse;
+    p.part_o = part_o;
+    p.part_ml = part_ml;
+    p.maxp = dims->max_pages_per_seq;
+    p.n_pages = dims->n_pages;
+    p.qk_scale = dims->scale * kLog2e;
+    static bool attr_set = false;
+    if (!attr_set) {
+        int rc = ct__cuda_status(cudaFuncSetAttribute(k_mla_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      (int)kSmemAlloc), "mla_tc attribute");
+        if (rc) return rc;
+        attr_set = true;
+    }
+    k_mla_tc<<<2 * n_workers, kThreads, kSmemAlloc, (cudaStream_t)stream>>>(kv_lat, kv_rope, q_lat, q_rope, p);
+    return ct__cuda_status(cudaGetLastError(), "mla_tc launch");
 }

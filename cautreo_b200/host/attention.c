@@ -72,6 +72,7 @@ struct ct_mla_plan {
     ct_mla_dims_t dims;
     uint32_t n_seq, n_workers, n_chunks, n_combines, n_parts;
     int device;
+    int tensor_cores;
     ct_mla_chunk_t *chunks;      /* device [n_chunks], worker-major */
     int32_t *worker_begin;       /* device [n_workers + 1] */
     ct_mla_combine_t *combines;  /* device [n_combines] */
@@ -96,7 +97,7 @@ void ct_mla_plan_destroy(ct_mla_plan_t *p) {
 ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *seq_rows,
                                   const int32_t *seq_lens, uint32_t n_seq, int device) {
     if (!shape || !seq_lens || shape->n_heads == 0 || shape->page_tokens == 0 || shape->v_dim > shape->entry_dim ||
-        shape->entry_dim == 0 || shape->max_pages_per_seq == 0) {
+        shape->entry_dim == 0 || shape->max_pages_per_seq == 0 || shape->n_pages == 0) {
         ct__set_error("ct_mla_plan_create: bad shape");
         return NULL;
     }
@@ -109,6 +110,8 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
     p->dims.max_pages_per_seq = shape->max_pages_per_seq;
     p->dims.kv_dtype = shape->kv_dtype;
     p->dims.scale = shape->scale;
+    p->dims.n_pages = shape->n_pages;
+    p->dims.n_seq = n_seq;
     p->n_seq = n_seq;
     p->device = device;
     const uint32_t P = shape->page_tokens;
@@ -120,6 +123,7 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
     }
     int tc_workers = ct__mla_tc_workers(&p->dims, device);
     p->n_workers = tc_workers > 0 ? (uint32_t)tc_workers : (uint32_t)n_sms;
+    p->tensor_cores = tc_workers > 0;
 
     /* Token quota per worker; cuts fall on page boundaries. */
     uint64_t total = 0;
@@ -209,6 +213,8 @@ fail:
 uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p) { return p ? p->n_chunks : 0; }
 size_t ct_mla_plan_scratch_bytes(const ct_mla_plan_t *p) { return p ? p->scratch_bytes : 0; }
 uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p) { return p ? p->last_launches : 0; }
+uint32_t ct_mla_plan_workers(const ct_mla_plan_t *p) { return p ? p->n_workers : 0; }
+int ct_mla_plan_tensor_cores(const ct_mla_plan_t *p) { return p ? p->tensor_cores : 0; }
 
 int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const void *pool, const float *scales,
                              const int32_t *block_table, const int32_t *seq_lens, void *out, float *lse,

@@ -76,6 +76,7 @@ typedef struct {
     uint32_t max_pages_per_seq;
     uint32_t kv_dtype;       /* ct_kv_dtype_t of the pool */
     float    scale;          /* softmax scale, e.g. 1/sqrt(192) */
+    uint32_t n_pages;        /* pages in the pool; block-table entries >= n_pages are skipped */
 } ct_mla_shape_t;
 
 /* A work plan: the split of every sequence's pages into chunks, the chunk
@@ -91,6 +92,11 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
 void   ct_mla_plan_destroy(ct_mla_plan_t *p);
 /* Number of work chunks and the split-KV scratch bytes the plan holds. */
 uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p);
+/* Workers the plan balances over, and whether it runs the tensor-core kernel
+ * (1: 128 heads x 576 bf16 entries x 64-token pages on sm_100; 0: the
+ * CUDA-core kernel for every other shape). */
+uint32_t ct_mla_plan_workers(const ct_mla_plan_t *p);
+int      ct_mla_plan_tensor_cores(const ct_mla_plan_t *p);
 size_t   ct_mla_plan_scratch_bytes(const ct_mla_plan_t *p);
 
 /* out[s][h][0:v_dim] = sum_t softmax_t(scale * q[s][h] . e_t) * e_t[0:v_dim]
@@ -105,6 +111,12 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
 
 /* Number of kernel launches the last ct_attn_mla_decode_paged issued. */
 uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p);
+
+/* Error word of the tensor-core MLA kernel on the current device: 0 when no
+ * bounded wait expired, else the code of the first wait that did (the kernel
+ * then returned early and its outputs are invalid).  clear != 0 resets it.
+ * Reading it synchronises with the device.  -1 if it cannot be read. */
+int ct_mla_tc_error(int clear);
 
 /* One serving step with host I/O, for callers that keep inputs and outputs
  * in host memory: copies q_host ([n_seq][n_heads][entry_dim] bf16) and

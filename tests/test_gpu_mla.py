@@ -18,10 +18,18 @@ GOLD = Path(__file__).resolve().parent / "golden"
 O = oracle.port()
 
 
+@pytest.fixture(autouse=True)
+def no_expired_waits():
+    """Every test leaves the tensor-core kernel's error word at 0."""
+    ct.lib().ct_mla_tc_error(1)
+    yield
+    assert ct.lib().ct_mla_tc_error(1) == 0
+
+
 def run_decode(pool, bt, lens, q, H=MLA_H, E=MLA_E, Dv=MLA_DV, P=PAGE, dtype=ct.CT_KV_BF16, scales=None,
                want_lse=False):
     lens = np.asarray(lens, np.int32)
-    plan = ct.MlaPlan(lens, n_heads=H, entry_dim=E, v_dim=Dv, page_tokens=P, max_pages_per_seq=bt.shape[1],
+    plan = ct.MlaPlan(lens, pool.shape[0], n_heads=H, entry_dim=E, v_dim=Dv, page_tokens=P, max_pages_per_seq=bt.shape[1],
                       kv_dtype=dtype, scale=MLA_SCALE)
     out = empty((len(lens), H, Dv), np.uint16)
     lse = empty((len(lens), H), np.float32) if want_lse else None
@@ -53,6 +61,7 @@ def test_mla_small_cases(lens):
     before = ct.launch_count()
     got, plan = run_decode(pool, bt, lens, q)
     assert ct.launch_count() > before
+    assert plan.tensor_cores and plan.workers >= 64        # the tcgen05 kernel ran
     want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
     ok, mx, rel = close(got, want)
     assert ok, (mx, rel)
@@ -68,7 +77,8 @@ def test_mla_matches_reference_golden_16_heads():
     lens = g["lens"]
     H = int(g["heads"])
     pool, bt, q = mla_case(lens, seed=1, H=H)
-    got, _ = run_decode(pool, bt, lens, q, H=H)
+    got, plan = run_decode(pool, bt, lens, q, H=H)
+    assert not plan.tensor_cores
     ok, mx, rel = close(got, g["out"])
     assert ok, (mx, rel)
 
@@ -81,13 +91,15 @@ def test_mla_lse_and_splits():
     want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
     ok, mx, rel = close(got, want)
     assert ok, (mx, rel)
-    # log-sum-exp of the scaled scores, from the oracle's fp64 scores
+    # log-sum-exp of the scaled scores, from the oracle's fp64 scores.  The
+    # kernels sum the probabilities as rounded to bf16 for the P.V product
+    # (so the normaliser matches the weights actually applied): a few 1e-4.
     for s, n in enumerate(lens):
         kv = np.stack([oracle.bf16_to_f32(pool[bt[s, t // PAGE], t % PAGE]) for t in range(n)]).astype(np.float64)
         sc = (oracle.bf16_to_f32(q[s]).astype(np.float64) @ kv.T) * MLA_SCALE
         m = sc.max(axis=1)
         ref = m + np.log(np.exp(sc - m[:, None]).sum(axis=1))
-        np.testing.assert_allclose(lse[s], ref, rtol=1e-4, atol=1e-3)
+        np.testing.assert_allclose(lse[s], ref, rtol=0, atol=5e-3)
 
 
 def test_mla_evicted_pages_are_skipped():
@@ -182,7 +194,7 @@ def test_mla_through_paged_handle():
     xd = dev(x)
     h.append(list(range(S)), lens, xd.data_ptr(), ct.CT_KV_BF16)
     q = oracle.normal_bf16(oracle.key(6, 5), 0, S * MLA_H * E).reshape(S, MLA_H, E)
-    plan = ct.MlaPlan(lens, max_pages_per_seq=8)
+    plan = ct.MlaPlan(lens, 20, max_pages_per_seq=8)
     out = empty((S, MLA_H, MLA_DV), np.uint16)
     qd = dev(q)
     plan.decode(qd.data_ptr(), h.pool, None, h.block_table_dev, h.seq_lens_dev, out.data_ptr(), None, stream())
