@@ -62,6 +62,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;
 constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
+constexpr int kPrefetchAhead = 6;                       /* pages pulled into L2 ahead of their TMA load */
+constexpr uint32_t kPageBytes = kP * kE * 2;            /* 73,728 */
 
 /* barrier slots */
 enum : uint32_t {
@@ -108,10 +110,6 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
 }
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -204,43 +202,11 @@ __device__ bool wait_bar(const Ctx &c, uint32_t b, uint32_t parity, bool cluster
     }
 }
 
-/* The pages of a chunk that hold tokens: page lp of row `row` with page id
- * pg >= 0 and ntok = min(64, len - 64*lp) > 0.  Every role walks the same list. */
-struct TileIter {
-    const int32_t *bt_row;
-    int32_t len, lp, end;
-    uint32_t n_pages;
-    __device__ bool next(int32_t &pg, int32_t &ntok) {
-        while (lp < end) {
-            const int32_t cur = lp++;
-            const int32_t n = min(kP, len - cur * kP);
-            const int32_t p = bt_row[cur];
-            if (n > 0 && p >= 0 && (uint32_t)p < n_pages) { pg = p; ntok = n; return true; }
-        }
-        return false;
-    }
-};
-
-__device__ __forceinline__ TileIter tiles_of(const ct_mla_chunk_t &ch, const int32_t *bt, uint32_t maxp,
-                                             const int32_t *lens, uint32_t n_pages) {
-    TileIter it;
-    it.n_pages = n_pages;
-    it.bt_row = bt + (size_t)ch.row * maxp;
-    it.len = lens[ch.row];
-    it.lp = ch.page_begin;
-    it.end = ch.page_end;
-    return it;
-}
-
-__device__ __forceinline__ int chunk_tiles(const ct_mla_chunk_t &ch, const int32_t *bt, uint32_t maxp,
-                                           const int32_t *lens, uint32_t n_pages) {
-    TileIter it = tiles_of(ch, bt, maxp, lens, n_pages);
-    int n = 0;
-    int32_t pg, nt;
-    while (it.next(pg, nt)) n++;
-    return n;
-}
-
+/* Warp-cooperative walk over the pages of a chunk that hold tokens: lanes
+ * read 32 consecutive block-table entries with one coalesced load, a ballot
+ * marks the usable pages (page id in [0, n_pages), at least one token), and
+ * next() hands them out in order.  All 32 lanes call it together; every
+ * role walks the same list. */
 struct Params {
     const ct_mla_chunk_t *chunks;
     const int32_t *worker_begin;
@@ -250,40 +216,122 @@ struct Params {
     float *lse;
     float *part_o;
     float *part_ml;
+    const uint8_t *pool;
     uint32_t maxp;
     uint32_t n_pages;
     float qk_scale;          /* scale * log2(e) */
 };
 
-/* ---- warp 0: TMA producer ------------------------------------------------ */
+struct WarpTiles {
+    const int32_t *bt_row;
+    int32_t len, next_lp, end, base, my_pg;
+    uint32_t n_pages, mask;
+    __device__ __forceinline__ void init(const ct_mla_chunk_t &ch, const Params &p) {
+        bt_row = p.bt + (size_t)ch.row * p.maxp;
+        len = p.lens[ch.row];
+        next_lp = ch.page_begin;
+        end = ch.page_end;
+        n_pages = p.n_pages;
+        mask = 0;
+        base = 0;
+        my_pg = -1;
+    }
+    __device__ __forceinline__ bool next(int32_t &pg, int32_t &ntok) {
+        const int32_t lane = (int32_t)(threadIdx.x & 31);
+        while (mask == 0) {
+            if (next_lp >= end) return false;
+            base = next_lp;
+            const int32_t cur = base + lane;
+            int32_t v = -1, n = 0;
+            if (cur < end) {
+                v = __ldg(bt_row + cur);
+                n = min(kP, len - cur * kP);
+            }
+            my_pg = v;
+            mask = __ballot_sync(0xFFFFFFFFu, cur < end && n > 0 && v >= 0 && (uint32_t)v < n_pages);
+            next_lp = base + 32;
+        }
+        const int i = __ffs(mask) - 1;
+        mask &= mask - 1;
+        pg = __shfl_sync(0xFFFFFFFFu, my_pg, i);
+        ntok = min(kP, len - (base + i) * kP);
+        return true;
+    }
+};
+
+__device__ __forceinline__ ct_mla_chunk_t load_chunk(const Params &p, int ci) {
+    const int4 *src = reinterpret_cast<const int4 *>(p.chunks + ci);
+    const int4 a = __ldg(src), b = __ldg(src + 1);
+    ct_mla_chunk_t ch;
+    ch.seq = a.x; ch.row = a.y; ch.page_begin = a.z; ch.page_end = a.w;
+    ch.part = b.x; ch.pad[0] = b.y; ch.pad[1] = b.z; ch.pad[2] = b.w;
+    return ch;
+}
+
+/* ---- warp 0: TMA producer (lane 0 issues) -------------------------------- */
 
 __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_lat, const CUtensorMap *kv_rope,
                          const CUtensorMap *q_lat, const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
+    const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nq = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
-        const ct_mla_chunk_t ch = p.chunks[ci];
-        if (chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages) == 0) continue;
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        WarpTiles it;
+        it.init(ch, p);
+        int32_t pg, ntok;
+        if (!it.next(pg, ntok)) continue;               /* nothing readable in this chunk */
         /* Q of this chunk's sequence, once the previous chunk's GEMM1s are done */
-        if (!wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1)) { ok = false; break; }
-        mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
-        const int qy = ch.seq * kH;
-        for (int b = 0; b < 4; b++) tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + b * 64, qy, bar(c, B_Q_FULL));
-        tma_load_2d(c.s + kOffQ + 4 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
-        nq++;
-        TileIter it = tiles_of(ch, p.bt, p.maxp, p.lens, p.n_pages);
-        int32_t pg, nt;
-        while (it.next(pg, nt)) {
-            const uint32_t st = g % kStages;
-            if (!wait_bar(c, bar(c, B_KV_EMPTY + st), ((g / kStages) & 1) ^ 1, false, 2)) { ok = false; break; }
-            mbar_expect_tx(bar(c, B_KV_FULL + st), kKvBytes);
-            const uint32_t dst = c.s + kOffKv + st * kKvBytes;
-            const int y = pg * kP;
-            for (int b = 0; b < 4; b++) tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, bar(c, B_KV_FULL + st));
-            tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, bar(c, B_KV_FULL + st));
-            g++;
+        if (leader) {
+            ok = wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1);
+            if (ok) {
+                mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
+                const int qy = ch.seq * kH;
+                for (int b = 0; b < 4; b++)
+                    tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + b * 64, qy, bar(c, B_Q_FULL));
+                tma_load_2d(c.s + kOffQ + 4 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
+            }
         }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        if (!ok) break;
+        nq++;
+        /* a second walk runs kPrefetchAhead pages ahead and pulls whole pages
+         * (both CTAs' halves) into L2, so the TMA loads below hit L2 */
+        WarpTiles pre = it;
+        int32_t ppg, pnt;
+        bool pre_ok = true;
+        const bool prefetcher = leader && rank == 0;
+        for (int k = 0; k < kPrefetchAhead && pre_ok; k++) {
+            if (k == 0) { ppg = pg; pnt = ntok; } else pre_ok = pre.next(ppg, pnt);
+            if (pre_ok && prefetcher)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                             ::"l"(p.pool + (size_t)ppg * kPageBytes), "r"(kPageBytes) : "memory");
+        }
+        do {
+            if (pre_ok) {
+                pre_ok = pre.next(ppg, pnt);
+                if (pre_ok && prefetcher)
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                                 ::"l"(p.pool + (size_t)ppg * kPageBytes), "r"(kPageBytes) : "memory");
+            }
+            const uint32_t st = g % kStages;
+            if (leader) {
+                ok = wait_bar(c, bar(c, B_KV_EMPTY + st), ((g / kStages) & 1) ^ 1, false, 2);
+                if (ok) {
+                    mbar_expect_tx(bar(c, B_KV_FULL + st), kKvBytes);
+                    const uint32_t dst = c.s + kOffKv + st * kKvBytes;
+                    const int y = pg * kP;
+                    for (int b = 0; b < 4; b++)
+                        tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, bar(c, B_KV_FULL + st));
+                    tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, bar(c, B_KV_FULL + st));
+                }
+            }
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            if (!ok) break;
+            g++;
+        } while (it.next(pg, ntok));
     }
+    if (!leader) return;
     /* Drain: every issued load must have landed before the CTA may exit. */
     for (uint32_t k = 0; k < kStages && k < g; k++) {
         const uint32_t last = g - 1 - k;
@@ -297,7 +345,7 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
     }
 }
 
-/* ---- warp 1 (one thread): MMA issuer ------------------------------------ */
+/* ---- warp 1: MMA issuer (lane 0 issues) ---------------------------------- */
 
 __device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf) {
     const uint32_t q = c.s + kOffQ, kv = c.s + kOffKv + st * kKvBytes;
@@ -325,43 +373,65 @@ __device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t p
                  (first && k == 0) ? 0u : 1u);
 }
 
+/* GEMM2 of global tile gj (the j-th of its chunk), with its releases. */
+__device__ bool mma_gemm2(const Ctx &c, uint32_t tmem, uint32_t gj, bool first, uint32_t nchunk) {
+    const uint32_t st = gj % kStages, pb = gj & 1;
+    if (!wait_bar(c, bar(c, B_P_FULL + pb), (gj >> 1) & 1, false, 7)) return false;
+    /* the first GEMM2 of a chunk overwrites O: the previous epilogue must have read it */
+    if (first && !wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 4)) return false;
+    tc_fence_after();
+    issue_gemm2(c, tmem, st, pb, first);
+    mma_commit(bar(c, B_KV_EMPTY + st));
+    mma_commit(bar(c, B_P_EMPTY + pb));
+    mma_commit(bar(c, B_O_READY));
+    return true;
+}
+
 __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nchunk = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
-        const ct_mla_chunk_t ch = p.chunks[ci];
-        const int nt = chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages);
-        if (nt == 0) continue;
-        if (!wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3)) { ok = false; break; }
-        tc_fence_after();
-        for (int j = 0; j <= nt && ok; j++) {
-            if (j < nt) {                                   /* GEMM1 of tile j */
-                const uint32_t gj = g + j;
-                const uint32_t st = gj % kStages, sb = gj & 1;
-                if (!wait_bar(c, bar(c, B_KV_FULL + st), (gj / kStages) & 1, false, 5)) { ok = false; break; }
-                if (!wait_bar(c, bar(c, B_S_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 6)) { ok = false; break; }
-                tc_fence_after();
-                issue_gemm1(c, tmem, st, sb);
-                mma_commit(bar(c, B_S_FULL + sb));
-                if (j == nt - 1) mma_commit(bar(c, B_Q_EMPTY));
-            }
-            if (j >= 1) {                                   /* GEMM2 of tile j-1 */
-                const uint32_t gj = g + j - 1;
-                const uint32_t st = gj % kStages, pb = gj & 1;
-                if (!wait_bar(c, bar(c, B_P_FULL + pb), (gj >> 1) & 1, false, 7)) { ok = false; break; }
-                /* the first GEMM2 overwrites O: the previous chunk's epilogue must have read it */
-                if (j == 1 && !wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 4)) { ok = false; break; }
-                tc_fence_after();
-                issue_gemm2(c, tmem, st, pb, j == 1);
-                mma_commit(bar(c, B_KV_EMPTY + st));
-                mma_commit(bar(c, B_P_EMPTY + pb));
-                mma_commit(bar(c, B_O_READY));
-                if (j == nt) mma_commit(bar(c, B_O_FINAL));
-            }
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        WarpTiles it;
+        it.init(ch, p);
+        int32_t pg, ntok;
+        if (!it.next(pg, ntok)) continue;
+        if (leader) {
+            ok = wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3);
+            tc_fence_after();
         }
-        g += nt;
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        if (!ok) break;
+        uint32_t j = 0;
+        do {
+            const uint32_t gj = g + j;
+            if (leader) {                                 /* GEMM1 of tile j, then GEMM2 of tile j-1 */
+                const uint32_t st = gj % kStages, sb = gj & 1;
+                ok = wait_bar(c, bar(c, B_KV_FULL + st), (gj / kStages) & 1, false, 5) &&
+                     wait_bar(c, bar(c, B_S_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 6);
+                if (ok) {
+                    tc_fence_after();
+                    issue_gemm1(c, tmem, st, sb);
+                    mma_commit(bar(c, B_S_FULL + sb));
+                    if (j >= 1) ok = mma_gemm2(c, tmem, gj - 1, j == 1, nchunk);
+                }
+            }
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            if (!ok) break;
+            j++;
+        } while (it.next(pg, ntok));
+        if (!ok) break;
+        if (leader) {
+            mma_commit(bar(c, B_Q_EMPTY));                /* every GEMM1 of the chunk has been issued */
+            ok = mma_gemm2(c, tmem, g + j - 1, j == 1, nchunk);
+            if (ok) mma_commit(bar(c, B_O_FINAL));
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        g += j;
         nchunk++;
     }
+    if (!leader) return;
     /* Drain the tensor pipe before TMEM is released. */
     mma_commit(bar(c, B_DRAIN));
     long long t0 = clock64();
@@ -377,6 +447,17 @@ __device__ __forceinline__ bool wait_warp(const Ctx &c, uint32_t b, uint32_t par
     return __all_sync(0xFFFFFFFFu, r);
 }
 
+/* One arrive per warp, after every lane's preceding work. */
+__device__ __forceinline__ void warp_arrive(uint32_t b) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(b);
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
 /* Swizzled position of 16-byte chunk `c` (0..15) of exchange row `row`. */
 __device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
 
@@ -385,106 +466,108 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     const uint32_t quad = warp & 3;                     /* TMEM lane quadrant this warp may access */
     const uint32_t row = quad * 32 + lane;              /* head */
     const uint32_t lane_base = (quad * 32) << 16;
-    const uint32_t x_mine = c.s + kOffX;
-    const uint32_t x_peer = mapa(x_mine, c.peer);
+    const uint32_t x_peer = mapa(c.s + kOffX, c.peer);
     const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
     const uint32_t xe_peer = mapa(bar(c, B_X_EMPTY), c.peer);
     uint32_t g = 0, nchunk = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
-        const ct_mla_chunk_t ch = p.chunks[ci];
-        const int nt = chunk_tiles(ch, p.bt, p.maxp, p.lens, p.n_pages);
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        WarpTiles it;
+        it.init(ch, p);
         float m_used = -INFINITY, l = 0.0f;
-        if (nt > 0) {
-            TileIter it = tiles_of(ch, p.bt, p.maxp, p.lens, p.n_pages);
-            for (int j = 0; j < nt && ok; j++) {
-                int32_t pg, ntok;
-                it.next(pg, ntok);
-                const uint32_t gj = g + j, sb = gj & 1, st = gj % kStages;
-                /* scores of this CTA's half */
-                if (!wait_warp(c, bar(c, B_S_FULL + sb), (gj >> 1) & 1, false, 8)) { ok = false; break; }
-                tc_fence_after();
-                float s[64];
-                tmem_ld32(tmem + lane_base + sb * 64, s);
-                tmem_ld32(tmem + lane_base + sb * 64 + 32, s + 32);
-                tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(bar(c, B_S_EMPTY + sb));
-                /* exchange with the other CTA: send mine, receive theirs */
-                if (!wait_warp(c, bar(c, B_X_EMPTY), (gj & 1) ^ 1, true, 9)) { ok = false; break; }
-                #pragma unroll
-                for (int q4 = 0; q4 < 16; q4++)
-                    st_cluster_v4(x_peer + xoff(row, q4), s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
-                mbar_arrive_remote(xf_peer);
-                if (!wait_warp(c, bar(c, B_X_FULL), gj & 1, true, 10)) { ok = false; break; }
-                const float4 *xr = reinterpret_cast<const float4 *>(c.smem + kOffX);
-                #pragma unroll
-                for (int q4 = 0; q4 < 16; q4++) {
-                    const float4 w = xr[xoff(row, q4) >> 4];
-                    s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
-                }
-                mbar_arrive_remote(xe_peer);
-                /* scaled scores, masked beyond the page's tokens */
-                float mx = -INFINITY;
-                #pragma unroll
-                for (int i = 0; i < 64; i++) {
-                    s[i] = (i < ntok) ? s[i] * p.qk_scale : -INFINITY;
-                    mx = fmaxf(mx, s[i]);
-                }
-                const bool grow = mx > m_used + kRescaleThreshold;   /* also true for the first tile */
-                const float m_new = grow ? mx : m_used;
-                const float alpha = exp2f(m_used - m_new);           /* 0 on the first tile, 1 if unchanged */
-                if (__any_sync(0xFFFFFFFFu, grow && j > 0)) {
-                    /* O holds tiles < j: wait for GEMM2(j-1), rescale this warp's rows */
-                    if (!wait_warp(c, bar(c, B_O_READY), (gj - 1) & 1, false, 11)) { ok = false; break; }
-                    tc_fence_after();
-                    const float a = grow ? alpha : 1.0f;
-                    #pragma unroll 1
-                    for (int cc = 0; cc < 8; cc++) {
-                        float o[32];
-                        tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
-                        tmem_wait_ld();
-                        #pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] *= a;
-                        tmem_st32(tmem + lane_base + kTmemO + cc * 32, o);
-                    }
-                    tmem_wait_st();
-                    tc_fence_before();
-                }
-                l *= alpha;
-                m_used = m_new;
-                /* P = bf16(2^(s - m)), row-wise into the SW128 K-major P buffer */
-                if (!wait_warp(c, bar(c, B_P_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 12)) { ok = false; break; }
-                uint8_t *pbuf = c.smem + kOffP + sb * kPBytes;
-                #pragma unroll
-                for (int ch16 = 0; ch16 < 8; ch16++) {
-                    uint32_t w[4];
-                    #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const uint16_t lo = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k] - m_used));
-                        const uint16_t hi = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k + 1] - m_used));
-                        l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
-                        w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
-                    }
-                    *reinterpret_cast<uint4 *>(pbuf + row * 128 + ((ch16 ^ (row & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                }
-                /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
-                if (ntok < kP) {
-                    uint8_t *kvs = c.smem + kOffKv + st * kKvBytes;
-                    const uint32_t tid = threadIdx.x - 64;
-                    const uint32_t n16 = (uint32_t)(kP - ntok) * 4 * 8;      /* 16-B words in 4 blocks */
-                    for (uint32_t i = tid; i < n16; i += 128) {
-                        const uint32_t blk = i / ((kP - ntok) * 8), rem = i % ((kP - ntok) * 8);
-                        const uint32_t r = ntok + rem / 8, w16 = rem % 8;
-                        *reinterpret_cast<uint4 *>(kvs + blk * 8192 + r * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
-                    }
-                }
-                proxy_fence();
-                mbar_arrive(bar(c, B_P_FULL + sb));
+        uint32_t j = 0;
+        int32_t pg, ntok;
+        while (it.next(pg, ntok)) {
+            const uint32_t gj = g + j, sb = gj & 1, st = gj % kStages;
+            /* scores of this CTA's half */
+            if (!wait_warp(c, bar(c, B_S_FULL + sb), (gj >> 1) & 1, false, 8)) { ok = false; break; }
+            tc_fence_after();
+            float s[64];
+            tmem_ld32(tmem + lane_base + sb * 64, s);
+            tmem_ld32(tmem + lane_base + sb * 64 + 32, s + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            warp_arrive(bar(c, B_S_EMPTY + sb));
+            /* exchange: my half into the peer's buffer, one release per warp, then theirs */
+            if (!wait_warp(c, bar(c, B_X_EMPTY), (gj & 1) ^ 1, true, 9)) { ok = false; break; }
+            #pragma unroll
+            for (int q4 = 0; q4 < 16; q4++)
+                st_cluster_v4(x_peer + xoff(row, q4), s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(xf_peer);
+            if (!wait_warp(c, bar(c, B_X_FULL), gj & 1, true, 10)) { ok = false; break; }
+            const float4 *xr = reinterpret_cast<const float4 *>(c.smem + kOffX);
+            #pragma unroll
+            for (int q4 = 0; q4 < 16; q4++) {
+                const float4 w = xr[xoff(row, q4) >> 4];
+                s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
             }
-            if (!ok) break;
-            g += nt;
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(xe_peer);
+            /* scaled scores, masked beyond the page's tokens */
+            float mx = -INFINITY;
+            #pragma unroll
+            for (int i = 0; i < 64; i++) {
+                s[i] = (i < ntok) ? s[i] * p.qk_scale : -INFINITY;
+                mx = fmaxf(mx, s[i]);
+            }
+            const bool grow = mx > m_used + kRescaleThreshold;   /* also true for the first tile */
+            const float m_new = grow ? mx : m_used;
+            const float alpha = exp2f(m_used - m_new);           /* 0 on the first tile, 1 if unchanged */
+            if (__any_sync(0xFFFFFFFFu, grow && j > 0)) {
+                /* O holds tiles < j: wait for GEMM2(j-1), rescale this warp's rows */
+                if (!wait_warp(c, bar(c, B_O_READY), (gj - 1) & 1, false, 11)) { ok = false; break; }
+                tc_fence_after();
+                const float a = grow ? alpha : 1.0f;
+                #pragma unroll 1
+                for (int cc = 0; cc < 8; cc++) {
+                    float o[32];
+                    tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
+                    tmem_wait_ld();
+                    #pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] *= a;
+                    tmem_st32(tmem + lane_base + kTmemO + cc * 32, o);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+            }
+            l *= alpha;
+            m_used = m_new;
+            /* P = bf16(2^(s - m)), row-wise into the SW128 K-major P buffer */
+            if (!wait_warp(c, bar(c, B_P_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 12)) { ok = false; break; }
+            uint8_t *pbuf = c.smem + kOffP + sb * kPBytes;
+            #pragma unroll
+            for (int ch16 = 0; ch16 < 8; ch16++) {
+                uint32_t w[4];
+                #pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const uint16_t lo = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k] - m_used));
+                    const uint16_t hi = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k + 1] - m_used));
+                    l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
+                    w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+                }
+                *reinterpret_cast<uint4 *>(pbuf + row * 128 + ((ch16 ^ (row & 7)) << 4)) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
+            if (ntok < kP) {
+                uint8_t *kvs = c.smem + kOffKv + st * kKvBytes;
+                const uint32_t tid = threadIdx.x - 64;
+                const uint32_t per_blk = (uint32_t)(kP - ntok) * 8;       /* 16-B words per block */
+                for (uint32_t i = tid; i < 4 * per_blk; i += 128) {
+                    const uint32_t blk = i / per_blk, rem = i % per_blk;
+                    const uint32_t r = (uint32_t)ntok + rem / 8, w16 = rem % 8;
+                    *reinterpret_cast<uint4 *>(kvs + blk * 8192 + r * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            proxy_fence();
+            warp_arrive(bar(c, B_P_FULL + sb));
+            j++;
+        }
+        if (!ok) break;
+        if (j > 0) {
+            g += j;
             /* epilogue: O rows of this CTA's 256 value dims */
             if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
             tc_fence_after();
@@ -514,7 +597,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                 }
             }
             tc_fence_before();
-            mbar_arrive(bar(c, B_O_FREE));
+            warp_arrive(bar(c, B_O_FREE));
             nchunk++;
         }
         /* outputs and statistics that only one CTA writes */
@@ -527,10 +610,10 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                 p.part_ml[2 * ((size_t)ch.part * kH + row) + 1] = l;
             }
         }
-        if (nt == 0 && ch.part < 0) {               /* nothing readable: zero output */
+        if (j == 0 && ch.part < 0) {               /* nothing readable: zero output */
             uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)ch.seq * kH + row) * kDv + rank * 256);
             for (int k = 0; k < 32; k++) dst[k] = make_uint4(0, 0, 0, 0);
-        } else if (nt == 0) {
+        } else if (j == 0) {
             float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + row) * kDv + rank * 256);
             for (int k = 0; k < 64; k++) dst[k] = make_float4(0, 0, 0, 0);
         }
@@ -562,11 +645,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_init(bar(c, B_KV_EMPTY + 0), 1); mbar_init(bar(c, B_KV_EMPTY + 1), 1);
         mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1);
         mbar_init(bar(c, B_S_FULL + 0), 1); mbar_init(bar(c, B_S_FULL + 1), 1);
-        mbar_init(bar(c, B_S_EMPTY + 0), 128); mbar_init(bar(c, B_S_EMPTY + 1), 128);
-        mbar_init(bar(c, B_P_FULL + 0), 128); mbar_init(bar(c, B_P_FULL + 1), 128);
+        mbar_init(bar(c, B_S_EMPTY + 0), 4); mbar_init(bar(c, B_S_EMPTY + 1), 4);
+        mbar_init(bar(c, B_P_FULL + 0), 4); mbar_init(bar(c, B_P_FULL + 1), 4);
         mbar_init(bar(c, B_P_EMPTY + 0), 1); mbar_init(bar(c, B_P_EMPTY + 1), 1);
-        mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1); mbar_init(bar(c, B_O_FREE), 128);
-        mbar_init(bar(c, B_X_FULL), 128); mbar_init(bar(c, B_X_EMPTY), 128);
+        mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1); mbar_init(bar(c, B_O_FREE), 4);
+        mbar_init(bar(c, B_X_FULL), 4); mbar_init(bar(c, B_X_EMPTY), 4);
         mbar_init(bar(c, B_DRAIN), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -582,9 +665,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
 
     if (warp == 0) {
-        if ((threadIdx.x & 31) == 0) producer(c, p, &kv_lat, &kv_rope, &q_lat, &q_rope, wbeg, wend, rank);
+        producer(c, p, &kv_lat, &kv_rope, &q_lat, &q_rope, wbeg, wend, rank);
     } else if (warp == 1) {
-        if ((threadIdx.x & 31) == 0) mma_issuer(c, p, tmem, wbeg, wend);
+        mma_issuer(c, p, tmem, wbeg, wend);
     } else {
         softmax_warps(c, p, tmem, wbeg, wend, rank);
     }
@@ -712,6 +795,7 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     p.lse = lse;
     p.part_o = part_o;
     p.part_ml = part_ml;
+    p.pool = static_cast<const uint8_t *>(pool);
     p.maxp = dims->max_pages_per_seq;
     p.n_pages = dims->n_pages;
     p.qk_scale = dims->scale * kLog2e;
