@@ -9,26 +9,36 @@
  * entry dimension: CTA r owns latent values [256r, 256r+256) and rope values
  * [512+32r, 544+32r).  Per 64-token page ("tile"):
  *   GEMM1  S_r = Q[:, own 288 dims] . KV[:, own 288 dims]^T  (M=128 heads,
- *          N=64 tokens, K=288) -> TMEM, double-buffered;
- *   the two partial S are exchanged through distributed shared memory and
- *   added (a + b is the same float in both CTAs, so both run the identical
- *   softmax on identical scores);
+ *          N=64 tokens, K=288) -> TMEM, double-buffered.  Q dims [0,128) of
+ *          the half are an A operand in TMEM, the other 160 in shared memory;
+ *   the two partial S are exchanged: each CTA stages its partial in shared
+ *          memory and a bulk copy moves it into the peer's receive buffer
+ *          (the SM-to-SM network moves ~20 B/clk this way, twice what
+ *          per-thread remote stores reach).  a + b is the same float in both
+ *          CTAs, so both run the identical softmax on identical scores;
  *   softmax in the log2 domain with a lazily updated row maximum (O is
  *          rescaled only when a row's maximum grows by more than 2^8);
- *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64) -> TMEM,
- *          reading V in MN-major form from the same shared-memory page tile.
- * Roles per CTA (192 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
- * issues the MMAs (one elected thread), warps 2-5 (thread = head row = TMEM
- * lane) do the exchange, softmax and epilogue.
+ *          P = bf16 probabilities, written to TMEM;
+ *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
+ *          from TMEM, V read MN-major from the same shared-memory page tile.
+ * The softmax warps run one tile behind the score exchange: they stage the
+ * scores of tile j for the peer, then finish tile j-1 while tile j's bytes
+ * travel, and the MMA warp issues GEMM1 of tile j+2 before GEMM2 of tile j.
  *
- * Shared memory (per CTA): Q 72 KB (4 SW128 [128x64] boxes + 1 SW64 [128x32]),
- * 2 page stages of 36 KB, 2 P buffers of 16 KB (SW128 K-major), the partial-S
- * exchange buffer 32 KB, barriers.  TMEM: S at columns 0/64, O at 256..511.
+ * Roles per CTA (352 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+ * issues the MMAs, warp 2 issues the exchange copies (one elected thread
+ * each), warps 3-10 finish scores, softmax and epilogue: two threads per
+ * head row (TMEM lane), one per 32-token half of a tile.
+ *
+ * Shared memory (per CTA): Q 40 KB (2 SW128 [128x64] boxes of latent dims
+ * [128,256) of the half + 1 SW64 [128x32] rope box), 3 page stages of 36 KB,
+ * exchange out / in buffers of 32 KB, a 3 KB row-statistics buffer, barriers.
+ * TMEM: S at columns 0/64, P at 128/160, Q at 192, O at 256..511.
  *
  * Every wait is bounded (about two seconds of clock); on expiry the kernel
- * records an error word, drains its own TMA loads and MMAs, frees TMEM and
- * returns.  No load uses cluster multicast, and no CTA reads another GPU's
- * memory.
+ * records an error word, drains its own TMA loads, copies and MMAs, frees
+ * TMEM and returns.  No load uses cluster multicast, and no CTA reads another
+ * GPU's memory.
  */
 #include "../../include/attention.h"
 #include "../../include/hal.h"
@@ -41,34 +51,41 @@
 namespace {
 
 constexpr int kH = 128, kE = 576, kDv = 512, kP = 64;
-constexpr int kThreads = 192;
-constexpr int kStages = 2;
-constexpr uint32_t kQBytes = 4 * 16384 + 8192;          /* 73,728 */
+constexpr int kSoftmaxWarps = 8;
+constexpr int kFirstSoftmaxWarp = 3;
+constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 352 */
+constexpr int kStages = 3;
+constexpr uint32_t kQBytes = 2 * 16384 + 8192;          /* 40,960 */
 constexpr uint32_t kKvBytes = 4 * 8192 + 4096;          /* 36,864 per stage */
-constexpr uint32_t kPBytes = 16384;
-constexpr uint32_t kXBytes = 32768;
+constexpr uint32_t kXBytes = 32768;                     /* one tile's partial scores, 128 x 64 fp32 */
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffKv = kOffQ + kQBytes;
-constexpr uint32_t kOffP = kOffKv + kStages * kKvBytes;
-constexpr uint32_t kOffX = kOffP + 2 * kPBytes;
-constexpr uint32_t kOffBar = kOffX + kXBytes;
+constexpr uint32_t kOffOut = kOffKv + kStages * kKvBytes;
+constexpr uint32_t kOffIn = kOffOut + kXBytes;
+constexpr uint32_t kOffRed = kOffIn + kXBytes;
+constexpr uint32_t kRedBytes = 6 * kH * 4;              /* row max [2 parities][2 halves], row sum [2 halves] */
+constexpr uint32_t kOffBar = kOffRed + kRedBytes;
 constexpr uint32_t kNumBars = 32;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
 constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
+static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
+static_assert(kOffKv % 1024 == 0 && kOffOut % 1024 == 0 && kOffIn % 1024 == 0, "swizzle atoms need 1 KB alignment");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns, fp32 scores */
+constexpr uint32_t kTmemP = 128;    /* 2 x 32 columns, bf16 probabilities (two per column) */
+constexpr uint32_t kTmemQ = 192;    /* 64 columns, bf16 query latent dims [0,128) of the half */
+constexpr uint32_t kTmemO = 256;    /* 256 columns, fp32 output accumulator */
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;
 constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
-constexpr int kPrefetchAhead = 6;                       /* pages pulled into L2 ahead of their TMA load */
-constexpr uint32_t kPageBytes = kP * kE * 2;            /* 73,728 */
 
 /* barrier slots */
 enum : uint32_t {
-    B_KV_FULL = 0, B_KV_EMPTY = 2, B_Q_FULL = 4, B_Q_EMPTY = 5, B_S_FULL = 6, B_S_EMPTY = 8, B_P_FULL = 10,
-    B_P_EMPTY = 12, B_O_READY = 14, B_O_FINAL = 15, B_O_FREE = 16, B_X_FULL = 17, B_X_EMPTY = 18, B_DRAIN = 19
+    B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_S_EMPTY = 11,
+    B_P_FULL = 13, B_P_EMPTY = 15, B_O_READY = 17, B_O_FINAL = 18, B_O_FREE = 19, B_SO_FULL = 20, B_SO_EMPTY = 21,
+    B_X_FULL = 22, B_X_EMPTY = 23, B_DRAIN = 24, B_RED = 25, B_RED_L = 27
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -124,19 +141,34 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
 }
+/* Bulk copy of this CTA's shared memory into the peer's, completing on the
+ * peer's barrier (both peer addresses from mapa). */
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "r"(src), "r"(bytes), "r"(bar) : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+/* D (TMEM) += A . B^T with A and B in shared memory. */
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
                  ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
+}
+/* The same with A in TMEM: lane m holds row m, column c its elements 2c, 2c+1. */
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }"
+                 ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc) : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-/* 32 consecutive TMEM columns of this thread's lane -> registers. */
+/* 32 consecutive TMEM columns of this thread's lane <-> registers. */
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     uint32_t r[32];
     asm volatile(
@@ -150,21 +182,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
         "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
-        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -202,26 +235,26 @@ __device__ bool wait_bar(const Ctx &c, uint32_t b, uint32_t parity, bool cluster
     }
 }
 
-/* Warp-cooperative walk over the pages of a chunk that hold tokens: lanes
- * read 32 consecutive block-table entries with one coalesced load, a ballot
- * marks the usable pages (page id in [0, n_pages), at least one token), and
- * next() hands them out in order.  All 32 lanes call it together; every
- * role walks the same list. */
 struct Params {
     const ct_mla_chunk_t *chunks;
     const int32_t *worker_begin;
     const int32_t *bt;
     const int32_t *lens;
+    const uint16_t *q;
     uint16_t *out;
     float *lse;
     float *part_o;
     float *part_ml;
-    const uint8_t *pool;
     uint32_t maxp;
     uint32_t n_pages;
     float qk_scale;          /* scale * log2(e) */
 };
 
+/* Warp-cooperative walk over the pages of a chunk that hold tokens: lanes
+ * read 32 consecutive block-table entries with one coalesced load, a ballot
+ * marks the usable pages (page id in [0, n_pages), at least one token), and
+ * next() hands them out in order.  All 32 lanes call it together; every
+ * role walks the same list. */
 struct WarpTiles {
     const int32_t *bt_row;
     int32_t len, next_lp, end, base, my_pg;
@@ -268,6 +301,16 @@ __device__ __forceinline__ ct_mla_chunk_t load_chunk(const Params &p, int ci) {
     return ch;
 }
 
+/* Tiles of a chunk (warp-collective). */
+__device__ __forceinline__ uint32_t count_tiles(const ct_mla_chunk_t &ch, const Params &p) {
+    WarpTiles it;
+    it.init(ch, p);
+    int32_t pg, ntok;
+    uint32_t n = 0;
+    while (it.next(pg, ntok)) n++;
+    return n;
+}
+
 /* ---- warp 0: TMA producer (lane 0 issues) -------------------------------- */
 
 __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_lat, const CUtensorMap *kv_rope,
@@ -281,39 +324,22 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
         it.init(ch, p);
         int32_t pg, ntok;
         if (!it.next(pg, ntok)) continue;               /* nothing readable in this chunk */
-        /* Q of this chunk's sequence, once the previous chunk's GEMM1s are done */
+        /* Q dims [128,256) of this CTA's half and its rope dims, once the
+         * previous chunk's GEMM1s are done */
         if (leader) {
             ok = wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1);
             if (ok) {
                 mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
                 const int qy = ch.seq * kH;
-                for (int b = 0; b < 4; b++)
-                    tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + b * 64, qy, bar(c, B_Q_FULL));
-                tma_load_2d(c.s + kOffQ + 4 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
+                for (int b = 0; b < 2; b++)
+                    tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + 128 + b * 64, qy, bar(c, B_Q_FULL));
+                tma_load_2d(c.s + kOffQ + 2 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
             }
         }
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         if (!ok) break;
         nq++;
-        /* a second walk runs kPrefetchAhead pages ahead and pulls whole pages
-         * (both CTAs' halves) into L2, so the TMA loads below hit L2 */
-        WarpTiles pre = it;
-        int32_t ppg, pnt;
-        bool pre_ok = true;
-        const bool prefetcher = leader && rank == 0;
-        for (int k = 0; k < kPrefetchAhead && pre_ok; k++) {
-            if (k == 0) { ppg = pg; pnt = ntok; } else pre_ok = pre.next(ppg, pnt);
-            if (pre_ok && prefetcher)
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                             ::"l"(p.pool + (size_t)ppg * kPageBytes), "r"(kPageBytes) : "memory");
-        }
         do {
-            if (pre_ok) {
-                pre_ok = pre.next(ppg, pnt);
-                if (pre_ok && prefetcher)
-                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                                 ::"l"(p.pool + (size_t)ppg * kPageBytes), "r"(kPageBytes) : "memory");
-            }
             const uint32_t st = g % kStages;
             if (leader) {
                 ok = wait_bar(c, bar(c, B_KV_EMPTY + st), ((g / kStages) & 1) ^ 1, false, 2);
@@ -333,7 +359,7 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
     }
     if (!leader) return;
     /* Drain: every issued load must have landed before the CTA may exit. */
-    for (uint32_t k = 0; k < kStages && k < g; k++) {
+    for (uint32_t k = 0; k < (uint32_t)kStages && k < g; k++) {
         const uint32_t last = g - 1 - k;
         const uint32_t st = last % kStages;
         long long t0 = clock64();
@@ -349,34 +375,48 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
 
 __device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf) {
     const uint32_t q = c.s + kOffQ, kv = c.s + kOffKv + st * kKvBytes;
-    const uint32_t d = tmem + sbuf * 64;
-    uint32_t acc = 0;
+    const uint32_t d = tmem + kTmemS + sbuf * 64;
+    /* latent dims [0,128) of the half: A from TMEM */
     #pragma unroll
-    for (int b = 0; b < 4; b++)
-        #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            mma_bf16(d, sdesc(q + b * 16384 + k * 32, 1, 64, kSw128), sdesc(kv + b * 8192 + k * 32, 1, 64, kSw128),
-                     kIdescS, acc);
-            acc = 1;
-        }
+    for (int i = 0; i < 8; i++)
+        mma_ts(d, tmem + kTmemQ + i * 8, sdesc(kv + (i >> 2) * 8192 + (i & 3) * 32, 1, 64, kSw128), kIdescS,
+               i > 0 ? 1u : 0u);
+    /* latent dims [128,256): A from shared memory */
+    #pragma unroll
+    for (int i = 8; i < 16; i++)
+        mma_ss(d, sdesc(q + ((i - 8) >> 2) * 16384 + (i & 3) * 32, 1, 64, kSw128),
+               sdesc(kv + (i >> 2) * 8192 + (i & 3) * 32, 1, 64, kSw128), kIdescS, 1);
+    /* rope dims */
     #pragma unroll
     for (int k = 0; k < 2; k++)
-        mma_bf16(d, sdesc(q + 4 * 16384 + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64),
-                 kIdescS, 1);
+        mma_ss(d, sdesc(q + 2 * 16384 + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64),
+               kIdescS, 1);
 }
 
 __device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t pbuf, bool first) {
-    const uint32_t pa = c.s + kOffP + pbuf * kPBytes, v = c.s + kOffKv + st * kKvBytes;
+    const uint32_t v = c.s + kOffKv + st * kKvBytes;
     #pragma unroll
     for (int k = 0; k < 4; k++)
-        mma_bf16(tmem + kTmemO, sdesc(pa + k * 32, 1, 64, kSw128), sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
-                 (first && k == 0) ? 0u : 1u);
+        mma_ts(tmem + kTmemO, tmem + kTmemP + pbuf * 32 + k * 8, sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
+               (first && k == 0) ? 0u : 1u);
 }
 
-/* GEMM2 of global tile gj (the j-th of its chunk), with its releases. */
-__device__ bool mma_gemm2(const Ctx &c, uint32_t tmem, uint32_t gj, bool first, uint32_t nchunk) {
-    const uint32_t st = gj % kStages, pb = gj & 1;
-    if (!wait_bar(c, bar(c, B_P_FULL + pb), (gj >> 1) & 1, false, 7)) return false;
+/* GEMM1 of global tile gt: needs its page and a free score buffer. */
+__device__ bool mma_gemm1(const Ctx &c, uint32_t tmem, uint32_t gt) {
+    const uint32_t st = gt % kStages, sb = gt & 1;
+    if (!wait_bar(c, bar(c, B_KV_FULL + st), (gt / kStages) & 1, false, 5) ||
+        !wait_bar(c, bar(c, B_S_EMPTY + sb), ((gt >> 1) & 1) ^ 1, false, 6))
+        return false;
+    tc_fence_after();
+    issue_gemm1(c, tmem, st, sb);
+    mma_commit(bar(c, B_S_FULL + sb));
+    return true;
+}
+
+/* GEMM2 of global tile gt (the first of its chunk if `first`), with its releases. */
+__device__ bool mma_gemm2(const Ctx &c, uint32_t tmem, uint32_t gt, bool first, uint32_t nchunk) {
+    const uint32_t st = gt % kStages, pb = gt & 1;
+    if (!wait_bar(c, bar(c, B_P_FULL + pb), (gt >> 1) & 1, false, 7)) return false;
     /* the first GEMM2 of a chunk overwrites O: the previous epilogue must have read it */
     if (first && !wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 4)) return false;
     tc_fence_after();
@@ -393,42 +433,29 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
-        WarpTiles it;
-        it.init(ch, p);
-        int32_t pg, ntok;
-        if (!it.next(pg, ntok)) continue;
+        const uint32_t n = count_tiles(ch, p);
+        if (n == 0) continue;
         if (leader) {
-            ok = wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3);
+            /* both parts of this chunk's Q: the TMA half and the TMEM half */
+            ok = wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3) &&
+                 wait_bar(c, bar(c, B_QT_FULL), nchunk & 1, false, 3);
             tc_fence_after();
-        }
-        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        if (!ok) break;
-        uint32_t j = 0;
-        do {
-            const uint32_t gj = g + j;
-            if (leader) {                                 /* GEMM1 of tile j, then GEMM2 of tile j-1 */
-                const uint32_t st = gj % kStages, sb = gj & 1;
-                ok = wait_bar(c, bar(c, B_KV_FULL + st), (gj / kStages) & 1, false, 5) &&
-                     wait_bar(c, bar(c, B_S_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 6);
-                if (ok) {
-                    tc_fence_after();
-                    issue_gemm1(c, tmem, st, sb);
-                    mma_commit(bar(c, B_S_FULL + sb));
-                    if (j >= 1) ok = mma_gemm2(c, tmem, gj - 1, j == 1, nchunk);
-                }
+            /* GEMM1 runs two tiles ahead of GEMM2 */
+            for (uint32_t j = 0; j < 2 && j < n && ok; j++) {
+                ok = mma_gemm1(c, tmem, g + j);
+                if (ok && j == n - 1) mma_commit(bar(c, B_Q_EMPTY));
             }
-            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-            if (!ok) break;
-            j++;
-        } while (it.next(pg, ntok));
-        if (!ok) break;
-        if (leader) {
-            mma_commit(bar(c, B_Q_EMPTY));                /* every GEMM1 of the chunk has been issued */
-            ok = mma_gemm2(c, tmem, g + j - 1, j == 1, nchunk);
+            for (uint32_t j = 0; j < n && ok; j++) {
+                if (j + 2 < n) {
+                    ok = mma_gemm1(c, tmem, g + j + 2);
+                    if (ok && j + 2 == n - 1) mma_commit(bar(c, B_Q_EMPTY));
+                }
+                if (ok) ok = mma_gemm2(c, tmem, g + j, j == 0, nchunk);
+            }
             if (ok) mma_commit(bar(c, B_O_FINAL));
         }
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        g += j;
+        g += n;
         nchunk++;
     }
     if (!leader) return;
@@ -438,7 +465,36 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
     while (!mbar_try(bar(c, B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {}
 }
 
-/* ---- warps 2-5: exchange, softmax, epilogue ------------------------------- */
+/* ---- warp 2: score exchange (lane 0 issues) ------------------------------- */
+
+__device__ void exchanger(const Ctx &c, const Params &p, int wbeg, int wend) {
+    const bool leader = (threadIdx.x & 31) == 0;
+    const uint32_t in_peer = mapa(c.s + kOffIn, c.peer);
+    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
+    uint32_t t = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        const uint32_t n = count_tiles(ch, p);
+        for (uint32_t j = 0; j < n && ok; j++, t++) {
+            if (leader) {
+                /* this tile's partial scores are staged, and the peer has
+                 * consumed the previous tile's from its receive buffer */
+                ok = wait_bar(c, bar(c, B_SO_FULL), t & 1, false, 14) &&
+                     wait_bar(c, bar(c, B_X_EMPTY), (t & 1) ^ 1, true, 15);
+                if (ok) {
+                    bulk_copy_to_peer(in_peer, c.s + kOffOut, kXBytes, xf_peer);
+                    bulk_wait_read();
+                    mbar_arrive(bar(c, B_SO_EMPTY));
+                }
+            }
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        }
+    }
+    if (leader) bulk_wait_all();                    /* every copy has landed in the peer */
+}
+
+/* ---- warps 3-10: scores, softmax, epilogue -------------------------------- */
 
 /* A wait all 32 lanes of a softmax warp leave together (the tcgen05 loads
  * and stores that follow are warp-collective). */
@@ -453,170 +509,225 @@ __device__ __forceinline__ void warp_arrive(uint32_t b) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(b);
 }
 
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
-}
-
 /* Swizzled position of 16-byte chunk `c` (0..15) of exchange row `row`. */
 __device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
+
+struct Row {
+    uint32_t row, half, lane_base, tid;
+    float m_used, l;
+};
+
+/* Finishes global tile t (index jj in its chunk): adds the peer's partial
+ * scores, updates the running maximum, rescales O if needed, writes P. */
+__device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r, uint32_t t, uint32_t jj, float *s,
+                            int32_t ntok) {
+    const uint32_t lane = threadIdx.x & 31;
+    float *red = reinterpret_cast<float *>(c.smem + kOffRed);
+    if (!wait_warp(c, bar(c, B_X_FULL), t & 1, true, 10)) return false;
+    const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn);
+    #pragma unroll
+    for (int q4 = 0; q4 < 8; q4++) {
+        const float4 w = xin[xoff(r.row, r.half * 8 + q4) >> 4];
+        s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(mapa(bar(c, B_X_EMPTY), c.peer));
+    if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL), kXBytes);      /* arm for the next tile */
+    /* scaled scores, masked beyond the page's tokens; row maximum over both halves */
+    float mx = -INFINITY;
+    #pragma unroll
+    for (int i = 0; i < 32; i++) {
+        s[i] = ((int32_t)(r.half * 32 + i) < ntok) ? s[i] * p.qk_scale : -INFINITY;
+        mx = fmaxf(mx, s[i]);
+    }
+    float *rm = red + (t & 1) * 2 * kH;
+    rm[r.half * kH + r.row] = mx;
+    warp_arrive(bar(c, B_RED + (t & 1)));
+    if (!wait_warp(c, bar(c, B_RED + (t & 1)), (t >> 1) & 1, false, 16)) return false;
+    mx = fmaxf(mx, rm[(r.half ^ 1) * kH + r.row]);
+    const bool grow = mx > r.m_used + kRescaleThreshold;   /* also true for the first tile */
+    const float m_new = grow ? mx : r.m_used;
+    const float alpha = exp2f(r.m_used - m_new);            /* 0 on the first tile, 1 if unchanged */
+    if (__any_sync(0xFFFFFFFFu, grow && jj > 0)) {
+        /* O holds tiles before t: wait for GEMM2(t-1), rescale this thread's half row */
+        if (!wait_warp(c, bar(c, B_O_READY), (t - 1) & 1, false, 11)) return false;
+        tc_fence_after();
+        const float a = grow ? alpha : 1.0f;
+        #pragma unroll 1
+        for (int cc = 0; cc < 4; cc++) {
+            float o[32];
+            uint32_t u[32];
+            tmem_ld32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, o);
+            tmem_wait_ld();
+            #pragma unroll
+            for (int i = 0; i < 32; i++) u[i] = __float_as_uint(o[i] * a);
+            tmem_st32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, u);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+    }
+    r.l *= alpha;
+    r.m_used = m_new;
+    /* P = bf16(2^(s - m)) into TMEM: 32 tokens = 16 columns of this half */
+    if (!wait_warp(c, bar(c, B_P_EMPTY + (t & 1)), ((t >> 1) & 1) ^ 1, false, 12)) return false;
+    uint32_t w[16];
+    #pragma unroll
+    for (int k = 0; k < 16; k++) {
+        const uint16_t lo = ct_f32_to_bf16(exp2f(s[2 * k] - r.m_used));
+        const uint16_t hi = ct_f32_to_bf16(exp2f(s[2 * k + 1] - r.m_used));
+        r.l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
+        w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    tmem_st16(tmem + r.lane_base + kTmemP + (t & 1) * 32 + r.half * 16, w);
+    /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
+    if (ntok < kP) {
+        uint8_t *kvs = c.smem + kOffKv + (t % kStages) * kKvBytes;
+        const uint32_t per_blk = (uint32_t)(kP - ntok) * 8;          /* 16-B words per box */
+        for (uint32_t i = r.tid; i < 4 * per_blk; i += 32 * kSoftmaxWarps) {
+            const uint32_t blk = i / per_blk, rem = i % per_blk;
+            const uint32_t rr = (uint32_t)ntok + rem / 8, w16 = rem % 8;
+            *reinterpret_cast<uint4 *>(kvs + blk * 8192 + rr * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
+        }
+        proxy_fence();
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    warp_arrive(bar(c, B_P_FULL + (t & 1)));
+    return true;
+}
 
 __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3;                     /* TMEM lane quadrant this warp may access */
-    const uint32_t row = quad * 32 + lane;              /* head */
-    const uint32_t lane_base = (quad * 32) << 16;
-    const uint32_t x_peer = mapa(c.s + kOffX, c.peer);
-    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
-    const uint32_t xe_peer = mapa(bar(c, B_X_EMPTY), c.peer);
+    Row r;
+    r.half = (warp - kFirstSoftmaxWarp) >> 2;           /* tokens [32h, 32h+32) of a tile, O columns [128h, +128) */
+    r.row = quad * 32 + lane;                           /* head */
+    r.lane_base = (quad * 32) << 16;
+    r.tid = (warp - kFirstSoftmaxWarp) * 32 + lane;
+    float *red = reinterpret_cast<float *>(c.smem + kOffRed);
     uint32_t g = 0, nchunk = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
         WarpTiles it;
         it.init(ch, p);
-        float m_used = -INFINITY, l = 0.0f;
-        uint32_t j = 0;
         int32_t pg, ntok;
-        while (it.next(pg, ntok)) {
-            const uint32_t gj = g + j, sb = gj & 1, st = gj % kStages;
-            /* scores of this CTA's half */
-            if (!wait_warp(c, bar(c, B_S_FULL + sb), (gj >> 1) & 1, false, 8)) { ok = false; break; }
+        const size_t oh = (size_t)ch.seq * kH + r.row;
+        const uint32_t d_base = rank * 256 + r.half * 128;
+        if (!it.next(pg, ntok)) {
+            /* nothing readable: zero output */
+            if (ch.part < 0) {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d_base);
+                for (int k = 0; k < 16; k++) dst[k] = make_uint4(0, 0, 0, 0);
+            } else {
+                float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + r.row) * kDv + d_base);
+                for (int k = 0; k < 32; k++) dst[k] = make_float4(0, 0, 0, 0);
+            }
+            if (rank == 0 && r.half == 0) {
+                if (ch.part < 0) {
+                    if (p.lse) p.lse[oh] = -INFINITY;
+                } else {
+                    p.part_ml[2 * ((size_t)ch.part * kH + r.row)] = -INFINITY;
+                    p.part_ml[2 * ((size_t)ch.part * kH + r.row) + 1] = 0.0f;
+                }
+            }
+            continue;
+        }
+        /* Q latent dims [0,128) of this CTA's half into TMEM, once the
+         * previous chunk's GEMM1s are done: this thread's 64 dims */
+        if (!wait_warp(c, bar(c, B_Q_EMPTY), (nchunk & 1) ^ 1, false, 17)) { ok = false; break; }
+        tc_fence_after();
+        {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.half * 64);
+            uint32_t u[32];
+            #pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint4 v = __ldg(src + k);
+                u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
+            }
+            tmem_st32(tmem + r.lane_base + kTmemQ + r.half * 32, u);
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        warp_arrive(bar(c, B_QT_FULL));
+        r.m_used = -INFINITY;
+        r.l = 0.0f;
+        float s_prev[32];
+        int32_t prev_ntok = 0;
+        uint32_t j = 0;
+        do {
+            const uint32_t gt = g + j, sb = gt & 1;
+            /* this CTA's partial scores of tile gt: to registers (freeing the
+             * score buffer) and to the exchange staging buffer */
+            float s_cur[32];
+            if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) { ok = false; break; }
             tc_fence_after();
-            float s[64];
-            tmem_ld32(tmem + lane_base + sb * 64, s);
-            tmem_ld32(tmem + lane_base + sb * 64 + 32, s + 32);
+            tmem_ld32(tmem + r.lane_base + kTmemS + sb * 64 + r.half * 32, s_cur);
             tmem_wait_ld();
             tc_fence_before();
             warp_arrive(bar(c, B_S_EMPTY + sb));
-            /* exchange: my half into the peer's buffer, one release per warp, then theirs */
-            if (!wait_warp(c, bar(c, B_X_EMPTY), (gj & 1) ^ 1, true, 9)) { ok = false; break; }
+            if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) { ok = false; break; }
+            float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
             #pragma unroll
-            for (int q4 = 0; q4 < 16; q4++)
-                st_cluster_v4(x_peer + xoff(row, q4), s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(xf_peer);
-            if (!wait_warp(c, bar(c, B_X_FULL), gj & 1, true, 10)) { ok = false; break; }
-            const float4 *xr = reinterpret_cast<const float4 *>(c.smem + kOffX);
+            for (int q4 = 0; q4 < 8; q4++)
+                xout[xoff(r.row, r.half * 8 + q4) >> 4] =
+                    make_float4(s_cur[4 * q4], s_cur[4 * q4 + 1], s_cur[4 * q4 + 2], s_cur[4 * q4 + 3]);
+            proxy_fence();
+            warp_arrive(bar(c, B_SO_FULL));
+            /* the previous tile, whose peer half has had this long to arrive */
+            if (j > 0 && !finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
             #pragma unroll
-            for (int q4 = 0; q4 < 16; q4++) {
-                const float4 w = xr[xoff(row, q4) >> 4];
-                s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(xe_peer);
-            /* scaled scores, masked beyond the page's tokens */
-            float mx = -INFINITY;
-            #pragma unroll
-            for (int i = 0; i < 64; i++) {
-                s[i] = (i < ntok) ? s[i] * p.qk_scale : -INFINITY;
-                mx = fmaxf(mx, s[i]);
-            }
-            const bool grow = mx > m_used + kRescaleThreshold;   /* also true for the first tile */
-            const float m_new = grow ? mx : m_used;
-            const float alpha = exp2f(m_used - m_new);           /* 0 on the first tile, 1 if unchanged */
-            if (__any_sync(0xFFFFFFFFu, grow && j > 0)) {
-                /* O holds tiles < j: wait for GEMM2(j-1), rescale this warp's rows */
-                if (!wait_warp(c, bar(c, B_O_READY), (gj - 1) & 1, false, 11)) { ok = false; break; }
-                tc_fence_after();
-                const float a = grow ? alpha : 1.0f;
-                #pragma unroll 1
-                for (int cc = 0; cc < 8; cc++) {
-                    float o[32];
-                    tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
-                    tmem_wait_ld();
-                    #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] *= a;
-                    tmem_st32(tmem + lane_base + kTmemO + cc * 32, o);
-                }
-                tmem_wait_st();
-                tc_fence_before();
-            }
-            l *= alpha;
-            m_used = m_new;
-            /* P = bf16(2^(s - m)), row-wise into the SW128 K-major P buffer */
-            if (!wait_warp(c, bar(c, B_P_EMPTY + sb), ((gj >> 1) & 1) ^ 1, false, 12)) { ok = false; break; }
-            uint8_t *pbuf = c.smem + kOffP + sb * kPBytes;
-            #pragma unroll
-            for (int ch16 = 0; ch16 < 8; ch16++) {
-                uint32_t w[4];
+            for (int i = 0; i < 32; i++) s_prev[i] = s_cur[i];
+            prev_ntok = ntok;
+            j++;
+        } while (it.next(pg, ntok));
+        if (!ok) break;
+        if (!finish_tile(c, p, tmem, r, g + j - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
+        g += j;
+        /* epilogue: the row sum over both halves, then O of this CTA's 256 value dims */
+        float *rl = red + 4 * kH;
+        rl[r.half * kH + r.row] = r.l;
+        warp_arrive(bar(c, B_RED_L));
+        if (!wait_warp(c, bar(c, B_RED_L), nchunk & 1, false, 18)) { ok = false; break; }
+        const float l_tot = r.l + rl[(r.half ^ 1) * kH + r.row];
+        if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
+        tc_fence_after();
+        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+        #pragma unroll 1
+        for (int cc = 0; cc < 4; cc++) {
+            float o[32];
+            tmem_ld32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, o);
+            tmem_wait_ld();
+            const uint32_t d0 = d_base + cc * 32;
+            if (ch.part < 0) {
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d0);
                 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    const uint16_t lo = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k] - m_used));
-                    const uint16_t hi = ct_f32_to_bf16(exp2f(s[ch16 * 8 + 2 * k + 1] - m_used));
-                    l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
-                    w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
-                }
-                *reinterpret_cast<uint4 *>(pbuf + row * 128 + ((ch16 ^ (row & 7)) << 4)) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
-            if (ntok < kP) {
-                uint8_t *kvs = c.smem + kOffKv + st * kKvBytes;
-                const uint32_t tid = threadIdx.x - 64;
-                const uint32_t per_blk = (uint32_t)(kP - ntok) * 8;       /* 16-B words per block */
-                for (uint32_t i = tid; i < 4 * per_blk; i += 128) {
-                    const uint32_t blk = i / per_blk, rem = i % per_blk;
-                    const uint32_t r = (uint32_t)ntok + rem / 8, w16 = rem % 8;
-                    *reinterpret_cast<uint4 *>(kvs + blk * 8192 + r * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
-                }
-            }
-            proxy_fence();
-            warp_arrive(bar(c, B_P_FULL + sb));
-            j++;
-        }
-        if (!ok) break;
-        if (j > 0) {
-            g += j;
-            /* epilogue: O rows of this CTA's 256 value dims */
-            if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
-            tc_fence_after();
-            const size_t oh = (size_t)ch.seq * kH + row;
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            #pragma unroll 1
-            for (int cc = 0; cc < 8; cc++) {
-                float o[32];
-                tmem_ld32(tmem + lane_base + kTmemO + cc * 32, o);
-                tmem_wait_ld();
-                const uint32_t d0 = rank * 256 + cc * 32;
-                if (ch.part < 0) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d0);
+                    uint32_t w[4];
                     #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        uint32_t w[4];
-                        #pragma unroll
-                        for (int e = 0; e < 4; e++)
-                            w[e] = (uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e] * inv) |
-                                   ((uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e + 1] * inv) << 16);
-                        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                } else {
-                    float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + row) * kDv + d0);
-                    #pragma unroll
-                    for (int k = 0; k < 8; k++) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                    for (int e = 0; e < 4; e++)
+                        w[e] = (uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e] * inv) |
+                               ((uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e + 1] * inv) << 16);
+                    dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
                 }
-            }
-            tc_fence_before();
-            warp_arrive(bar(c, B_O_FREE));
-            nchunk++;
-        }
-        /* outputs and statistics that only one CTA writes */
-        if (rank == 0) {
-            const size_t oh = (size_t)ch.seq * kH + row;
-            if (ch.part < 0) {
-                if (p.lse) p.lse[oh] = l > 0.0f ? m_used * kLn2 + logf(l) : -INFINITY;
             } else {
-                p.part_ml[2 * ((size_t)ch.part * kH + row)] = m_used;
-                p.part_ml[2 * ((size_t)ch.part * kH + row) + 1] = l;
+                float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + r.row) * kDv + d0);
+                #pragma unroll
+                for (int k = 0; k < 8; k++) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
             }
         }
-        if (j == 0 && ch.part < 0) {               /* nothing readable: zero output */
-            uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)ch.seq * kH + row) * kDv + rank * 256);
-            for (int k = 0; k < 32; k++) dst[k] = make_uint4(0, 0, 0, 0);
-        } else if (j == 0) {
-            float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + row) * kDv + rank * 256);
-            for (int k = 0; k < 64; k++) dst[k] = make_float4(0, 0, 0, 0);
+        tc_fence_before();
+        warp_arrive(bar(c, B_O_FREE));
+        /* statistics that one thread per row writes */
+        if (rank == 0 && r.half == 0) {
+            if (ch.part < 0) {
+                if (p.lse) p.lse[oh] = l_tot > 0.0f ? r.m_used * kLn2 + logf(l_tot) : -INFINITY;
+            } else {
+                p.part_ml[2 * ((size_t)ch.part * kH + r.row)] = r.m_used;
+                p.part_ml[2 * ((size_t)ch.part * kH + r.row) + 1] = l_tot;
+            }
         }
+        nchunk++;
     }
 }
 
@@ -641,17 +752,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         s_abort = 0;
-        mbar_init(bar(c, B_KV_FULL + 0), 1); mbar_init(bar(c, B_KV_FULL + 1), 1);
-        mbar_init(bar(c, B_KV_EMPTY + 0), 1); mbar_init(bar(c, B_KV_EMPTY + 1), 1);
-        mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1);
-        mbar_init(bar(c, B_S_FULL + 0), 1); mbar_init(bar(c, B_S_FULL + 1), 1);
-        mbar_init(bar(c, B_S_EMPTY + 0), 4); mbar_init(bar(c, B_S_EMPTY + 1), 4);
-        mbar_init(bar(c, B_P_FULL + 0), 4); mbar_init(bar(c, B_P_FULL + 1), 4);
-        mbar_init(bar(c, B_P_EMPTY + 0), 1); mbar_init(bar(c, B_P_EMPTY + 1), 1);
-        mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1); mbar_init(bar(c, B_O_FREE), 4);
-        mbar_init(bar(c, B_X_FULL), 4); mbar_init(bar(c, B_X_EMPTY), 4);
-        mbar_init(bar(c, B_DRAIN), 1);
+        for (int i = 0; i < kStages; i++) {
+            mbar_init(bar(c, B_KV_FULL + i), 1);
+            mbar_init(bar(c, B_KV_EMPTY + i), 1);
+        }
+        mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1); mbar_init(bar(c, B_QT_FULL), kSoftmaxWarps);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(c, B_S_FULL + i), 1);
+            mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps);
+            mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
+            mbar_init(bar(c, B_P_EMPTY + i), 1);
+            mbar_init(bar(c, B_RED + i), kSoftmaxWarps);
+        }
+        mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
+        mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
+        mbar_init(bar(c, B_SO_FULL), kSoftmaxWarps); mbar_init(bar(c, B_SO_EMPTY), 1);
+        mbar_init(bar(c, B_X_FULL), 1); mbar_init(bar(c, B_X_EMPTY), kSoftmaxWarps);
+        mbar_init(bar(c, B_DRAIN), 1); mbar_init(bar(c, B_RED_L), kSoftmaxWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(bar(c, B_X_FULL), kXBytes);   /* armed for the first tile */
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -660,7 +779,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();                                 /* both CTAs' barriers exist before any remote arrive */
+    cluster_sync();                                 /* both CTAs' barriers exist before any remote arrive or copy */
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
 
@@ -668,6 +787,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         producer(c, p, &kv_lat, &kv_rope, &q_lat, &q_rope, wbeg, wend, rank);
     } else if (warp == 1) {
         mma_issuer(c, p, tmem, wbeg, wend);
+    } else if (warp == 2) {
+        exchanger(c, p, wbeg, wend);
     } else {
         softmax_warps(c, p, tmem, wbeg, wend, rank);
     }
@@ -771,8 +892,6 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     cudaGetDevice(&dev);
     if (ct__mla_tc_workers(dims, dev) <= 0 || n_workers == 0) return CT_ERR_UNSUPPORTED;
     if (((uintptr_t)pool & 15u) || ((uintptr_t)q & 15u) || ((uintptr_t)out & 15u)) return CT_ERR_UNSUPPORTED;
-    /* Rows of the pool map: pages are addressed by the block table; the map
-     * covers up to the largest page id the tables can hold (2^31 / 64). */
     /* Maps cover exactly the pool and q: a page id beyond the pool reads
      * zeros (TMA out-of-bounds fill) rather than foreign memory. */
     CUtensorMap kv_lat, kv_rope, q_lat, q_rope;
@@ -791,11 +910,11 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     p.worker_begin = worker_begin;
     p.bt = block_table;
     p.lens = seq_lens;
+    p.q = static_cast<const uint16_t *>(q);
     p.out = static_cast<uint16_t *>(out);
     p.lse = lse;
     p.part_o = part_o;
     p.part_ml = part_ml;
-    p.pool = static_cast<const uint8_t *>(pool);
     p.maxp = dims->max_pages_per_seq;
     p.n_pages = dims->n_pages;
     p.qk_scale = dims->scale * kLog2e;
