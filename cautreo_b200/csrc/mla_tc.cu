@@ -21,9 +21,10 @@
  *          P = bf16 probabilities, written to TMEM;
  *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
  *          from TMEM, V read MN-major from the same shared-memory page tile.
- * The softmax warps run one tile behind the score exchange: they stage the
- * scores of tile j for the peer, then finish tile j-1 while tile j's bytes
- * travel, and the MMA warp issues GEMM1 of tile j+2 before GEMM2 of tile j.
+ * The softmax warps keep one tile in flight: they finish tile j-1 (once the
+ * peer's half is in) and stage tile j for the peer in whichever order their
+ * inputs arrive, and the MMA warp issues each GEMM as soon as its operands
+ * are ready, GEMM1 up to two tiles ahead of GEMM2.
  *
  * Roles per CTA (352 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
@@ -125,8 +126,12 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+/* Arrive on the peer's barrier without release semantics: it only signals
+ * that this thread's loads of the receive buffer have returned, which every
+ * later instruction already depends on (a release at cluster scope costs about
+ * a microsecond here). */
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -401,32 +406,6 @@ __device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t p
                (first && k == 0) ? 0u : 1u);
 }
 
-/* GEMM1 of global tile gt: needs its page and a free score buffer. */
-__device__ bool mma_gemm1(const Ctx &c, uint32_t tmem, uint32_t gt) {
-    const uint32_t st = gt % kStages, sb = gt & 1;
-    if (!wait_bar(c, bar(c, B_KV_FULL + st), (gt / kStages) & 1, false, 5) ||
-        !wait_bar(c, bar(c, B_S_EMPTY + sb), ((gt >> 1) & 1) ^ 1, false, 6))
-        return false;
-    tc_fence_after();
-    issue_gemm1(c, tmem, st, sb);
-    mma_commit(bar(c, B_S_FULL + sb));
-    return true;
-}
-
-/* GEMM2 of global tile gt (the first of its chunk if `first`), with its releases. */
-__device__ bool mma_gemm2(const Ctx &c, uint32_t tmem, uint32_t gt, bool first, uint32_t nchunk) {
-    const uint32_t st = gt % kStages, pb = gt & 1;
-    if (!wait_bar(c, bar(c, B_P_FULL + pb), (gt >> 1) & 1, false, 7)) return false;
-    /* the first GEMM2 of a chunk overwrites O: the previous epilogue must have read it */
-    if (first && !wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 4)) return false;
-    tc_fence_after();
-    issue_gemm2(c, tmem, st, pb, first);
-    mma_commit(bar(c, B_KV_EMPTY + st));
-    mma_commit(bar(c, B_P_EMPTY + pb));
-    mma_commit(bar(c, B_O_READY));
-    return true;
-}
-
 __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
     const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nchunk = 0;
@@ -440,17 +419,46 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
             ok = wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3) &&
                  wait_bar(c, bar(c, B_QT_FULL), nchunk & 1, false, 3);
             tc_fence_after();
-            /* GEMM1 runs two tiles ahead of GEMM2 */
-            for (uint32_t j = 0; j < 2 && j < n && ok; j++) {
-                ok = mma_gemm1(c, tmem, g + j);
-                if (ok && j == n - 1) mma_commit(bar(c, B_Q_EMPTY));
-            }
-            for (uint32_t j = 0; j < n && ok; j++) {
-                if (j + 2 < n) {
-                    ok = mma_gemm1(c, tmem, g + j + 2);
-                    if (ok && j + 2 == n - 1) mma_commit(bar(c, B_Q_EMPTY));
+            /* Issue whichever GEMM is ready, GEMM2 first (it frees a page
+             * stage); GEMM1 runs at most two tiles ahead of GEMM2. */
+            uint32_t n1 = 0, n2 = 0;
+            long long t0 = clock64();
+            while (ok && n2 < n) {
+                bool did = false;
+                if (n2 < n1) {
+                    const uint32_t gt = g + n2;
+                    if (mbar_try(bar(c, B_P_FULL + (gt & 1)), (gt >> 1) & 1) &&
+                        (n2 > 0 || mbar_try(bar(c, B_O_FREE), (nchunk & 1) ^ 1))) {
+                        tc_fence_after();
+                        issue_gemm2(c, tmem, gt % kStages, gt & 1, n2 == 0);
+                        mma_commit(bar(c, B_KV_EMPTY + gt % kStages));
+                        mma_commit(bar(c, B_P_EMPTY + (gt & 1)));
+                        mma_commit(bar(c, B_O_READY));
+                        n2++;
+                        did = true;
+                    }
                 }
-                if (ok) ok = mma_gemm2(c, tmem, g + j, j == 0, nchunk);
+                if (n1 < n && n1 <= n2 + 2) {
+                    const uint32_t gt = g + n1;
+                    if (mbar_try(bar(c, B_KV_FULL + gt % kStages), (gt / kStages) & 1) &&
+                        mbar_try(bar(c, B_S_EMPTY + (gt & 1)), ((gt >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        issue_gemm1(c, tmem, gt % kStages, gt & 1);
+                        mma_commit(bar(c, B_S_FULL + (gt & 1)));
+                        if (n1 == n - 1) mma_commit(bar(c, B_Q_EMPTY));
+                        n1++;
+                        did = true;
+                    }
+                }
+                if (did) {
+                    t0 = clock64();
+                } else if (*c.abort) {
+                    ok = false;
+                } else if (clock64() - t0 > kWaitCycles) {
+                    atomicCAS(&g_mla_tc_error, 0, n2 < n1 ? 7 : 5);
+                    *c.abort = 1;
+                    ok = false;
+                }
             }
             if (ok) mma_commit(bar(c, B_O_FINAL));
         }
@@ -509,6 +517,13 @@ __device__ __forceinline__ void warp_arrive(uint32_t b) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(b);
 }
 
+/* Two floats -> packed bf16 pair (lo in the low half), round to nearest even. */
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 /* Swizzled position of 16-byte chunk `c` (0..15) of exchange row `row`. */
 __device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
 
@@ -531,7 +546,7 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
         s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_remote(mapa(bar(c, B_X_EMPTY), c.peer));
+    if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY), c.peer));
     if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL), kXBytes);      /* arm for the next tile */
     /* scaled scores, masked beyond the page's tokens; row maximum over both halves */
     float mx = -INFINITY;
@@ -573,10 +588,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     uint32_t w[16];
     #pragma unroll
     for (int k = 0; k < 16; k++) {
-        const uint16_t lo = ct_f32_to_bf16(exp2f(s[2 * k] - r.m_used));
-        const uint16_t hi = ct_f32_to_bf16(exp2f(s[2 * k + 1] - r.m_used));
-        r.l += ct_bf16_to_f32(lo) + ct_bf16_to_f32(hi);
-        w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+        w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
+        r.l += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
     }
     tmem_st16(tmem + r.lane_base + kTmemP + (t & 1) * 32 + r.half * 16, w);
     /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
@@ -593,6 +606,26 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     tmem_wait_st();
     tc_fence_before();
     warp_arrive(bar(c, B_P_FULL + (t & 1)));
+    return true;
+}
+
+/* Stages global tile gt: this CTA's partial scores to registers (freeing the
+ * score buffer) and to the exchange buffer the bulk copy sends. */
+__device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t gt, float *s) {
+    const uint32_t sb = gt & 1;
+    if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) return false;
+    tc_fence_after();
+    tmem_ld32(tmem + r.lane_base + kTmemS + sb * 64 + r.half * 32, s);
+    tmem_wait_ld();
+    tc_fence_before();
+    warp_arrive(bar(c, B_S_EMPTY + sb));
+    if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) return false;
+    float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
+    #pragma unroll
+    for (int q4 = 0; q4 < 8; q4++)
+        xout[xoff(r.row, r.half * 8 + q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
+    proxy_fence();
+    warp_arrive(bar(c, B_SO_FULL));
     return true;
 }
 
@@ -656,26 +689,35 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
         int32_t prev_ntok = 0;
         uint32_t j = 0;
         do {
-            const uint32_t gt = g + j, sb = gt & 1;
-            /* this CTA's partial scores of tile gt: to registers (freeing the
-             * score buffer) and to the exchange staging buffer */
+            const uint32_t gt = g + j;
             float s_cur[32];
-            if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) { ok = false; break; }
-            tc_fence_after();
-            tmem_ld32(tmem + r.lane_base + kTmemS + sb * 64 + r.half * 32, s_cur);
-            tmem_wait_ld();
-            tc_fence_before();
-            warp_arrive(bar(c, B_S_EMPTY + sb));
-            if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) { ok = false; break; }
-            float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
-            #pragma unroll
-            for (int q4 = 0; q4 < 8; q4++)
-                xout[xoff(r.row, r.half * 8 + q4) >> 4] =
-                    make_float4(s_cur[4 * q4], s_cur[4 * q4 + 1], s_cur[4 * q4 + 2], s_cur[4 * q4 + 3]);
-            proxy_fence();
-            warp_arrive(bar(c, B_SO_FULL));
-            /* the previous tile, whose peer half has had this long to arrive */
-            if (j > 0 && !finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
+            if (j == 0) {
+                if (!stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
+            } else {
+                /* finish tile gt-1 once the peer's half is in, or stage tile
+                 * gt first if its scores are ready sooner */
+                bool finish_first = false;
+                long long t0 = clock64();
+                for (;;) {
+                    bool xr = false, sr = false;
+                    if (lane == 0) {
+                        xr = mbar_try_cluster(bar(c, B_X_FULL), (gt - 1) & 1);
+                        sr = !xr && mbar_try(bar(c, B_S_FULL + (gt & 1)), (gt >> 1) & 1) &&
+                             mbar_try(bar(c, B_SO_EMPTY), (gt & 1) ^ 1);
+                    }
+                    xr = __shfl_sync(0xFFFFFFFFu, xr, 0);
+                    sr = __shfl_sync(0xFFFFFFFFu, sr, 0);
+                    if (xr) { finish_first = true; break; }
+                    if (sr || *c.abort || clock64() - t0 > kWaitCycles) break;   /* the waits below bound the rest */
+                }
+                if (finish_first) {
+                    if (!finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok) ||
+                        !stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
+                } else {
+                    if (!stage_tile(c, tmem, r, gt, s_cur) ||
+                        !finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
+                }
+            }
             #pragma unroll
             for (int i = 0; i < 32; i++) s_prev[i] = s_cur[i];
             prev_ntok = ntok;
