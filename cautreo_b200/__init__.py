@@ -256,7 +256,10 @@ class KvCache:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):   # interpreter shutdown: module globals already cleared
+            pass
 
     def append(self, layer, pos, k, v) -> bool:
         k = np.ascontiguousarray(k, np.float32)
@@ -292,7 +295,10 @@ class PagedKV:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):   # interpreter shutdown: module globals already cleared
+            pass
 
     def set_free_order(self, order):
         order = np.ascontiguousarray(order, np.int32)
@@ -369,7 +375,10 @@ class MlaPlan:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):   # interpreter shutdown: module globals already cleared
+            pass
 
     @property
     def n_chunks(self):
