@@ -9,8 +9,8 @@
  * entry dimension: CTA r owns latent values [256r, 256r+256) and rope values
  * [512+32r, 544+32r).  Per 64-token page ("tile"):
  *   GEMM1  S_r = Q[:, own 288 dims] . KV[:, own 288 dims]^T  (M=128 heads,
- *          N=64 tokens, K=288) -> TMEM, double-buffered.  Q dims [0,128) of
- *          the half are an A operand in TMEM, the other 160 in shared memory;
+ *          N=64 tokens, K=288) -> TMEM, double-buffered.  The 256 latent dims
+ *          of Q are an A operand in TMEM, the 32 rope dims in shared memory;
  *   the two partial S are exchanged: each CTA stages its partial in shared
  *          memory and a bulk copy moves it into the peer's receive buffer
  *          (the SM-to-SM network moves ~20 B/clk this way, twice what
@@ -18,23 +18,25 @@
  *          CTAs, so both run the identical softmax on identical scores;
  *   softmax in the log2 domain with a lazily updated row maximum (O is
  *          rescaled only when a row's maximum grows by more than 2^8);
- *          P = bf16 probabilities, written to TMEM;
+ *          P = bf16 probabilities, written over the tile's scores in TMEM;
  *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
  *          from TMEM, V read MN-major from the same shared-memory page tile.
  * The softmax warps keep one tile in flight: they finish tile j-1 (once the
  * peer's half is in) and stage tile j for the peer in whichever order their
  * inputs arrive, and the MMA warp issues each GEMM as soon as its operands
- * are ready, GEMM1 up to two tiles ahead of GEMM2.
+ * are ready, GEMM1 one tile ahead of GEMM2.  The peer's partial scores land
+ * in one of two receive slots, so the copy of tile j+1 does not wait for
+ * tile j to be consumed.
  *
  * Roles per CTA (352 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
  * each), warps 3-10 finish scores, softmax and epilogue: two threads per
  * head row (TMEM lane), one per 32-token half of a tile.
  *
- * Shared memory (per CTA): Q 40 KB (2 SW128 [128x64] boxes of latent dims
- * [128,256) of the half + 1 SW64 [128x32] rope box), 3 page stages of 36 KB,
- * exchange out / in buffers of 32 KB, a 3 KB row-statistics buffer, barriers.
- * TMEM: S at columns 0/64, P at 128/160, Q at 192, O at 256..511.
+ * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
+ * 36 KB, an exchange out buffer and two in slots of 32 KB, a 3 KB
+ * row-statistics buffer, barriers.  TMEM: S / P at columns 0 and 64, Q at
+ * 128, O at 256..511.
  *
  * Every wait is bounded (about two seconds of clock); on expiry the kernel
  * records an error word, drains its own TMA loads, copies and MMAs, frees
@@ -56,26 +58,25 @@ constexpr int kSoftmaxWarps = 8;
 constexpr int kFirstSoftmaxWarp = 3;
 constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 352 */
 constexpr int kStages = 3;
-constexpr uint32_t kQBytes = 2 * 16384 + 8192;          /* 40,960 */
+constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
 constexpr uint32_t kKvBytes = 4 * 8192 + 4096;          /* 36,864 per stage */
 constexpr uint32_t kXBytes = 32768;                     /* one tile's partial scores, 128 x 64 fp32 */
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffKv = kOffQ + kQBytes;
 constexpr uint32_t kOffOut = kOffKv + kStages * kKvBytes;
-constexpr uint32_t kOffIn = kOffOut + kXBytes;
-constexpr uint32_t kOffRed = kOffIn + kXBytes;
+constexpr uint32_t kOffIn = kOffOut + kXBytes;         /* two receive slots */
+constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
 constexpr uint32_t kRedBytes = 6 * kH * 4;              /* row max [2 parities][2 halves], row sum [2 halves] */
 constexpr uint32_t kOffBar = kOffRed + kRedBytes;
-constexpr uint32_t kNumBars = 32;
+constexpr uint32_t kNumBars = 40;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
 constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
 static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
 static_assert(kOffKv % 1024 == 0 && kOffOut % 1024 == 0 && kOffIn % 1024 == 0, "swizzle atoms need 1 KB alignment");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns, fp32 scores */
-constexpr uint32_t kTmemP = 128;    /* 2 x 32 columns, bf16 probabilities (two per column) */
-constexpr uint32_t kTmemQ = 192;    /* 64 columns, bf16 query latent dims [0,128) of the half */
+constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns: fp32 scores, then bf16 P in the first 32 */
+constexpr uint32_t kTmemQ = 128;    /* 128 columns, bf16 query latent dims of the half */
 constexpr uint32_t kTmemO = 256;    /* 256 columns, fp32 output accumulator */
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -84,9 +85,9 @@ constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
 
 /* barrier slots */
 enum : uint32_t {
-    B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_S_EMPTY = 11,
-    B_P_FULL = 13, B_P_EMPTY = 15, B_O_READY = 17, B_O_FINAL = 18, B_O_FREE = 19, B_SO_FULL = 20, B_SO_EMPTY = 21,
-    B_X_FULL = 22, B_X_EMPTY = 23, B_DRAIN = 24, B_RED = 25, B_RED_L = 27
+    B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_P_FULL = 11,
+    B_O_READY = 13, B_O_FINAL = 14, B_O_FREE = 15, B_SO_FULL = 16, B_SO_EMPTY = 17, B_X_FULL = 18 /* [slot] */,
+    B_X_EMPTY = 20 /* [slot] */, B_DRAIN = 22, B_RED = 23 /* [parity][quad] */, B_RED_L = 31 /* [quad] */
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -117,6 +118,21 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; "
+                 "selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+/* Non-blocking probes (try_wait may suspend the thread for a while when the
+ * phase is incomplete, which stalls a loop that polls several barriers). */
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; "
                  "selp.u32 %0, 1, 0, p; }"
                  : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
@@ -319,7 +335,7 @@ __device__ __forceinline__ uint32_t count_tiles(const ct_mla_chunk_t &ch, const 
 /* ---- warp 0: TMA producer (lane 0 issues) -------------------------------- */
 
 __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_lat, const CUtensorMap *kv_rope,
-                         const CUtensorMap *q_lat, const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
+                         const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
     const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nq = 0;
     bool ok = true;
@@ -329,16 +345,13 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
         it.init(ch, p);
         int32_t pg, ntok;
         if (!it.next(pg, ntok)) continue;               /* nothing readable in this chunk */
-        /* Q dims [128,256) of this CTA's half and its rope dims, once the
-         * previous chunk's GEMM1s are done */
+        /* the rope dims of this CTA's half of Q, once the previous chunk's
+         * GEMM1s are done (the latent dims go to TMEM) */
         if (leader) {
             ok = wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1);
             if (ok) {
                 mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
-                const int qy = ch.seq * kH;
-                for (int b = 0; b < 2; b++)
-                    tma_load_2d(c.s + kOffQ + b * 16384, q_lat, rank * 256 + 128 + b * 64, qy, bar(c, B_Q_FULL));
-                tma_load_2d(c.s + kOffQ + 2 * 16384, q_rope, 512 + rank * 32, qy, bar(c, B_Q_FULL));
+                tma_load_2d(c.s + kOffQ, q_rope, 512 + rank * 32, ch.seq * kH, bar(c, B_Q_FULL));
             }
         }
         ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
@@ -381,28 +394,22 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
 __device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf) {
     const uint32_t q = c.s + kOffQ, kv = c.s + kOffKv + st * kKvBytes;
     const uint32_t d = tmem + kTmemS + sbuf * 64;
-    /* latent dims [0,128) of the half: A from TMEM */
+    /* the 256 latent dims of the half: A from TMEM */
     #pragma unroll
-    for (int i = 0; i < 8; i++)
+    for (int i = 0; i < 16; i++)
         mma_ts(d, tmem + kTmemQ + i * 8, sdesc(kv + (i >> 2) * 8192 + (i & 3) * 32, 1, 64, kSw128), kIdescS,
                i > 0 ? 1u : 0u);
-    /* latent dims [128,256): A from shared memory */
-    #pragma unroll
-    for (int i = 8; i < 16; i++)
-        mma_ss(d, sdesc(q + ((i - 8) >> 2) * 16384 + (i & 3) * 32, 1, 64, kSw128),
-               sdesc(kv + (i >> 2) * 8192 + (i & 3) * 32, 1, 64, kSw128), kIdescS, 1);
-    /* rope dims */
+    /* rope dims: A from shared memory */
     #pragma unroll
     for (int k = 0; k < 2; k++)
-        mma_ss(d, sdesc(q + 2 * 16384 + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64),
-               kIdescS, 1);
+        mma_ss(d, sdesc(q + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64), kIdescS, 1);
 }
 
 __device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t pbuf, bool first) {
     const uint32_t v = c.s + kOffKv + st * kKvBytes;
     #pragma unroll
     for (int k = 0; k < 4; k++)
-        mma_ts(tmem + kTmemO, tmem + kTmemP + pbuf * 32 + k * 8, sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
+        mma_ts(tmem + kTmemO, tmem + kTmemS + pbuf * 64 + k * 8, sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
                (first && k == 0) ? 0u : 1u);
 }
 
@@ -420,28 +427,29 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
                  wait_bar(c, bar(c, B_QT_FULL), nchunk & 1, false, 3);
             tc_fence_after();
             /* Issue whichever GEMM is ready, GEMM2 first (it frees a page
-             * stage); GEMM1 runs at most two tiles ahead of GEMM2. */
+             * stage).  P of tile t sits in the score columns of tile t, so
+             * GEMM1 of tile t+2 (same columns) is issued after GEMM2 of tile
+             * t; tcgen05.mma instructions of one thread execute in issue
+             * order, so GEMM2 has read P before GEMM1 overwrites it. */
             uint32_t n1 = 0, n2 = 0;
             long long t0 = clock64();
             while (ok && n2 < n) {
                 bool did = false;
                 if (n2 < n1) {
                     const uint32_t gt = g + n2;
-                    if (mbar_try(bar(c, B_P_FULL + (gt & 1)), (gt >> 1) & 1) &&
-                        (n2 > 0 || mbar_try(bar(c, B_O_FREE), (nchunk & 1) ^ 1))) {
+                    if (mbar_test(bar(c, B_P_FULL + (gt & 1)), (gt >> 1) & 1) &&
+                        (n2 > 0 || mbar_test(bar(c, B_O_FREE), (nchunk & 1) ^ 1))) {
                         tc_fence_after();
                         issue_gemm2(c, tmem, gt % kStages, gt & 1, n2 == 0);
                         mma_commit(bar(c, B_KV_EMPTY + gt % kStages));
-                        mma_commit(bar(c, B_P_EMPTY + (gt & 1)));
                         mma_commit(bar(c, B_O_READY));
                         n2++;
                         did = true;
                     }
                 }
-                if (n1 < n && n1 <= n2 + 2) {
+                if (n1 < n && n1 <= n2 + 1) {
                     const uint32_t gt = g + n1;
-                    if (mbar_try(bar(c, B_KV_FULL + gt % kStages), (gt / kStages) & 1) &&
-                        mbar_try(bar(c, B_S_EMPTY + (gt & 1)), ((gt >> 1) & 1) ^ 1)) {
+                    if (mbar_test(bar(c, B_KV_FULL + gt % kStages), (gt / kStages) & 1)) {
                         tc_fence_after();
                         issue_gemm1(c, tmem, gt % kStages, gt & 1);
                         mma_commit(bar(c, B_S_FULL + (gt & 1)));
@@ -478,7 +486,7 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
 __device__ void exchanger(const Ctx &c, const Params &p, int wbeg, int wend) {
     const bool leader = (threadIdx.x & 31) == 0;
     const uint32_t in_peer = mapa(c.s + kOffIn, c.peer);
-    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
+    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);      /* slot b's barrier is 8 b bytes on */
     uint32_t t = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
@@ -487,11 +495,11 @@ __device__ void exchanger(const Ctx &c, const Params &p, int wbeg, int wend) {
         for (uint32_t j = 0; j < n && ok; j++, t++) {
             if (leader) {
                 /* this tile's partial scores are staged, and the peer has
-                 * consumed the previous tile's from its receive buffer */
+                 * consumed tile t-2 from receive slot t & 1 */
                 ok = wait_bar(c, bar(c, B_SO_FULL), t & 1, false, 14) &&
-                     wait_bar(c, bar(c, B_X_EMPTY), (t & 1) ^ 1, true, 15);
+                     wait_bar(c, bar(c, B_X_EMPTY + (t & 1)), ((t >> 1) & 1) ^ 1, true, 15);
                 if (ok) {
-                    bulk_copy_to_peer(in_peer, c.s + kOffOut, kXBytes, xf_peer);
+                    bulk_copy_to_peer(in_peer + (t & 1) * kXBytes, c.s + kOffOut, kXBytes, xf_peer + (t & 1) * 8);
                     bulk_wait_read();
                     mbar_arrive(bar(c, B_SO_EMPTY));
                 }
@@ -528,7 +536,7 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
 __device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
 
 struct Row {
-    uint32_t row, half, lane_base, tid;
+    uint32_t row, half, quad, lane_base, tid;
     float m_used, l;
 };
 
@@ -538,31 +546,37 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
                             int32_t ntok) {
     const uint32_t lane = threadIdx.x & 31;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
-    if (!wait_warp(c, bar(c, B_X_FULL), t & 1, true, 10)) return false;
-    const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn);
+    const uint32_t slot = t & 1;
+    if (!wait_warp(c, bar(c, B_X_FULL + slot), (t >> 1) & 1, true, 10)) return false;
+    const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn + slot * kXBytes);
     #pragma unroll
     for (int q4 = 0; q4 < 8; q4++) {
         const float4 w = xin[xoff(r.row, r.half * 8 + q4) >> 4];
         s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY), c.peer));
-    if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL), kXBytes);      /* arm for the next tile */
+    if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY + slot), c.peer));
+    if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL + slot), kXBytes);   /* arm for tile t + 2 */
     /* scaled scores, masked beyond the page's tokens; row maximum over both halves */
-    float mx = -INFINITY;
+    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     #pragma unroll
     for (int i = 0; i < 32; i++) {
         s[i] = ((int32_t)(r.half * 32 + i) < ntok) ? s[i] * p.qk_scale : -INFINITY;
-        mx = fmaxf(mx, s[i]);
+        m4[i & 3] = fmaxf(m4[i & 3], s[i]);
     }
+    float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    /* the other half of each row is in the partner warp of this quadrant */
     float *rm = red + (t & 1) * 2 * kH;
     rm[r.half * kH + r.row] = mx;
-    warp_arrive(bar(c, B_RED + (t & 1)));
-    if (!wait_warp(c, bar(c, B_RED + (t & 1)), (t >> 1) & 1, false, 16)) return false;
+    const uint32_t rb = bar(c, B_RED + (t & 1) * 4 + r.quad);
+    tc_fence_before();      /* the partner half writes P over scores this thread has read */
+    warp_arrive(rb);
+    if (!wait_warp(c, rb, (t >> 1) & 1, false, 16)) return false;
+    tc_fence_after();
     mx = fmaxf(mx, rm[(r.half ^ 1) * kH + r.row]);
     const bool grow = mx > r.m_used + kRescaleThreshold;   /* also true for the first tile */
     const float m_new = grow ? mx : r.m_used;
-    const float alpha = exp2f(r.m_used - m_new);            /* 0 on the first tile, 1 if unchanged */
+    const float alpha = grow ? exp2f(r.m_used - m_new) : 1.0f;   /* 0 on the first tile */
     if (__any_sync(0xFFFFFFFFu, grow && jj > 0)) {
         /* O holds tiles before t: wait for GEMM2(t-1), rescale this thread's half row */
         if (!wait_warp(c, bar(c, B_O_READY), (t - 1) & 1, false, 11)) return false;
@@ -583,15 +597,18 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     }
     r.l *= alpha;
     r.m_used = m_new;
-    /* P = bf16(2^(s - m)) into TMEM: 32 tokens = 16 columns of this half */
-    if (!wait_warp(c, bar(c, B_P_EMPTY + (t & 1)), ((t >> 1) & 1) ^ 1, false, 12)) return false;
+    /* P = bf16(2^(s - m)) into the first 32 score columns of tile t (this
+     * thread read its scores in stage_tile; GEMM2 of tile t-2, which read
+     * the previous P there, completed before GEMM1 of tile t did) */
     uint32_t w[16];
+    float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     #pragma unroll
     for (int k = 0; k < 16; k++) {
         w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
-        r.l += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
+        l4[k & 3] += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
     }
-    tmem_st16(tmem + r.lane_base + kTmemP + (t & 1) * 32 + r.half * 16, w);
+    r.l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+    tmem_st16(tmem + r.lane_base + kTmemS + (t & 1) * 64 + r.half * 16, w);
     /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
     if (ntok < kP) {
         uint8_t *kvs = c.smem + kOffKv + (t % kStages) * kKvBytes;
@@ -609,16 +626,14 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     return true;
 }
 
-/* Stages global tile gt: this CTA's partial scores to registers (freeing the
- * score buffer) and to the exchange buffer the bulk copy sends. */
+/* Stages global tile gt: this CTA's partial scores to registers and to the
+ * exchange buffer the bulk copy sends. */
 __device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t gt, float *s) {
     const uint32_t sb = gt & 1;
     if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) return false;
     tc_fence_after();
     tmem_ld32(tmem + r.lane_base + kTmemS + sb * 64 + r.half * 32, s);
     tmem_wait_ld();
-    tc_fence_before();
-    warp_arrive(bar(c, B_S_EMPTY + sb));
     if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) return false;
     float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
     #pragma unroll
@@ -635,6 +650,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     Row r;
     r.half = (warp - kFirstSoftmaxWarp) >> 2;           /* tokens [32h, 32h+32) of a tile, O columns [128h, +128) */
     r.row = quad * 32 + lane;                           /* head */
+    r.quad = quad;
     r.lane_base = (quad * 32) << 16;
     r.tid = (warp - kFirstSoftmaxWarp) * 32 + lane;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
@@ -666,21 +682,22 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             }
             continue;
         }
-        /* Q latent dims [0,128) of this CTA's half into TMEM, once the
-         * previous chunk's GEMM1s are done: this thread's 64 dims */
+        /* the latent dims of this CTA's half of Q into TMEM, once the
+         * previous chunk's GEMM1s are done: this thread's 128 dims */
         if (!wait_warp(c, bar(c, B_Q_EMPTY), (nchunk & 1) ^ 1, false, 17)) { ok = false; break; }
         tc_fence_after();
-        {
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.half * 64);
+        #pragma unroll 1
+        for (int part = 0; part < 2; part++) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.half * 128 + part * 64);
             uint32_t u[32];
             #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const uint4 v = __ldg(src + k);
                 u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
             }
-            tmem_st32(tmem + r.lane_base + kTmemQ + r.half * 32, u);
-            tmem_wait_st();
+            tmem_st32(tmem + r.lane_base + kTmemQ + r.half * 64 + part * 32, u);
         }
+        tmem_wait_st();
         tc_fence_before();
         warp_arrive(bar(c, B_QT_FULL));
         r.m_used = -INFINITY;
@@ -701,9 +718,9 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                 for (;;) {
                     bool xr = false, sr = false;
                     if (lane == 0) {
-                        xr = mbar_try_cluster(bar(c, B_X_FULL), (gt - 1) & 1);
-                        sr = !xr && mbar_try(bar(c, B_S_FULL + (gt & 1)), (gt >> 1) & 1) &&
-                             mbar_try(bar(c, B_SO_EMPTY), (gt & 1) ^ 1);
+                        xr = mbar_test_cluster(bar(c, B_X_FULL + ((gt - 1) & 1)), ((gt - 1) >> 1) & 1);
+                        sr = !xr && mbar_test(bar(c, B_S_FULL + (gt & 1)), (gt >> 1) & 1) &&
+                             mbar_test(bar(c, B_SO_EMPTY), (gt & 1) ^ 1);
                     }
                     xr = __shfl_sync(0xFFFFFFFFu, xr, 0);
                     sr = __shfl_sync(0xFFFFFFFFu, sr, 0);
@@ -729,8 +746,8 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
         /* epilogue: the row sum over both halves, then O of this CTA's 256 value dims */
         float *rl = red + 4 * kH;
         rl[r.half * kH + r.row] = r.l;
-        warp_arrive(bar(c, B_RED_L));
-        if (!wait_warp(c, bar(c, B_RED_L), nchunk & 1, false, 18)) { ok = false; break; }
+        warp_arrive(bar(c, B_RED_L + r.quad));
+        if (!wait_warp(c, bar(c, B_RED_L + r.quad), nchunk & 1, false, 18)) { ok = false; break; }
         const float l_tot = r.l + rl[(r.half ^ 1) * kH + r.row];
         if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
         tc_fence_after();
@@ -777,7 +794,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     k_mla_tc(const __grid_constant__ CUtensorMap kv_lat, const __grid_constant__ CUtensorMap kv_rope,
-             const __grid_constant__ CUtensorMap q_lat, const __grid_constant__ CUtensorMap q_rope, Params p) {
+             const __grid_constant__ CUtensorMap q_rope, Params p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
     const uint32_t raw = smem_addr(smem_raw);
@@ -801,18 +818,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1); mbar_init(bar(c, B_QT_FULL), kSoftmaxWarps);
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(c, B_S_FULL + i), 1);
-            mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps);
             mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
-            mbar_init(bar(c, B_P_EMPTY + i), 1);
-            mbar_init(bar(c, B_RED + i), kSoftmaxWarps);
+            mbar_init(bar(c, B_X_FULL + i), 1);
+            mbar_init(bar(c, B_X_EMPTY + i), kSoftmaxWarps);
         }
+        for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), 2);      /* the two warps of a quadrant */
+        for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), 2);
         mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
         mbar_init(bar(c, B_SO_FULL), kSoftmaxWarps); mbar_init(bar(c, B_SO_EMPTY), 1);
-        mbar_init(bar(c, B_X_FULL), 1); mbar_init(bar(c, B_X_EMPTY), kSoftmaxWarps);
-        mbar_init(bar(c, B_DRAIN), 1); mbar_init(bar(c, B_RED_L), kSoftmaxWarps);
+        mbar_init(bar(c, B_DRAIN), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        mbar_expect_tx(bar(c, B_X_FULL), kXBytes);   /* armed for the first tile */
+        mbar_expect_tx(bar(c, B_X_FULL + 0), kXBytes);   /* armed for the first two tiles */
+        mbar_expect_tx(bar(c, B_X_FULL + 1), kXBytes);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -826,7 +844,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
 
     if (warp == 0) {
-        producer(c, p, &kv_lat, &kv_rope, &q_lat, &q_rope, wbeg, wend, rank);
+        producer(c, p, &kv_lat, &kv_rope, &q_rope, wbeg, wend, rank);
     } else if (warp == 1) {
         mma_issuer(c, p, tmem, wbeg, wend);
     } else if (warp == 2) {
@@ -936,13 +954,12 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     if (((uintptr_t)pool & 15u) || ((uintptr_t)q & 15u) || ((uintptr_t)out & 15u)) return CT_ERR_UNSUPPORTED;
     /* Maps cover exactly the pool and q: a page id beyond the pool reads
      * zeros (TMA out-of-bounds fill) rather than foreign memory. */
-    CUtensorMap kv_lat, kv_rope, q_lat, q_rope;
+    CUtensorMap kv_lat, kv_rope, q_rope;
     if (dims->n_pages == 0 || dims->n_seq == 0) return CT_ERR_ARG;
     const uint64_t pool_rows = (uint64_t)dims->n_pages * kP;
     const uint64_t q_rows = (uint64_t)dims->n_seq * kH;
     if (!make_map(&kv_lat, pool, pool_rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map(&kv_rope, pool, pool_rows, 32, 64, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&q_lat, q, q_rows, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map(&q_rope, q, q_rows, 32, 128, CU_TENSOR_MAP_SWIZZLE_64B)) {
         ct__set_error("mla_tc: cuTensorMapEncodeTiled failed");
         return CT_ERR_CUDA;
@@ -967,6 +984,6 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
         if (rc) return rc;
         attr_set = true;
     }
-    k_mla_tc<<<2 * n_workers, kThreads, kSmemAlloc, (cudaStream_t)stream>>>(kv_lat, kv_rope, q_lat, q_rope, p);
+    k_mla_tc<<<2 * n_workers, kThreads, kSmemAlloc, (cudaStream_t)stream>>>(kv_lat, kv_rope, q_rope, p);
     return ct__cuda_status(cudaGetLastError(), "mla_tc launch");
 }
