@@ -284,7 +284,10 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- reduce over ranks ----
     import torch.distributed as dist
-    vals = torch.tensor([ms, e2e_ms, dec_ms, app_ms, tokens, float(launches), float(n)], dtype=torch.float64,
+    # this GPU's decode: algorithmic bytes over its own mean launch time
+    my_bytes = tokens * BYTES_PER_TOKEN + n * H * E * 2 + n * H * DV * 2
+    my_gbs = my_bytes / (dec_ms * 1e-3) / 1e9
+    vals = torch.tensor([ms, e2e_ms, dec_ms, app_ms, tokens, float(launches), float(n), my_gbs], dtype=torch.float64,
                         device="cuda")
     if world > 1:
         mx = vals.clone()
@@ -296,30 +299,27 @@ def run_ours(args, rank, world, local_rank):
     ms_max, e2e_max, dec_max = float(mx[0]), float(mx[1]), float(mx[2])
     tok_total = float(sm[4])
     launches_total = int(sm[5])
+    gbs_mean = float(sm[7]) / world                     # per-GPU achieved GB/s, mean over ranks
+    tok_rank0 = tokens
 
     # ---- the one exchange: gather outputs to rank 0 (timed separately) ----
     gather_ms = None
     if world > 1:
-        n_max = int(mx[6])
-        pad = torch.zeros(n_max * H * DV, dtype=torch.int16, device="cuda")
-        pad[:n * H * DV] = out
-        gl = [torch.empty_like(pad) for _ in range(world)] if rank == 0 else None
+        from cautreo_b200.shard import gather_rows
+        gather_rows(out.view(n, H * DV), rank_of, rank, world)    # first collective sets up the communicator
         torch.cuda.synchronize()
         g0 = time.perf_counter()
-        dist.gather(pad, gl, dst=0)
+        full = gather_rows(out.view(n, H * DV), rank_of, rank, world)
         torch.cuda.synchronize()
         gather_ms = (time.perf_counter() - g0) * 1e3
-        if rank == 0:
-            full = torch.empty((n_all, H * DV), dtype=torch.int16, device="cuda")
-            for r in range(world):
-                ids = np.nonzero(rank_of == r)[0]
-                full[torch.from_numpy(ids).cuda()] = gl[r].view(n_max, H * DV)[:len(ids)]
 
     if rank != 0:
         return None
     hbm, hbm_kind = measured_hbm()
-    bytes_dec = tok_total * BYTES_PER_TOKEN + n_all * H * E * 2 + n_all * H * DV * 2
-    achieved = bytes_dec / (dec_max * 1e-3) / 1e9
+    achieved = gbs_mean             # per GPU: its own bytes over its own decode time, averaged over ranks
+    traffic = committed_traffic(args.workload)
+    if traffic is not None and world > 1:
+        traffic = traffic * tok_rank0 / tok_total      # rank 0's launch: the one-GPU capture scaled by its tokens
     value = tok_total * args.steps / (ms_max * 1e-3)
     line = {
         "metric": METRIC,
@@ -346,7 +346,7 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": int(n_all * H * DV * 2),
                 "path": "ct_attn_mla_decode_step_host (pinned host q/new tokens in, outputs out)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": committed_traffic(args.workload), "peak_kind": hbm_kind,
+                     "traffic": traffic, "peak_kind": hbm_kind, "per": "GPU (mean over ranks)",
                      "kernel": "MLA decode + split-KV combine (one ct_attn_mla_decode_paged call)",
                      "decode_ms": dec_max, "append_ms": float(mx[3])},
         "clocks": clk,
@@ -466,7 +466,7 @@ def main():
     from datetime import timedelta
     if world > 1:
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:
         line = run_ours(args, rank, world, local_rank)
         if line is not None and world == 1 and not args.no_cpu_baseline:
