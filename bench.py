@@ -439,18 +439,290 @@ def run_reference(args):
             "e2e": {"value": value, "unit": "KV tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# secondary workloads (one JSON line each; the default line above is the
+# headline): plain decode, quantised pools, eviction + compaction
+# ---------------------------------------------------------------------------
+
+def _events(torch, n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def run_plain(args):
+    """4 layers x 8 heads x 64 fp32 contiguous cache, batch 1: 256 steps of
+    (append one token to every layer, attend over the whole cache), captured
+    in one CUDA graph.  The cache (4 MiB) stays in L2."""
+    import torch
+    import cautreo_b200 as ct
+    L_, Hh, D, steps = 4, 8, 64, 256
+    L = ct.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    n = steps * L_ * Hh * D
+    q, k, v = (torch.empty(n, dtype=torch.float32, device="cuda") for _ in range(3))
+    for i, t in enumerate((q, k, v)):
+        ct.check(L.ct_synth_fill(t.data_ptr(), 1, ct.synth_key(0, i), 0, n, 0, 1.0, sp))
+    kc = torch.zeros(L_ * steps * Hh * D, dtype=torch.float32, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    row = L_ * Hh * D
+
+    def run_all():
+        for s in range(steps):
+            ct.check(L.ct_attn_decode_step_contig(q.data_ptr() + 4 * s * row, k.data_ptr() + 4 * s * row,
+                                                  v.data_ptr() + 4 * s * row, kc.data_ptr(), vc.data_ptr(), L_,
+                                                  steps, Hh, Hh, D, s, 0.0, out.data_ptr() + 4 * s * row, sp))
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        run_all()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        run_all()
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = _events(torch, 2)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps                  # one 256-step run
+    tokens = L_ * steps * (steps + 1) // 2                  # KV positions read (all heads), per run
+    kv_bytes = tokens * Hh * D * 4 * 2
+    line = {"metric": "plain decode KV tokens/s (4 layers x 8 heads x 64 fp32, batch 1, 256 steps)",
+            "value": tokens / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "us_per_decode_step": ms * 1e3 / steps,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic (seed 0)",
+            "config": {"workload": "plain contiguous KV decode: 4 layers, 8 heads, head_dim 64, fp32, batch 1, "
+                                   "256 append+attend steps in one CUDA graph (a bench step = the 256-step run)"},
+            "gpu_launches": steps * args.steps,
+            "roofline": {"bound": "l2", "achieved": kv_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+                         "note": "the whole cache (4 MiB) is L2-resident; an HBM fraction is not meaningful"}}
+    if not args.no_cpu_baseline:
+        try:
+            import oracle
+            if oracle.ref_available():
+                line["cpu_baseline"] = _plain_reference(oracle, q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(),
+                                                        L_, Hh, D, steps, tokens)
+        except Exception as e:  # pragma: no cover
+            line["cpu_baseline"] = {"value": None, "error": str(e)}
+    return line
+
+
+def _plain_reference(oracle, q, k, v, L_, Hh, D, steps, tokens):
+    """The reference CPU path timed on this host: ct_kv_append for every
+    layer, then per layer and head ct_kv_get of that head's rows and
+    ct_attn_forward (the engine's loop), one thread."""
+    import ctypes as C
+    R = oracle.ref()
+    row = L_ * Hh * D
+    q, k, v = q.reshape(steps, L_, Hh * D), k.reshape(steps, L_, Hh * D), v.reshape(steps, L_, Hh * D)
+    cfg = oracle.KvConfig(L_, Hh, D, steps, 1.0)
+    c = R.ct_kv_create(C.byref(cfg))
+    krow = np.empty(Hh * D, np.float32)
+    vrow = np.empty(Hh * D, np.float32)
+    kh = np.empty((steps, D), np.float32)
+    vh = np.empty((steps, D), np.float32)
+    out = np.empty(D, np.float32)
+    t0 = time.perf_counter()
+    try:
+        for s in range(steps):
+            for l in range(L_):
+                R.ct_kv_append(c, l, s, k[s, l].ctypes.data, v[s, l].ctypes.data)
+            for l in range(L_):
+                for t in range(s + 1):
+                    R.ct_kv_get(c, l, t, krow.ctypes.data, vrow.ctypes.data)
+                    kh[t] = krow.reshape(Hh, D)[0]
+                    vh[t] = vrow.reshape(Hh, D)[0]
+                for h in range(Hh):
+                    R.ct_attn_forward(q[s, l, h * D:(h + 1) * D].ctypes.data, kh.ctypes.data, vh.ctypes.data,
+                                      s + 1, 1, D, 0.0, out.ctypes.data)
+    finally:
+        R.ct_kv_destroy(c)
+    el = time.perf_counter() - t0
+    return {"value": tokens / el, "unit": "KV tokens/s", "cores": 1, "kind": "reference",
+            "sample": "the whole 256-step run through the reference ct_kv_append / ct_kv_get / ct_attn_forward "
+                      "(head 0's rows gathered once per layer and step and reused for every head)"}
+
+
+def run_quant(args):
+    """64 sequences x 8192 tokens of MLA entries (N(0,1), 1 % x20 outliers) in
+    int8 and fp8-e4m3 pools with one fp32 scale per token: quantise-on-append,
+    dequantise-on-gather and decode over the quantised pages."""
+    import torch
+    import cautreo_b200 as ct
+    L = ct.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    B, T = 64, 8192
+    n_tok = B * T
+    pages_per = T // PAGE
+    n_pages = B * pages_per
+    src = torch.empty(n_tok * E, dtype=torch.int16, device="cuda")
+    ct.check(L.ct_synth_fill(src.data_ptr(), 0, ct.synth_key(2, 10), 0, n_tok * E, 100, 20.0, sp))
+    perm = np.random.default_rng(2).permutation(n_pages).astype(np.int32)
+    q = torch.empty(B * H * E, dtype=torch.int16, device="cuda")
+    ct.check(L.ct_synth_fill(q.data_ptr(), 0, ct.synth_key(2, 11), 0, B * H * E, 0, 1.0, sp))
+    out = torch.empty(B * H * DV, dtype=torch.int16, device="cuda")
+    gat = torch.empty(T * E, dtype=torch.int16, device="cuda")
+    hbm, hbm_kind = measured_hbm()
+    res = {}
+    for name, dt in (("int8", ct.CT_KV_INT8), ("e4m3", ct.CT_KV_E4M3)):
+        kv = ct.PagedKV(B, pages_per, n_pages, PAGE, E, 0, dt, 0, sp)
+        kv.set_free_order(perm)
+        kv.append(list(range(B)), [T] * B, None)             # every slot reserved, pages permuted
+        bt = kv.block_table()
+        dest = (bt[:, :, None] * PAGE + np.arange(PAGE)[None, None, :]).reshape(-1).astype(np.int32)
+        dest_dev = torch.from_numpy(dest).cuda()
+
+        def append():
+            ct.check(L.ct_kv_paged_write_slots(kv.pool, kv.scales, dt, src.data_ptr(), ct.CT_KV_BF16,
+                                               dest_dev.data_ptr(), n_tok, E, sp))
+
+        def gather():
+            for s in range(B):
+                ct.check(L.ct_kv_paged_gather(kv.h, s, 0, T, gat.data_ptr(), ct.CT_KV_BF16))
+
+        plan = ct.MlaPlan(np.full(B, T, np.int32), n_pages, kv_dtype=dt, max_pages_per_seq=pages_per)
+
+        def decode():
+            plan.decode(q.data_ptr(), kv.pool, kv.scales, kv.block_table_dev, kv.seq_lens_dev, out.data_ptr(), None,
+                        sp)
+
+        r = {}
+        for what, fn, reps in (("append", append, args.steps), ("gather", gather, args.steps),
+                               ("decode", decode, max(1, args.steps // 4))):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = _events(torch, 2)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            r[what] = e0.elapsed_time(e1) / reps
+        code_bytes = n_tok * (E + 4)
+        res[name] = {
+            "append_ms": r["append"], "append_gbs": (n_tok * E * 2 + code_bytes) / (r["append"] * 1e-3) / 1e9,
+            "gather_ms": r["gather"], "gather_gbs": (code_bytes + n_tok * E * 2) / (r["gather"] * 1e-3) / 1e9,
+            "decode_ms": r["decode"], "decode_tokens_s": n_tok / (r["decode"] * 1e-3),
+            "decode_kernel": "tensor cores" if plan.tensor_cores else "CUDA cores",
+        }
+        res[name]["append_frac"] = res[name]["append_gbs"] / hbm
+        res[name]["gather_frac"] = res[name]["gather_gbs"] / hbm
+        plan.close()
+        kv.close()
+    line = {"metric": "quantised paged KV: append / gather GB/s and decode KV tokens/s", "value": res["int8"]["append_gbs"],
+            "unit": "GB/s (int8 quantise-on-append)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "int8 / e4m3 codes + fp32 per-token scale", "data": "synthetic (seed 2)",
+            "config": {"workload": "64 seqs x 8192 tokens, 576-value MLA entries N(0,1) with 1 % x20 outliers, "
+                                   "64-token pages randomly permuted; append = one write of every token from bf16, "
+                                   "gather = every sequence to contiguous bf16, decode = 128 heads over all pages",
+                       "l2": "inputs larger than L2 (302 MB codes, 604 MB bf16); no flush"},
+            "roofline": {"bound": "hbm", "achieved": res["int8"]["append_gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": res["int8"]["append_frac"], "peak_kind": hbm_kind,
+                         "kernel": "k_write_slots (bf16 -> int8 + scale)"},
+            "paths": res}
+    return line
+
+
+def run_evict(args):
+    """256 sequences, lengths log-uniform 512..32768 (seed 3), 64-token bf16
+    MLA pages in a pool of 60 % of the demand, 4096-token sliding window with
+    LRU eviction under pressure: every token appended in rounds through the
+    allocator, then a defragmenting compaction."""
+    import torch
+    import cautreo_b200 as ct
+    L = ct.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    lens = lengths_loguniform(256, 512, 32768, seed=3)
+    demand = int(((lens + PAGE - 1) // PAGE).sum())
+    n_pages = int(0.6 * demand)
+    max_pages = int((lens.max() + PAGE - 1) // PAGE)
+    n_tok = int(lens.sum())
+    src = torch.empty(n_tok * E, dtype=torch.int16, device="cuda")
+    ct.check(L.ct_synth_fill(src.data_ptr(), 0, ct.synth_key(3, 10), 0, n_tok * E, 0, 1.0, sp))
+    torch.cuda.synchronize()
+    app, comp, whole, moved = [], [], [], []
+    warm, reps = 1, max(2, args.steps // 5)            # each repetition rebuilds the cache from scratch
+    for it in range(warm + reps):
+        kv = ct.PagedKV(256, max_pages, n_pages, PAGE, E, 4096, ct.CT_KV_BF16, 0, sp)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        kv.append(list(range(256)), lens.tolist(), src.data_ptr())
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        # the compaction gather alone: live pages in (seq, lpage) order into a spare buffer
+        bt = kv.block_table()
+        live = bt[bt >= 0].astype(np.int32)               # row-major = (seq, lpage) order
+        map_dev = torch.from_numpy(live).cuda()
+        spare = torch.empty(len(live) * PAGE * E, dtype=torch.int16, device="cuda")
+        e0, e1 = _events(torch, 2)
+        e0.record(stream)
+        ct.check(L.ct_kv_paged_move_pages(kv.pool, None, spare.data_ptr(), None, map_dev.data_ptr(), len(live),
+                                          PAGE * E * 2, PAGE, sp))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del spare
+        # the whole call: renumbering, upload, gather into a fresh pool, table update
+        t2 = time.perf_counter()
+        ct.check(L.ct_kv_paged_compact(kv.h))
+        torch.cuda.synchronize()
+        t3 = time.perf_counter()
+        st = kv.stats()
+        if it >= warm:
+            app.append(t1 - t0)
+            comp.append(e0.elapsed_time(e1))
+            whole.append((t3 - t2) * 1e3)
+            moved.append(st.bytes_compacted)
+        stats = st
+        kv.close()
+    hbm, hbm_kind = measured_hbm()
+    comp_ms = float(np.mean(comp))
+    comp_gbs = float(np.mean(moved)) / (comp_ms * 1e-3) / 1e9     # bytes_compacted counts read + write
+    return {"metric": "eviction + compaction: compaction GB/s and append tokens/s through the allocator",
+            "value": comp_gbs, "unit": "GB/s (compaction, read + write)", "n_gpus": 1, "steps": reps,
+            "warmup": warm, "higher_is_better": True, "dtype": "bf16 pages", "data": "synthetic (seed 3)",
+            "config": {"workload": f"256 seqs, lengths log-uniform 512..32768 (seed 3, {n_tok} tokens, {demand} pages "
+                                   f"demanded), pool {n_pages} pages (60 %), window 4096, LRU under pressure, then "
+                                   f"compaction"},
+            "append_s": float(np.mean(app)), "append_tokens_s": n_tok / float(np.mean(app)),
+            "compact_kernel_ms": comp_ms, "compact_call_ms": float(np.mean(whole)),
+            "bytes_compacted": int(np.mean(moved)),
+            "evictions": {"window": int(stats.n_evict_window), "lru": int(stats.n_evict_lru),
+                          "live_pages": int(stats.n_pages_live)},
+            "roofline": {"bound": "hbm", "achieved": comp_gbs, "peak": hbm, "unit": "GB/s", "frac": comp_gbs / hbm,
+                         "peak_kind": hbm_kind, "kernel": "k_move_pages (compaction gather)"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sharded", choices=["sharded", "mla32"])
+    ap.add_argument("--workload", default="sharded", choices=["sharded", "mla32", "plain", "quant", "evict"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+
+    if args.workload in ("plain", "quant", "evict"):
+        if int(os.environ.get("RANK", "0")) != 0 or args.impl == "reference":
+            return 0          # one-GPU measurements of the other configurations
+        line = {"plain": run_plain, "quant": run_quant, "evict": run_evict}[args.workload](args)
+        print(json.dumps(line), flush=True)
+        return 0
 
     if args.impl == "reference":
         line = run_reference(args)

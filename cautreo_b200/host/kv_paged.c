@@ -45,6 +45,7 @@ struct ct_kv_paged {
     /* device */
     void *pool;
     float *scales;
+    int pool_async;             /* pool / scales came from cudaMallocAsync (a compaction) */
     int32_t *bt_dev;
     int32_t *len_dev;
     int32_t *stage_dev;         /* staged dest slots + (index, value) pairs */
@@ -172,6 +173,7 @@ void ct_kv_paged_destroy(ct_kv_paged_t *h) {
     if (!h) return;
     if (!h->host_only) {
         if (h->stage_pending) cudaEventSynchronize(h->stage_ev);
+        cudaStreamSynchronize(h->stream);         /* no access to the buffers may be in flight */
         if (h->stage_ev) cudaEventDestroy(h->stage_ev);
         cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->bt_dev); cudaFree(h->len_dev); cudaFree(h->stage_dev);
         if (h->stage_host) cudaFreeHost(h->stage_host);
@@ -465,8 +467,12 @@ int ct_kv_paged_compact(ct_kv_paged_t *h) {
     if (h->host_only) goto renumbered;
     void *new_pool = NULL;
     float *new_scales = NULL;
-    rc = ct__cuda_status(cudaMalloc(&new_pool, (size_t)NP * h->page_bytes), "compact pool");
-    if (!rc && h->scales) rc = ct__cuda_status(cudaMalloc((void **)&new_scales, (size_t)NP * P * sizeof(float)), "compact scales");
+    /* stream-ordered allocations: after the first compaction the pool's
+     * memory comes back from the driver's cache without a device sync */
+    rc = ct__cuda_status(cudaMallocAsync(&new_pool, (size_t)NP * h->page_bytes, h->stream), "compact pool");
+    if (!rc && h->scales)
+        rc = ct__cuda_status(cudaMallocAsync((void **)&new_scales, (size_t)NP * P * sizeof(float), h->stream),
+                             "compact scales");
     if (!rc && new_scales) rc = ct__cuda_status(cudaMemsetAsync(new_scales, 0, (size_t)NP * P * sizeof(float), h->stream), "compact");
     /* bt image follows the map in the staging buffer */
     memcpy(map + n_live, h->bt, (size_t)S * MP * sizeof(int32_t));
@@ -476,10 +482,24 @@ int ct_kv_paged_compact(ct_kv_paged_t *h) {
                                          h->page_bytes, P, h->stream);
     if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(h->bt_dev, h->stage_dev + n_live, (size_t)S * MP * sizeof(int32_t),
                                                   cudaMemcpyDeviceToDevice, h->stream), "compact bt");
-    if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(h->stream), "compact sync");
-    if (rc) { cudaFree(new_pool); cudaFree(new_scales); return rc; }
-    cudaFree(h->pool);
-    cudaFree(h->scales);
+    if (rc) {
+        if (new_pool) cudaFreeAsync(new_pool, h->stream);
+        if (new_scales) cudaFreeAsync(new_scales, h->stream);
+        cudaStreamSynchronize(h->stream);
+        return rc;
+    }
+    if (h->pool_async) {                          /* from an earlier compaction: back to the cache */
+        cudaFreeAsync(h->pool, h->stream);
+        if (h->scales) cudaFreeAsync(h->scales, h->stream);
+    }
+    /* the staging buffer is reused by the next call on the host */
+    rc = ct__cuda_status(cudaStreamSynchronize(h->stream), "compact sync");
+    if (rc) return rc;
+    if (!h->pool_async) {                         /* the create-time buffers */
+        cudaFree(h->pool);
+        cudaFree(h->scales);
+    }
+    h->pool_async = 1;
     h->pool = new_pool;
     h->scales = new_scales;
 renumbered:
