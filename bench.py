@@ -570,7 +570,7 @@ def run_quant(args):
     q = torch.empty(B * H * E, dtype=torch.int16, device="cuda")
     ct.check(L.ct_synth_fill(q.data_ptr(), 0, ct.synth_key(2, 11), 0, B * H * E, 0, 1.0, sp))
     out = torch.empty(B * H * DV, dtype=torch.int16, device="cuda")
-    gat = torch.empty(T * E, dtype=torch.int16, device="cuda")
+    gat = torch.empty(n_tok * E, dtype=torch.int16, device="cuda")
     hbm, hbm_kind = measured_hbm()
     res = {}
     for name, dt in (("int8", ct.CT_KV_INT8), ("e4m3", ct.CT_KV_E4M3)):
@@ -585,9 +585,13 @@ def run_quant(args):
             ct.check(L.ct_kv_paged_write_slots(kv.pool, kv.scales, dt, src.data_ptr(), ct.CT_KV_BF16,
                                                dest_dev.data_ptr(), n_tok, E, sp))
 
-        def gather():
-            for s in range(B):
-                ct.check(L.ct_kv_paged_gather(kv.h, s, 0, T, gat.data_ptr(), ct.CT_KV_BF16))
+        g_seqs = np.arange(B, dtype=np.uint32)
+        g_starts = np.zeros(B, np.uint32)
+        g_counts = np.full(B, T, np.uint32)
+
+        def gather():                                     # every sequence, one launch
+            ct.check(L.ct_kv_paged_gather_batch(kv.h, g_seqs.ctypes.data, g_starts.ctypes.data, g_counts.ctypes.data,
+                                                B, gat.data_ptr(), ct.CT_KV_BF16))
 
         plan = ct.MlaPlan(np.full(B, T, np.int32), n_pages, kv_dtype=dt, max_pages_per_seq=pages_per)
 

@@ -105,6 +105,7 @@ SIGNATURES = {
     "ct_kv_paged_evict_lru": (I, [P, U32]),
     "ct_kv_paged_compact": (I, [P]),
     "ct_kv_paged_gather": (I, [P, U32, U32, U32, P, U32]),
+    "ct_kv_paged_gather_batch": (I, [P, P, P, P, U32, P, U32]),
     "ct_kv_paged_block_table": (I, [P, P]),
     "ct_kv_paged_seq_lens": (I, [P, P]),
     "ct_kv_paged_last_access": (I, [P, P]),

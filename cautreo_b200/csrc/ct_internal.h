@@ -50,6 +50,11 @@ int ct__launch_kv_gather(const void *pool, const float *scales, uint32_t pool_dt
                          const int32_t *bt_row, uint32_t page_tokens, uint32_t dim,
                          uint32_t start, uint32_t n, void *out, uint32_t out_dtype,
                          void *stream);
+/* Several (seq, start, count, first output row) ranges in one launch; desc is
+ * a device array of n_desc int4, max_count the largest count. */
+int ct__launch_kv_gather_batch(const void *pool, const float *scales, uint32_t pool_dtype, const int32_t *bt,
+                               uint32_t max_pages, uint32_t page_tokens, uint32_t dim, const void *desc,
+                               uint32_t n_desc, uint32_t max_count, void *out, uint32_t out_dtype, void *stream);
 int ct__launch_kv_compress(float *k, float *v, float *scratch, uint32_t n_layers,
                            uint32_t max_ctx, uint32_t stride, uint32_t new_len,
                            uint32_t step, void *stream);
@@ -138,6 +143,18 @@ CT_DEV uint8_t ct_e4m3_code(float x, float id) {
 CT_DEV float ct_e4m3_to_f32(uint8_t v) {
     __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)v, __NV_E4M3);
     return __half2float(__half(hr));
+}
+
+/* Two e4m3 codes (low byte first) -> two floats, one conversion per pair. */
+CT_DEV float2 ct_e4m3x2_to_f32x2(uint16_t v) {
+    __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
+    return __half22float2(__half2(hr));
+}
+
+/* e4m3 codes of (x0 * id, x1 * id) packed low byte first, RNE, saturating. */
+CT_DEV uint16_t ct_e4m3x2_code(float x0, float x1, float id) {
+    return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(x0, id), __fmul_rn(x1, id)), __NV_SATFINITE,
+                                              __NV_E4M3);
 }
 
 CT_DEV float ct_warp_max(float v) {

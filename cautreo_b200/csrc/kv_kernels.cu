@@ -19,25 +19,30 @@ namespace {
 
 constexpr int kWarps = 8;          /* tokens per 256-thread block */
 
-/* Loads 16 consecutive source values of token `tok`, chunk `c` (16 values). */
+/* 16 consecutive source values of a token as raw words: bf16 -> 8 words
+ * (two per word, low half first), fp32 -> 16 words. */
 template <bool SrcBf16>
-__device__ __forceinline__ void load16(const void *src, size_t tok, uint32_t dim, uint32_t c, float v[16]) {
-    if (SrcBf16) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + tok * dim + c * 16);
-        uint4 a = __ldg(p), b = __ldg(p + 1);
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+struct Chunk {
+    uint32_t w[SrcBf16 ? 8 : 16];
+    __device__ __forceinline__ void load(const void *src, size_t tok, uint32_t dim, uint32_t c) {
+        const uint4 *p = SrcBf16 ? reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + tok * dim + c * 16)
+                                 : reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + tok * dim + c * 16);
         #pragma unroll
-        for (int i = 0; i < 8; i++) { v[2 * i] = __uint_as_float(w[i] << 16); v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u); }
-    } else {
-        const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(src) + tok * dim + c * 16);
-        #pragma unroll
-        for (int i = 0; i < 4; i++) { float4 f = __ldg(p + i); v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w; }
+        for (int i = 0; i < (SrcBf16 ? 2 : 4); i++) {
+            const uint4 v = __ldg(p + i);
+            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        }
     }
-}
+    __device__ __forceinline__ float val(int i) const {
+        if (SrcBf16) return __uint_as_float((i & 1) ? (w[i >> 1] & 0xFFFF0000u) : (w[i >> 1] << 16));
+        return __uint_as_float(w[i]);
+    }
+};
 
 /* K1 / K2: one warp per token.  Lane l owns 16-value chunks l, l+32, ...
- * (MaxChunks per lane); quantised pools need the token's absmax, reduced
- * with warp shuffles, before any code is written. */
+ * (MaxChunks per lane), kept as raw words so a 576-value token costs few
+ * registers and many warps stay resident; quantised pools need the token's
+ * absmax, reduced with warp shuffles, before any code is written. */
 template <bool SrcBf16, int PoolDtype, int MaxChunks>
 __global__ void __launch_bounds__(256) k_write_slots(void *pool, float *scales, const void *src,
                                                      const int32_t *dest, uint32_t n, uint32_t dim) {
@@ -47,55 +52,67 @@ __global__ void __launch_bounds__(256) k_write_slots(void *pool, float *scales, 
     const int32_t slot = dest[warp];
     if (slot < 0) return;
     const uint32_t n_chunks = dim / 16;
-    float v[MaxChunks][16];
-    float amax = 0.0f;
+    Chunk<SrcBf16> v[MaxChunks];
     #pragma unroll
     for (int k = 0; k < MaxChunks; k++) {
-        uint32_t c = lane + 32u * k;
-        if (c < n_chunks) {
-            load16<SrcBf16>(src, warp, dim, c, v[k]);
-            #pragma unroll
-            for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[k][i]));
-        }
+        const uint32_t c = lane + 32u * k;
+        if (c < n_chunks) v[k].load(src, warp, dim, c);
     }
     const size_t base = (size_t)slot * dim;
     if (PoolDtype == CT_KV_BF16) {
         #pragma unroll
         for (int k = 0; k < MaxChunks; k++) {
-            uint32_t c = lane + 32u * k;
+            const uint32_t c = lane + 32u * k;
             if (c >= n_chunks) continue;
             uint32_t w[8];
-            #pragma unroll
-            for (int i = 0; i < 8; i++) w[i] = (uint32_t)ct_f32_to_bf16(v[k][2 * i]) | ((uint32_t)ct_f32_to_bf16(v[k][2 * i + 1]) << 16);
+            if (SrcBf16) {
+                #pragma unroll
+                for (int i = 0; i < 8; i++) w[i] = v[k].w[i];
+            } else {
+                #pragma unroll
+                for (int i = 0; i < 8; i++)
+                    w[i] = (uint32_t)ct_f32_to_bf16(v[k].val(2 * i)) | ((uint32_t)ct_f32_to_bf16(v[k].val(2 * i + 1)) << 16);
+            }
             uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(pool) + base + c * 16);
-            p[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            p[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            __stcs(p, make_uint4(w[0], w[1], w[2], w[3]));
+            __stcs(p + 1, make_uint4(w[4], w[5], w[6], w[7]));
         }
     } else if (PoolDtype == CT_KV_F32) {
         #pragma unroll
         for (int k = 0; k < MaxChunks; k++) {
-            uint32_t c = lane + 32u * k;
+            const uint32_t c = lane + 32u * k;
             if (c >= n_chunks) continue;
             float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(pool) + base + c * 16);
             #pragma unroll
-            for (int i = 0; i < 4; i++) p[i] = make_float4(v[k][4 * i], v[k][4 * i + 1], v[k][4 * i + 2], v[k][4 * i + 3]);
+            for (int i = 0; i < 4; i++)
+                __stcs(p + i, make_float4(v[k].val(4 * i), v[k].val(4 * i + 1), v[k].val(4 * i + 2), v[k].val(4 * i + 3)));
         }
     } else {
+        float amax = 0.0f;
+        #pragma unroll
+        for (int k = 0; k < MaxChunks; k++) {
+            if (lane + 32u * k >= n_chunks) continue;
+            #pragma unroll
+            for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[k].val(i)));
+        }
         amax = ct_warp_max(amax);
         const float d = __fdiv_rn(amax, PoolDtype == CT_KV_INT8 ? 127.0f : 448.0f);
         const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
         #pragma unroll
         for (int k = 0; k < MaxChunks; k++) {
-            uint32_t c = lane + 32u * k;
+            const uint32_t c = lane + 32u * k;
             if (c >= n_chunks) continue;
             uint32_t w[4] = {0, 0, 0, 0};
-            #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                uint32_t b = PoolDtype == CT_KV_INT8 ? (uint32_t)(uint8_t)(int8_t)ct_q8_code(v[k][i], id)
-                                                     : (uint32_t)ct_e4m3_code(v[k][i], id);
-                w[i >> 2] |= b << (8 * (i & 3));
+            if (PoolDtype == CT_KV_INT8) {
+                #pragma unroll
+                for (int i = 0; i < 16; i++)
+                    w[i >> 2] |= (uint32_t)(uint8_t)(int8_t)ct_q8_code(v[k].val(i), id) << (8 * (i & 3));
+            } else {
+                #pragma unroll
+                for (int i = 0; i < 16; i += 2)
+                    w[i >> 2] |= (uint32_t)ct_e4m3x2_code(v[k].val(i), v[k].val(i + 1), id) << (8 * (i & 3));
             }
-            *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(pool) + base + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            __stcs(reinterpret_cast<uint4 *>(static_cast<uint8_t *>(pool) + base + c * 16), make_uint4(w[0], w[1], w[2], w[3]));
         }
         if (lane == 0) scales[slot] = d;
     }
@@ -114,44 +131,95 @@ int launch_write(void *pool, float *scales, const void *src, const int32_t *dest
     return ct__cuda_status(cudaGetLastError(), "write_slots");
 }
 
-/* K3: one warp per token, dequantising to fp32 or bf16. */
-template <int PoolDtype, bool OutBf16>
+/* One token of a gather (whole warp): pool slot -> output row, dequantising
+ * to fp32 or bf16.  Lanes own 16-value chunks; every load is issued before
+ * any store. */
+template <int PoolDtype, bool OutBf16, int MaxChunks>
+__device__ __forceinline__ void gather_token(const void *pool, const float *scales, size_t slot, uint32_t dim,
+                                             void *out_row) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t n_chunks = dim / 16;
+    constexpr int kWords = (PoolDtype == CT_KV_F32) ? 16 : (PoolDtype == CT_KV_BF16 ? 8 : 4);
+    uint32_t w[MaxChunks][kWords];
+    #pragma unroll
+    for (int k = 0; k < MaxChunks; k++) {
+        const uint32_t c = lane + 32u * k;
+        if (c >= n_chunks) continue;
+        const size_t byte = (slot * dim + c * 16) * (PoolDtype == CT_KV_F32 ? 4 : PoolDtype == CT_KV_BF16 ? 2 : 1);
+        const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(pool) + byte);
+        #pragma unroll
+        for (int i = 0; i < kWords / 4; i++) {
+            const uint4 v = __ldcs(p + i);
+            w[k][4 * i] = v.x; w[k][4 * i + 1] = v.y; w[k][4 * i + 2] = v.z; w[k][4 * i + 3] = v.w;
+        }
+    }
+    const float sc = (PoolDtype == CT_KV_INT8 || PoolDtype == CT_KV_E4M3) ? scales[slot] : 1.0f;
+    #pragma unroll
+    for (int k = 0; k < MaxChunks; k++) {
+        const uint32_t c = lane + 32u * k;
+        if (c >= n_chunks) continue;
+        if (PoolDtype == CT_KV_BF16 && OutBf16) {
+            uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_row) + c * 16);
+            __stcs(p, make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]));
+            __stcs(p + 1, make_uint4(w[k][4], w[k][5], w[k][6], w[k][7]));
+            continue;
+        }
+        float v[16];
+        #pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (PoolDtype == CT_KV_BF16) v[i] = __uint_as_float((i & 1) ? (w[k][i >> 1] & 0xFFFF0000u) : (w[k][i >> 1] << 16));
+            else if (PoolDtype == CT_KV_F32) v[i] = __uint_as_float(w[k][i]);
+            else if (PoolDtype == CT_KV_INT8) {
+                v[i] = (float)(int8_t)(uint8_t)(w[k][i >> 2] >> (8 * (i & 3))) * sc;
+            } else if ((i & 1) == 0) {
+                const float2 f = ct_e4m3x2_to_f32x2((uint16_t)(w[k][i >> 2] >> (8 * (i & 3))));
+                v[i] = f.x * sc;
+                v[i + 1] = f.y * sc;
+            }
+        }
+        if (OutBf16) {
+            uint32_t o[8];
+            #pragma unroll
+            for (int i = 0; i < 8; i++) o[i] = (uint32_t)ct_f32_to_bf16(v[2 * i]) | ((uint32_t)ct_f32_to_bf16(v[2 * i + 1]) << 16);
+            uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_row) + c * 16);
+            __stcs(p, make_uint4(o[0], o[1], o[2], o[3]));
+            __stcs(p + 1, make_uint4(o[4], o[5], o[6], o[7]));
+        } else {
+            float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(out_row) + c * 16);
+            #pragma unroll
+            for (int i = 0; i < 4; i++) __stcs(p + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        }
+    }
+}
+
+/* K3: tokens [start, start+n) of one sequence, one warp per token. */
+template <int PoolDtype, bool OutBf16, int MaxChunks>
 __global__ void __launch_bounds__(256) k_gather(const void *pool, const float *scales,
                                                 const int32_t *bt_row, uint32_t page_tokens,
                                                 uint32_t dim, uint32_t start, uint32_t n, void *out) {
     const uint32_t t = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    const uint32_t lane = threadIdx.x & 31;
     if (t >= n) return;
     const uint32_t pos = start + t;
     const int32_t pg = bt_row[pos / page_tokens];
     const size_t slot = (size_t)pg * page_tokens + pos % page_tokens;
-    const float sc = (PoolDtype == CT_KV_INT8 || PoolDtype == CT_KV_E4M3) ? scales[slot] : 1.0f;
-    for (uint32_t c = lane; c < dim / 16; c += 32) {
-        float v[16];
-        if (PoolDtype == CT_KV_BF16) load16<true>(pool, slot, dim, c, v);
-        else if (PoolDtype == CT_KV_F32) load16<false>(pool, slot, dim, c, v);
-        else {
-            uint4 w = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(pool) + slot * dim + c * 16));
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-            #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                uint8_t b = (uint8_t)(ws[i >> 2] >> (8 * (i & 3)));
-                v[i] = (PoolDtype == CT_KV_INT8 ? (float)(int8_t)b : ct_e4m3_to_f32(b)) * sc;
-            }
-        }
-        if (OutBf16) {
-            uint32_t w[8];
-            #pragma unroll
-            for (int i = 0; i < 8; i++) w[i] = (uint32_t)ct_f32_to_bf16(v[2 * i]) | ((uint32_t)ct_f32_to_bf16(v[2 * i + 1]) << 16);
-            uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + (size_t)t * dim + c * 16);
-            p[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            p[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
-            float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(out) + (size_t)t * dim + c * 16);
-            #pragma unroll
-            for (int i = 0; i < 4; i++) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-    }
+    const size_t out_elt = (size_t)t * dim * (OutBf16 ? 2 : 4);
+    gather_token<PoolDtype, OutBf16, MaxChunks>(pool, scales, slot, dim, static_cast<uint8_t *>(out) + out_elt);
+}
+
+/* K3b: several sequences in one launch; desc[y] = (seq, start, count,
+ * first output row) and blockIdx.y selects it. */
+template <int PoolDtype, bool OutBf16, int MaxChunks>
+__global__ void __launch_bounds__(256) k_gather_batch(const void *pool, const float *scales, const int32_t *bt,
+                                                      uint32_t max_pages, uint32_t page_tokens, uint32_t dim,
+                                                      const int4 *desc, void *out) {
+    const int4 d = desc[blockIdx.y];
+    const uint32_t t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (t >= (uint32_t)d.z) return;
+    const uint32_t pos = (uint32_t)d.y + t;
+    const int32_t pg = bt[(size_t)d.x * max_pages + pos / page_tokens];
+    const size_t slot = (size_t)pg * page_tokens + pos % page_tokens;
+    const size_t out_elt = ((size_t)(uint32_t)d.w + t) * dim * (OutBf16 ? 2 : 4);
+    gather_token<PoolDtype, OutBf16, MaxChunks>(pool, scales, slot, dim, static_cast<uint8_t *>(out) + out_elt);
 }
 
 /* K4 (pages): block b copies whole page map[b] -> b; 16-byte vectors with
@@ -249,27 +317,71 @@ extern "C" int ct_kv_paged_move_pages(const void *src_pool, const float *src_sca
     return ct__cuda_status(cudaGetLastError(), "move_pages");
 }
 
+namespace {
+
+template <int D, bool Ob, int MC>
+void gather_one(const void *pool, const float *scales, const int32_t *bt_row, uint32_t P, uint32_t dim, uint32_t start,
+                uint32_t n, void *out, cudaStream_t st) {
+    k_gather<D, Ob, MC><<<(n + kWarps - 1) / kWarps, 256, 0, st>>>(pool, scales, bt_row, P, dim, start, n, out);
+}
+template <int D, bool Ob, int MC>
+void gather_many(const void *pool, const float *scales, const int32_t *bt, uint32_t maxp, uint32_t P, uint32_t dim,
+                 const int4 *desc, uint32_t n_desc, uint32_t max_n, void *out, cudaStream_t st) {
+    k_gather_batch<D, Ob, MC><<<dim3((max_n + kWarps - 1) / kWarps, n_desc), 256, 0, st>>>(pool, scales, bt, maxp, P,
+                                                                                          dim, desc, out);
+}
+
+template <int D>
+int gather_dispatch(bool ob, uint32_t chunks, const void *pool, const float *scales, const int32_t *bt, uint32_t maxp,
+                    uint32_t P, uint32_t dim, uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc,
+                    void *out, cudaStream_t st) {
+    const int mc = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : 0;
+    if (!mc) return CT_ERR_UNSUPPORTED;
+#define CT_G(OB, MC) (desc ? gather_many<D, OB, MC>(pool, scales, bt, maxp, P, dim, desc, n_desc, n, out, st) \
+                           : gather_one<D, OB, MC>(pool, scales, bt, P, dim, start, n, out, st))
+    if (ob) { if (mc == 1) CT_G(true, 1); else if (mc == 2) CT_G(true, 2); else CT_G(true, 4); }
+    else    { if (mc == 1) CT_G(false, 1); else if (mc == 2) CT_G(false, 2); else CT_G(false, 4); }
+#undef CT_G
+    return CT_OK;
+}
+
+int gather_any(uint32_t pool_dtype, bool ob, const void *pool, const float *scales, const int32_t *bt, uint32_t maxp,
+               uint32_t P, uint32_t dim, uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc, void *out,
+               cudaStream_t st) {
+    const uint32_t chunks = dim / 16;
+    int rc;
+    switch (pool_dtype) {
+        case CT_KV_BF16: rc = gather_dispatch<CT_KV_BF16>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+        case CT_KV_F32:  rc = gather_dispatch<CT_KV_F32>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+        case CT_KV_INT8: rc = gather_dispatch<CT_KV_INT8>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+        case CT_KV_E4M3: rc = gather_dispatch<CT_KV_E4M3>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+        default: return CT_ERR_ARG;
+    }
+    if (rc) return rc;
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "gather");
+}
+
+}  // namespace
+
 extern "C" int ct__launch_kv_gather(const void *pool, const float *scales, uint32_t pool_dtype,
                                     const int32_t *bt_row, uint32_t page_tokens, uint32_t dim,
                                     uint32_t start, uint32_t n, void *out, uint32_t out_dtype,
                                     void *stream) {
     if (n == 0) return CT_OK;
     if (dim % 16 != 0) return CT_ERR_ARG;
-    cudaStream_t st = (cudaStream_t)stream;
-    const int blocks = (int)((n + kWarps - 1) / kWarps);
-    const bool ob = out_dtype == CT_KV_BF16;
-#define CT_GATHER(D) (ob ? (k_gather<D, true><<<blocks, 256, 0, st>>>(pool, scales, bt_row, page_tokens, dim, start, n, out), 0) \
-                         : (k_gather<D, false><<<blocks, 256, 0, st>>>(pool, scales, bt_row, page_tokens, dim, start, n, out), 0))
-    switch (pool_dtype) {
-        case CT_KV_BF16: CT_GATHER(CT_KV_BF16); break;
-        case CT_KV_F32:  CT_GATHER(CT_KV_F32); break;
-        case CT_KV_INT8: CT_GATHER(CT_KV_INT8); break;
-        case CT_KV_E4M3: CT_GATHER(CT_KV_E4M3); break;
-        default: return CT_ERR_ARG;
-    }
-#undef CT_GATHER
-    ct__count_launches(1);
-    return ct__cuda_status(cudaGetLastError(), "gather");
+    return gather_any(pool_dtype, out_dtype == CT_KV_BF16, pool, scales, bt_row, 0, page_tokens, dim, start, n,
+                      nullptr, 0, out, (cudaStream_t)stream);
+}
+
+extern "C" int ct__launch_kv_gather_batch(const void *pool, const float *scales, uint32_t pool_dtype,
+                                          const int32_t *bt, uint32_t max_pages, uint32_t page_tokens,
+                                          uint32_t dim, const void *desc, uint32_t n_desc, uint32_t max_count,
+                                          void *out, uint32_t out_dtype, void *stream) {
+    if (n_desc == 0 || max_count == 0) return CT_OK;
+    if (dim % 16 != 0 || n_desc > 65535) return CT_ERR_ARG;
+    return gather_any(pool_dtype, out_dtype == CT_KV_BF16, pool, scales, bt, max_pages, page_tokens, dim, 0, max_count,
+                      static_cast<const int4 *>(desc), n_desc, out, (cudaStream_t)stream);
 }
 
 extern "C" int ct__launch_kv_compress(float *k, float *v, float *scratch, uint32_t n_layers,

@@ -528,6 +528,49 @@ int ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t 
                                 P, h->cfg.entry_dim, start, n, out, out_dtype, h->stream);
 }
 
+int ct_kv_paged_gather_batch(ct_kv_paged_t *h, const uint32_t *seqs, const uint32_t *starts,
+                             const uint32_t *counts, uint32_t n, void *out, uint32_t out_dtype) {
+    if (!h || (n && (!seqs || !starts || !counts || !out))) return CT_ERR_ARG;
+    if (h->host_only) return CT_ERR_UNSUPPORTED;
+    if (out_dtype != CT_KV_BF16 && out_dtype != CT_KV_F32) return CT_ERR_ARG;
+    const uint32_t P = h->cfg.page_tokens, MP = h->cfg.max_pages_per_seq;
+    for (uint32_t i = 0; i < n; i++) {
+        if (seqs[i] >= h->cfg.n_seqs || (uint64_t)starts[i] + counts[i] > h->len[seqs[i]]) return CT_ERR_ARG;
+        if (counts[i] == 0) continue;
+        for (uint32_t lp = starts[i] / P; lp <= (starts[i] + counts[i] - 1) / P; lp++)
+            if (h->bt[(size_t)seqs[i] * MP + lp] < 0) return CT_ERR_UNMAPPED;
+    }
+    const size_t row_bytes = (size_t)h->cfg.entry_dim * (out_dtype == CT_KV_BF16 ? 2 : 4);
+    uint64_t row = 0;
+    for (uint32_t b = 0; b < n; b += 65535u) {                /* one launch per 65535 ranges */
+        const uint32_t m = n - b < 65535u ? n - b : 65535u;
+        int rc = stage_reserve(h, (size_t)4 * m);
+        if (rc) return rc;
+        uint32_t max_count = 0;
+        const uint64_t row0 = row;
+        for (uint32_t i = 0; i < m; i++) {
+            int32_t *d = h->stage_host + 4 * (size_t)i;
+            d[0] = (int32_t)seqs[b + i];
+            d[1] = (int32_t)starts[b + i];
+            d[2] = (int32_t)counts[b + i];
+            d[3] = (int32_t)(row - row0);
+            row += counts[b + i];
+            if (counts[b + i] > max_count) max_count = counts[b + i];
+        }
+        if (row - row0 > 0x7FFFFFFFu) return CT_ERR_ARG;
+        rc = ct__cuda_status(cudaMemcpyAsync(h->stage_dev, h->stage_host, (size_t)4 * m * sizeof(int32_t),
+                                             cudaMemcpyHostToDevice, h->stream), "gather_batch upload");
+        if (!rc) rc = ct__cuda_status(cudaEventRecord(h->stage_ev, h->stream), "gather_batch event");
+        if (rc) return rc;
+        h->stage_pending = 1;
+        rc = ct__launch_kv_gather_batch(h->pool, h->scales, h->cfg.dtype, h->bt_dev, MP, P, h->cfg.entry_dim,
+                                        h->stage_dev, m, max_count, (uint8_t *)out + row0 * row_bytes, out_dtype,
+                                        h->stream);
+        if (rc) return rc;
+    }
+    return CT_OK;
+}
+
 int ct_kv_paged_block_table(const ct_kv_paged_t *h, int32_t *out) {
     if (!h || !out) return CT_ERR_ARG;
     memcpy(out, h->bt, (size_t)h->cfg.n_seqs * h->cfg.max_pages_per_seq * sizeof(int32_t));

@@ -170,6 +170,13 @@ int  ct_kv_paged_compact(ct_kv_paged_t *h);
 int  ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t n,
                         void *out, uint32_t out_dtype);
 
+/* The same for n ranges at once (host arrays): tokens [starts[i],
+ * starts[i] + counts[i]) of sequence seqs[i], written back to back in range
+ * order into out (device).  One launch per 65,535 ranges.  New; no reference
+ * counterpart (the reference reads one row at a time, kv_cache.c:63-71). */
+int  ct_kv_paged_gather_batch(ct_kv_paged_t *h, const uint32_t *seqs, const uint32_t *starts,
+                              const uint32_t *counts, uint32_t n, void *out, uint32_t out_dtype);
+
 /* Host mirrors / device views. */
 int  ct_kv_paged_block_table(const ct_kv_paged_t *h, int32_t *out_host);  /* [n_seqs][max_pages] */
 int  ct_kv_paged_seq_lens(const ct_kv_paged_t *h, uint32_t *out_host);    /* [n_seqs] */

@@ -169,6 +169,41 @@ def test_paged_append_gather_bit_exact(pool_dtype, src):
     h.close()
 
 
+@pytest.mark.parametrize("pool_dtype", [ct.CT_KV_BF16, ct.CT_KV_F32, ct.CT_KV_INT8, ct.CT_KV_E4M3])
+def test_paged_gather_batch_matches_per_sequence_gathers(pool_dtype):
+    """ct_kv_paged_gather_batch: the rows of every range, back to back, bit for
+    bit what one ct_kv_paged_gather per range returns (empty and page-crossing
+    ranges included); bad ranges fail before anything is written."""
+    S, P, E = 6, 64, 576
+    lens = [1, 63, 64, 65, 300, 130]
+    ent, xf, sdt = entries_for(sum(lens), E, 12, "bf16")
+    h = ct.PagedKV(S, 8, 48, P, E, 0, pool_dtype, 0, stream())
+    h.set_free_order(oracle.permutation(oracle.key(12, 1), 48))
+    h.append(list(range(S)), lens, ent.data_ptr(), sdt)
+    L = ct.lib()
+    seqs = np.array([4, 0, 3, 5, 1, 2, 4], np.uint32)
+    starts = np.array([60, 0, 0, 64, 10, 0, 299], np.uint32)
+    counts = np.array([10, 1, 65, 66, 0, 64, 1], np.uint32)
+    n_rows = int(counts.sum())
+    for out_dt, npdt in ((ct.CT_KV_F32, np.float32), (ct.CT_KV_BF16, np.uint16)):
+        out = empty((n_rows, E), npdt)
+        ct.check(L.ct_kv_paged_gather_batch(h.h, seqs.ctypes.data, starts.ctypes.data, counts.ctypes.data, len(seqs),
+                                            out.data_ptr(), out_dt), "gather_batch")
+        got = host(out, npdt)
+        row = 0
+        for s_, st, n in zip(seqs, starts, counts):
+            if n:
+                one = empty((int(n), E), npdt)
+                ct.check(L.ct_kv_paged_gather(h.h, int(s_), int(st), int(n), one.data_ptr(), out_dt))
+                assert np.array_equal(got[row:row + n].view(np.uint8), host(one, npdt).view(np.uint8)), (s_, st, n)
+            row += int(n)
+    bad = np.array([5], np.uint32)
+    assert L.ct_kv_paged_gather_batch(h.h, bad.ctypes.data, np.array([100], np.uint32).ctypes.data,
+                                      np.array([40], np.uint32).ctypes.data, 1, out.data_ptr(),
+                                      ct.CT_KV_F32) == ct.CT_ERR_ARG          # past the sequence's length
+    h.close()
+
+
 def test_paged_gather_unmapped_is_an_error():
     h = ct.PagedKV(1, 8, 4, 4, 16, 4, ct.CT_KV_BF16, 0, stream())
     ent = dev(oracle.f32_to_bf16(oracle.normal_f32(oracle.key(1, 1), 0, 12 * 16)))
