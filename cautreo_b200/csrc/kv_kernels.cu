@@ -158,12 +158,12 @@ __device__ __forceinline__ void gather_token(const void *pool, const float *scal
     for (int k = 0; k < MaxChunks; k++) {
         const uint32_t c = lane + 32u * k;
         if (c >= n_chunks) continue;
-        if (PoolDtype == CT_KV_BF16 && OutBf16) {
+        if constexpr (PoolDtype == CT_KV_BF16 && OutBf16) {
             uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_row) + c * 16);
             __stcs(p, make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]));
             __stcs(p + 1, make_uint4(w[k][4], w[k][5], w[k][6], w[k][7]));
             continue;
-        }
+        } else {
         float v[16];
         #pragma unroll
         for (int i = 0; i < 16; i++) {
@@ -188,6 +188,7 @@ __device__ __forceinline__ void gather_token(const void *pool, const float *scal
             float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(out_row) + c * 16);
             #pragma unroll
             for (int i = 0; i < 4; i++) __stcs(p + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        }
         }
     }
 }

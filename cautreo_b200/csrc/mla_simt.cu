@@ -213,11 +213,12 @@ __global__ void __launch_bounds__(128) k_mla_combine(const ct_mla_combine_t *ite
 }
 
 /* Declared in mla_tc.cu: the tcgen05 kernel for H=128, E=576, Dv=512, P=64,
- * bf16 pools.  Returns CT_ERR_UNSUPPORTED when it does not take the shape. */
+ * bf16 / int8 / e4m3 pools.  Returns CT_ERR_UNSUPPORTED when it does not take
+ * the shape. */
 extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks, uint32_t n_chunks,
-                                 const int32_t *worker_begin, uint32_t n_workers, const void *q, const void *pool, const int32_t *block_table,
-                                 const int32_t *seq_lens, void *out, float *lse, float *part_o,
-                                 float *part_ml, void *stream);
+                                 const int32_t *worker_begin, uint32_t n_workers, const void *q, const void *pool,
+                                 const float *scales, const int32_t *block_table, const int32_t *seq_lens, void *out,
+                                 float *lse, float *part_o, float *part_ml, void *stream);
 
 extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks,
                                      uint32_t n_chunks, const int32_t *worker_begin, uint32_t n_workers,
@@ -229,8 +230,8 @@ extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chu
     cudaStream_t st = (cudaStream_t)stream;
     uint32_t launches = 0;
     if (n_chunks > 0) {
-        int rc = ct__launch_mla_tc(dims, chunks, n_chunks, worker_begin, n_workers, q, pool, block_table, seq_lens, out, lse, part_o,
-                                   part_ml, stream);
+        int rc = ct__launch_mla_tc(dims, chunks, n_chunks, worker_begin, n_workers, q, pool, scales, block_table,
+                                   seq_lens, out, lse, part_o, part_ml, stream);
         if (rc == CT_ERR_UNSUPPORTED) {
             if (dims->entry_dim > EMAX || dims->v_dim > VMAX || dims->entry_dim % 8 != 0 || dims->page_tokens == 0)
                 return CT_ERR_UNSUPPORTED;

@@ -57,8 +57,12 @@ constexpr int kH = 128, kE = 576, kDv = 512, kP = 64;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kFirstSoftmaxWarp = 3;
 constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 352 */
+constexpr int kConvWarps = 2;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
+constexpr int kFirstConvWarp = kFirstSoftmaxWarp + kSoftmaxWarps;
+constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 416 */
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
+constexpr uint32_t kCodeBytes = 4 * 4096 + 2048 + 256;  /* quantised page half: codes + 64 scales */
 constexpr uint32_t kKvBytes = 4 * 8192 + 4096;          /* 36,864 per stage */
 constexpr uint32_t kXBytes = 32768;                     /* one tile's partial scores, 128 x 64 fp32 */
 constexpr uint32_t kOffQ = 0;
@@ -67,7 +71,8 @@ constexpr uint32_t kOffOut = kOffKv + kStages * kKvBytes;
 constexpr uint32_t kOffIn = kOffOut + kXBytes;         /* two receive slots */
 constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
 constexpr uint32_t kRedBytes = 6 * kH * 4;              /* row max [2 parities][2 halves], row sum [2 halves] */
-constexpr uint32_t kOffBar = kOffRed + kRedBytes;
+constexpr uint32_t kOffScale = kOffRed + kRedBytes;    /* per stage: 64 fp32 token scales (quantised pools) */
+constexpr uint32_t kOffBar = kOffScale + kStages * 256;
 constexpr uint32_t kNumBars = 40;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
@@ -87,7 +92,8 @@ constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
 enum : uint32_t {
     B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_P_FULL = 11,
     B_O_READY = 13, B_O_FINAL = 14, B_O_FREE = 15, B_SO_FULL = 16, B_SO_EMPTY = 17, B_X_FULL = 18 /* [slot] */,
-    B_X_EMPTY = 20 /* [slot] */, B_DRAIN = 22, B_RED = 23 /* [parity][quad] */, B_RED_L = 31 /* [quad] */
+    B_X_EMPTY = 20 /* [slot] */, B_DRAIN = 22, B_RED = 23 /* [parity][quad] */, B_RED_L = 31 /* [quad] */,
+    B_CONV_FULL = 35 /* [stage]: page converted to bf16 (quantised pools) */
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -168,6 +174,12 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, ui
     asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "r"(src), "r"(bytes), "r"(bar) : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+/* Untiled bulk copy global -> this CTA's shared memory (16-B aligned, size
+ * a multiple of 16), completing on a local barrier. */
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -266,6 +278,7 @@ struct Params {
     float *lse;
     float *part_o;
     float *part_ml;
+    const float *scales;     /* quantised pools: fp32 per token, [n_pages][64] */
     uint32_t maxp;
     uint32_t n_pages;
     float qk_scale;          /* scale * log2(e) */
@@ -334,8 +347,10 @@ __device__ __forceinline__ uint32_t count_tiles(const ct_mla_chunk_t &ch, const 
 
 /* ---- warp 0: TMA producer (lane 0 issues) -------------------------------- */
 
+template <int KV>
 __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_lat, const CUtensorMap *kv_rope,
                          const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
+    constexpr bool kQuant = KV != CT_KV_BF16;
     const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nq = 0;
     bool ok = true;
@@ -362,12 +377,21 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
             if (leader) {
                 ok = wait_bar(c, bar(c, B_KV_EMPTY + st), ((g / kStages) & 1) ^ 1, false, 2);
                 if (ok) {
-                    mbar_expect_tx(bar(c, B_KV_FULL + st), kKvBytes);
-                    const uint32_t dst = c.s + kOffKv + st * kKvBytes;
+                    const uint32_t dst = c.s + kOffKv + st * kKvBytes, fb = bar(c, B_KV_FULL + st);
                     const int y = pg * kP;
-                    for (int b = 0; b < 4; b++)
-                        tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, bar(c, B_KV_FULL + st));
-                    tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, bar(c, B_KV_FULL + st));
+                    if (!kQuant) {
+                        mbar_expect_tx(fb, kKvBytes);
+                        for (int b = 0; b < 4; b++) tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, fb);
+                        tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, fb);
+                    } else {
+                        /* 8-bit codes into the upper half of each bf16 box (the
+                         * converter widens them in place), and the page's scales */
+                        mbar_expect_tx(fb, kCodeBytes);
+                        for (int b = 0; b < 4; b++)
+                            tma_load_2d(dst + b * 8192 + 4096, kv_lat, rank * 256 + b * 64, y, fb);
+                        tma_load_2d(dst + 4 * 8192 + 2048, kv_rope, 512 + rank * 32, y, fb);
+                        bulk_load(c.s + kOffScale + st * 256, p.scales + (size_t)pg * kP, 256, fb);
+                    }
                 }
             }
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
@@ -413,7 +437,9 @@ __device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t p
                (first && k == 0) ? 0u : 1u);
 }
 
+template <int KV>
 __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    constexpr uint32_t kPageReady = KV == CT_KV_BF16 ? B_KV_FULL : B_CONV_FULL;
     const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0, nchunk = 0;
     bool ok = true;
@@ -449,7 +475,7 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
                 }
                 if (n1 < n && n1 <= n2 + 1) {
                     const uint32_t gt = g + n1;
-                    if (mbar_test(bar(c, B_KV_FULL + gt % kStages), (gt / kStages) & 1)) {
+                    if (mbar_test(bar(c, kPageReady + gt % kStages), (gt / kStages) & 1)) {
                         tc_fence_after();
                         issue_gemm1(c, tmem, gt % kStages, gt & 1);
                         mma_commit(bar(c, B_S_FULL + (gt & 1)));
@@ -542,8 +568,11 @@ struct Row {
 
 /* Finishes global tile t (index jj in its chunk): adds the peer's partial
  * scores, updates the running maximum, rescales O if needed, writes P. */
+template <int KV>
 __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r, uint32_t t, uint32_t jj, float *s,
                             int32_t ntok) {
+    constexpr bool kQuant = KV != CT_KV_BF16;
+    const float *tok_scale = reinterpret_cast<const float *>(c.smem + kOffScale + (t % kStages) * 256) + r.half * 32;
     const uint32_t lane = threadIdx.x & 31;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
     const uint32_t slot = t & 1;
@@ -561,7 +590,9 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     #pragma unroll
     for (int i = 0; i < 32; i++) {
-        s[i] = ((int32_t)(r.half * 32 + i) < ntok) ? s[i] * p.qk_scale : -INFINITY;
+        /* quantised pages: the scores are code dot products; times the token's scale */
+        const float v = kQuant ? s[i] * tok_scale[i] : s[i];
+        s[i] = ((int32_t)(r.half * 32 + i) < ntok) ? v * p.qk_scale : -INFINITY;
         m4[i & 3] = fmaxf(m4[i & 3], s[i]);
     }
     float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
@@ -602,15 +633,27 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
      * the previous P there, completed before GEMM1 of tile t did) */
     uint32_t w[16];
     float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    #pragma unroll
-    for (int k = 0; k < 16; k++) {
-        w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
-        l4[k & 3] += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
+    if (!kQuant) {
+        #pragma unroll
+        for (int k = 0; k < 16; k++) {
+            w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
+            l4[k & 3] += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+    } else {
+        /* V = scale x codes: the scale folds into P; the normaliser sums P itself */
+        #pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const float p0 = exp2f(s[2 * k] - r.m_used), p1 = exp2f(s[2 * k + 1] - r.m_used);
+            l4[k & 3] += p0 + p1;
+            const bool in0 = (int32_t)(r.half * 32 + 2 * k) < ntok, in1 = (int32_t)(r.half * 32 + 2 * k + 1) < ntok;
+            w[k] = bf16x2_rn(in0 ? p0 * tok_scale[2 * k] : 0.0f, in1 ? p1 * tok_scale[2 * k + 1] : 0.0f);
+        }
     }
     r.l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
     tmem_st16(tmem + r.lane_base + kTmemS + (t & 1) * 64 + r.half * 16, w);
-    /* a partial page: zero the V rows past its tokens (stale slots may hold anything) */
-    if (ntok < kP) {
+    /* a partial page: zero the V rows past its tokens (stale slots may hold
+     * anything; the converter already wrote zeros there for quantised pages) */
+    if (!kQuant && ntok < kP) {
         uint8_t *kvs = c.smem + kOffKv + (t % kStages) * kKvBytes;
         const uint32_t per_blk = (uint32_t)(kP - ntok) * 8;          /* 16-B words per box */
         for (uint32_t i = r.tid; i < 4 * per_blk; i += 32 * kSoftmaxWarps) {
@@ -644,6 +687,7 @@ __device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t g
     return true;
 }
 
+template <int KV>
 __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3;                     /* TMEM lane quadrant this warp may access */
@@ -728,11 +772,11 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                     if (sr || *c.abort || clock64() - t0 > kWaitCycles) break;   /* the waits below bound the rest */
                 }
                 if (finish_first) {
-                    if (!finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok) ||
+                    if (!finish_tile<KV>(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok) ||
                         !stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
                 } else {
                     if (!stage_tile(c, tmem, r, gt, s_cur) ||
-                        !finish_tile(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
+                        !finish_tile<KV>(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
                 }
             }
             #pragma unroll
@@ -741,7 +785,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             j++;
         } while (it.next(pg, ntok));
         if (!ok) break;
-        if (!finish_tile(c, p, tmem, r, g + j - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
+        if (!finish_tile<KV>(c, p, tmem, r, g + j - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
         g += j;
         /* epilogue: the row sum over both halves, then O of this CTA's 256 value dims */
         float *rl = red + 4 * kH;
@@ -790,9 +834,95 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     }
 }
 
+/* ---- warps 11-12 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
+
+/* 16 codes (one 16-byte chunk) -> 16 bf16 values as two 16-byte chunks.
+ * Every int8 and e4m3 value is exactly representable in bf16. */
+template <int KV>
+__device__ __forceinline__ void widen16(const uint4 &c, uint4 &lo, uint4 &hi) {
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    uint32_t o[8];
+    #pragma unroll
+    for (int i = 0; i < 8; i++) {                      /* codes 2i, 2i+1 */
+        const uint32_t pair = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+        float f0, f1;
+        if (KV == CT_KV_INT8) {
+            f0 = (float)(int8_t)(pair & 0xFF);
+            f1 = (float)(int8_t)(pair >> 8);
+        } else {
+            const float2 f = ct_e4m3x2_to_f32x2((uint16_t)pair);
+            f0 = f.x;
+            f1 = f.y;
+        }
+        o[i] = bf16x2_rn(f0, f1);
+    }
+    lo = make_uint4(o[0], o[1], o[2], o[3]);
+    hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+/* The TMA put each box's codes in the upper half of its bf16 box (latent:
+ * 64 rows x 64 codes at +4 KB of an 8 KB SW128 box; rope: 64 x 32 at +2 KB of
+ * a 4 KB SW64 box).  A warp owns whole boxes (latent boxes w and w+2, the
+ * rope box for warp 0): it loads all of a box's codes into registers, then
+ * writes the bf16 rows over them, so no other warp's codes are overwritten.
+ * Latent rows past the page's tokens become zeros (they are V rows of GEMM2). */
+template <int KV>
+__device__ void converter(const Ctx &c, const Params &p, int wbeg, int wend) {
+    const uint32_t lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - kFirstConvWarp;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        WarpTiles it;
+        it.init(ch, p);
+        int32_t pg, ntok;
+        while (it.next(pg, ntok)) {
+            const uint32_t st = g % kStages;
+            if (!wait_warp(c, bar(c, B_KV_FULL + st), (g / kStages) & 1, false, 19)) { ok = false; break; }
+            uint8_t *kv = c.smem + kOffKv + st * kKvBytes;
+            #pragma unroll 1
+            for (int bi = 0; bi < 2; bi++) {
+                uint8_t *box = kv + (cw + 2 * bi) * 8192;
+                uint4 code[8];
+                #pragma unroll
+                for (int k = 0; k < 8; k++) code[k] = reinterpret_cast<const uint4 *>(box + 4096)[lane + 32 * k];
+                __syncwarp();
+                #pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const uint32_t idx = lane + 32 * k, row = idx >> 2, cc = idx & 3;
+                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                    if ((int32_t)row < ntok) widen16<KV>(code[k], lo, hi);
+                    *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc) ^ (row & 7)) << 4)) = lo;
+                    *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc + 1) ^ (row & 7)) << 4)) = hi;
+                }
+                __syncwarp();
+            }
+            if (cw == 0) {
+                uint8_t *box = kv + 4 * 8192;
+                uint4 code[4];
+                #pragma unroll
+                for (int k = 0; k < 4; k++) code[k] = reinterpret_cast<const uint4 *>(box + 2048)[lane + 32 * k];
+                __syncwarp();
+                #pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const uint32_t idx = lane + 32 * k, row = idx >> 1, cc = idx & 1, sw = (row >> 1) & 3;
+                    uint4 lo, hi;
+                    widen16<KV>(code[k], lo, hi);
+                    *reinterpret_cast<uint4 *>(box + row * 64 + (((2 * cc) ^ sw) << 4)) = lo;
+                    *reinterpret_cast<uint4 *>(box + row * 64 + (((2 * cc + 1) ^ sw) << 4)) = hi;
+                }
+            }
+            proxy_fence();                             /* generic writes -> the tensor core's view */
+            warp_arrive(bar(c, B_CONV_FULL + st));
+            g++;
+        }
+    }
+}
+
 /* ---- the kernel ----------------------------------------------------------- */
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int KV>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? kThreads : kThreadsQ, 1)
     k_mla_tc(const __grid_constant__ CUtensorMap kv_lat, const __grid_constant__ CUtensorMap kv_rope,
              const __grid_constant__ CUtensorMap q_rope, Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -828,6 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
         mbar_init(bar(c, B_SO_FULL), kSoftmaxWarps); mbar_init(bar(c, B_SO_EMPTY), 1);
         mbar_init(bar(c, B_DRAIN), 1);
+        for (int i = 0; i < kStages; i++) mbar_init(bar(c, B_CONV_FULL + i), kConvWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mbar_expect_tx(bar(c, B_X_FULL + 0), kXBytes);   /* armed for the first two tiles */
         mbar_expect_tx(bar(c, B_X_FULL + 1), kXBytes);
@@ -844,13 +975,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
 
     if (warp == 0) {
-        producer(c, p, &kv_lat, &kv_rope, &q_rope, wbeg, wend, rank);
+        producer<KV>(c, p, &kv_lat, &kv_rope, &q_rope, wbeg, wend, rank);
     } else if (warp == 1) {
-        mma_issuer(c, p, tmem, wbeg, wend);
+        mma_issuer<KV>(c, p, tmem, wbeg, wend);
     } else if (warp == 2) {
         exchanger(c, p, wbeg, wend);
-    } else {
-        softmax_warps(c, p, tmem, wbeg, wend, rank);
+    } else if (warp < (uint32_t)kFirstConvWarp) {
+        softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
+    } else if (KV != CT_KV_BF16) {
+        converter<KV>(c, p, wbeg, wend);
     }
     __syncwarp();
     tc_fence_before();
@@ -877,24 +1010,37 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-/* 2-D bf16 map over [rows][576] with a (box_cols x box_rows) box. */
+/* 2-D map over [rows][576] values (bf16, or 1-byte codes) with a
+ * (box_cols x box_rows) box. */
 bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
-              CUtensorMapSwizzle sw) {
+              CUtensorMapSwizzle sw, bool bytes = false) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const uint32_t elt = bytes ? 1 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)kE, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)kE * 2};
+    cuuint64_t strides[1] = {(cuuint64_t)kE * elt};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(m, bytes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool shape_ok(const ct_mla_dims_t *d) {
     return d->n_heads == (uint32_t)kH && d->entry_dim == (uint32_t)kE && d->v_dim == (uint32_t)kDv &&
-           d->page_tokens == (uint32_t)kP && d->kv_dtype == CT_KV_BF16;
+           d->page_tokens == (uint32_t)kP &&
+           (d->kv_dtype == CT_KV_BF16 || d->kv_dtype == CT_KV_INT8 || d->kv_dtype == CT_KV_E4M3);
 }
+
+const void *kernel_for(uint32_t kv) {
+    switch (kv) {
+        case CT_KV_INT8: return (const void *)k_mla_tc<CT_KV_INT8>;
+        case CT_KV_E4M3: return (const void *)k_mla_tc<CT_KV_E4M3>;
+        default: return (const void *)k_mla_tc<CT_KV_BF16>;
+    }
+}
+
+int threads_for(uint32_t kv) { return kv == CT_KV_BF16 ? kThreads : kThreadsQ; }
 
 }  // namespace
 
@@ -909,26 +1055,27 @@ extern "C" int ct__mla_tc_workers(const ct_mla_dims_t *dims, int device) {
     }
     if (major != 10 || minor != 0 || !encode_fn()) return 0;
     /* One worker per co-resident cluster, so every worker runs in one wave. */
-    static int cached[64];
+    static int cached[64][4];
     if (device < 0 || device >= 64) return 0;
-    if (cached[device] == 0) {
+    const uint32_t kv = dims->kv_dtype;
+    if (cached[device][kv] == 0) {
         int prev = 0;
         cudaGetDevice(&prev);
         cudaSetDevice(device);
         int n = 0;
-        if (cudaFuncSetAttribute(k_mla_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc) ==
-            cudaSuccess) {
+        const void *fn = kernel_for(kv);
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc) == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.blockDim = dim3(threads_for(kv), 1, 1);
             cfg.dynamicSmemBytes = kSmemAlloc;
-            if (cudaOccupancyMaxActiveClusters(&n, (void *)k_mla_tc, &cfg) != cudaSuccess) n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) n = 0;
         }
         cudaGetLastError();
         cudaSetDevice(prev);
-        cached[device] = n > 0 ? n : -1;
+        cached[device][kv] = n > 0 ? n : -1;
     }
-    return cached[device] > 0 ? cached[device] : 0;
+    return cached[device][kv] > 0 ? cached[device][kv] : 0;
 }
 
 /* Error word of the tensor-core kernel (0 = no wait expired), for tests. */
@@ -944,10 +1091,14 @@ extern "C" int ct_mla_tc_error(int clear) {
 
 extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks, uint32_t n_chunks,
                                  const int32_t *worker_begin, uint32_t n_workers, const void *q,
-                                 const void *pool, const int32_t *block_table, const int32_t *seq_lens,
-                                 void *out, float *lse, float *part_o, float *part_ml, void *stream) {
+                                 const void *pool, const float *scales, const int32_t *block_table,
+                                 const int32_t *seq_lens, void *out, float *lse, float *part_o, float *part_ml,
+                                 void *stream) {
     (void)n_chunks;
     if (!shape_ok(dims)) return CT_ERR_UNSUPPORTED;
+    const uint32_t kv = dims->kv_dtype;
+    const bool quant = kv != CT_KV_BF16;
+    if (quant && (!scales || ((uintptr_t)scales & 15u))) return CT_ERR_UNSUPPORTED;
     int dev = 0;
     cudaGetDevice(&dev);
     if (ct__mla_tc_workers(dims, dev) <= 0 || n_workers == 0) return CT_ERR_UNSUPPORTED;
@@ -958,9 +1109,12 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     if (dims->n_pages == 0 || dims->n_seq == 0) return CT_ERR_ARG;
     const uint64_t pool_rows = (uint64_t)dims->n_pages * kP;
     const uint64_t q_rows = (uint64_t)dims->n_seq * kH;
-    if (!make_map(&kv_lat, pool, pool_rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&kv_rope, pool, pool_rows, 32, 64, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&q_rope, q, q_rows, 32, 128, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    const bool maps_ok =
+        quant ? make_map(&kv_lat, pool, pool_rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE, true) &&
+                    make_map(&kv_rope, pool, pool_rows, 32, 64, CU_TENSOR_MAP_SWIZZLE_NONE, true)
+              : make_map(&kv_lat, pool, pool_rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                    make_map(&kv_rope, pool, pool_rows, 32, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (!maps_ok || !make_map(&q_rope, q, q_rows, 32, 128, CU_TENSOR_MAP_SWIZZLE_64B)) {
         ct__set_error("mla_tc: cuTensorMapEncodeTiled failed");
         return CT_ERR_CUDA;
     }
@@ -974,16 +1128,23 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     p.lse = lse;
     p.part_o = part_o;
     p.part_ml = part_ml;
+    p.scales = scales;
     p.maxp = dims->max_pages_per_seq;
     p.n_pages = dims->n_pages;
     p.qk_scale = dims->scale * kLog2e;
-    static bool attr_set = false;
-    if (!attr_set) {
-        int rc = ct__cuda_status(cudaFuncSetAttribute(k_mla_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static bool attr_set[4] = {false, false, false, false};
+    if (!attr_set[kv]) {
+        int rc = ct__cuda_status(cudaFuncSetAttribute(kernel_for(kv), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                       (int)kSmemAlloc), "mla_tc attribute");
         if (rc) return rc;
-        attr_set = true;
+        attr_set[kv] = true;
     }
-    k_mla_tc<<<2 * n_workers, kThreads, kSmemAlloc, (cudaStream_t)stream>>>(kv_lat, kv_rope, q_rope, p);
+    cudaStream_t st = (cudaStream_t)stream;
+    const dim3 grid(2 * n_workers);
+    switch (kv) {
+        case CT_KV_INT8: k_mla_tc<CT_KV_INT8><<<grid, kThreadsQ, kSmemAlloc, st>>>(kv_lat, kv_rope, q_rope, p); break;
+        case CT_KV_E4M3: k_mla_tc<CT_KV_E4M3><<<grid, kThreadsQ, kSmemAlloc, st>>>(kv_lat, kv_rope, q_rope, p); break;
+        default: k_mla_tc<CT_KV_BF16><<<grid, kThreads, kSmemAlloc, st>>>(kv_lat, kv_rope, q_rope, p); break;
+    }
     return ct__cuda_status(cudaGetLastError(), "mla_tc launch");
 }

@@ -132,7 +132,44 @@ def test_mla_quantised_pool(dtype):
     else:
         O.orc_kv_quant_e4m3(xf.ctypes.data, NP * PAGE, MLA_E, codes.ctypes.data, sc.ctypes.data)
         O.orc_kv_dequant_e4m3(codes.ctypes.data, sc.ctypes.data, NP * PAGE, MLA_E, back.ctypes.data)
-    got, _ = run_decode(codes, bt, lens, q, dtype=dtype, scales=sc)
+    got, plan = run_decode(codes.reshape(NP, PAGE, MLA_E), bt, lens, q, dtype=dtype, scales=sc)
+    assert plan.tensor_cores                         # codes widened to bf16 in shared memory, tcgen05 GEMMs
+    want = oracle_decode_f32(back.reshape(NP, PAGE, MLA_E), bt, lens, oracle.bf16_to_f32(q.reshape(-1)).reshape(
+        q.shape), MLA_H, MLA_E, MLA_DV, PAGE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+    # stale slots past each sequence's end hold NaN codes and NaN scales: no effect
+    codes2 = codes.reshape(NP * PAGE, MLA_E).copy()
+    sc2 = sc.copy()
+    for s_, n in enumerate(lens):
+        for t in range(n, ((n + PAGE - 1) // PAGE) * PAGE):
+            slot = bt[s_, t // PAGE] * PAGE + t % PAGE
+            codes2[slot] = 0x7F if dtype == ct.CT_KV_E4M3 else 0x80
+            sc2[slot] = np.nan
+    got2, _ = run_decode(codes2.reshape(NP, PAGE, MLA_E), bt, lens, q, dtype=dtype, scales=sc2)
+    assert np.array_equal(np.isnan(got2), np.zeros_like(got2, bool))
+    ok, mx, rel = close(got2, want)
+    assert ok, (mx, rel)
+
+
+@pytest.mark.parametrize("dtype", [ct.CT_KV_INT8, ct.CT_KV_E4M3])
+def test_mla_quantised_pool_long(dtype):
+    """Quantised pages through the full tensor-core pipeline: sequences long
+    enough to be split across workers (combine path) and to cycle every page
+    stage many times."""
+    lens = [9000, 4097, 31, 12800]
+    pool16, bt, q = mla_case(lens, seed=5, outlier_bp=100, outlier_mul=20.0)
+    NP = pool16.shape[0]
+    xf = np.ascontiguousarray(oracle.bf16_to_f32(pool16.reshape(-1)).reshape(NP * PAGE, MLA_E))
+    codes = np.zeros(NP * PAGE * MLA_E, np.uint8)
+    sc = np.zeros(NP * PAGE, np.float32)
+    back = np.zeros(NP * PAGE * MLA_E, np.float32)
+    quant = O.orc_kv_quant_int8 if dtype == ct.CT_KV_INT8 else O.orc_kv_quant_e4m3
+    dequant = O.orc_kv_dequant_int8 if dtype == ct.CT_KV_INT8 else O.orc_kv_dequant_e4m3
+    quant(xf.ctypes.data, NP * PAGE, MLA_E, codes.ctypes.data, sc.ctypes.data)
+    dequant(codes.ctypes.data, sc.ctypes.data, NP * PAGE, MLA_E, back.ctypes.data)
+    got, plan = run_decode(codes.reshape(NP, PAGE, MLA_E), bt, lens, q, dtype=dtype, scales=sc)
+    assert plan.tensor_cores
     want = oracle_decode_f32(back.reshape(NP, PAGE, MLA_E), bt, lens, oracle.bf16_to_f32(q.reshape(-1)).reshape(
         q.shape), MLA_H, MLA_E, MLA_DV, PAGE)
     ok, mx, rel = close(got, want)
