@@ -28,13 +28,13 @@
  * in one of two receive slots, so the copy of tile j+1 does not wait for
  * tile j to be consumed.
  *
- * Roles per CTA (352 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+ * Roles per CTA (608 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
- * each), warps 3-10 finish scores, softmax and epilogue: two threads per
- * head row (TMEM lane), one per 32-token half of a tile.
+ * each), warps 3-18 finish scores, softmax and epilogue: four threads per
+ * head row (TMEM lane), one per 16-token quarter of a tile.
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
- * 36 KB, an exchange out buffer and two in slots of 32 KB, a 3 KB
+ * 36 KB, an exchange out buffer and two in slots of 32 KB, a 6 KB
  * row-statistics buffer, barriers.  TMEM: S / P at columns 0 and 64, Q at
  * 128, O at 256..511.
  *
@@ -54,12 +54,15 @@
 namespace {
 
 constexpr int kH = 128, kE = 576, kDv = 512, kP = 64;
-constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxWarps = 16;
+constexpr int kParts = kSoftmaxWarps / 4;               /* threads per head row (one per TMEM lane quadrant warp) */
+constexpr int kTPT = 64 / kParts;                       /* tokens of a page per thread */
+constexpr int kOCols = 256 / kParts;                    /* O columns (value dims) per thread */
 constexpr int kFirstSoftmaxWarp = 3;
-constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 352 */
+constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 608 */
 constexpr int kConvWarps = 2;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
 constexpr int kFirstConvWarp = kFirstSoftmaxWarp + kSoftmaxWarps;
-constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 416 */
+constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 672 */
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
 constexpr uint32_t kCodeBytes = 4 * 4096 + 2048 + 256;  /* quantised page half: codes + 64 scales */
@@ -70,7 +73,7 @@ constexpr uint32_t kOffKv = kOffQ + kQBytes;
 constexpr uint32_t kOffOut = kOffKv + kStages * kKvBytes;
 constexpr uint32_t kOffIn = kOffOut + kXBytes;         /* two receive slots */
 constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
-constexpr uint32_t kRedBytes = 6 * kH * 4;              /* row max [2 parities][2 halves], row sum [2 halves] */
+constexpr uint32_t kRedBytes = 3 * kParts * kH * 4;     /* row max [2 parities][parts], row sum [parts] */
 constexpr uint32_t kOffScale = kOffRed + kRedBytes;    /* per stage: 64 fp32 token scales (quantised pools) */
 constexpr uint32_t kOffBar = kOffScale + kStages * 256;
 constexpr uint32_t kNumBars = 40;
@@ -224,6 +227,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
           "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
           "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    #pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
     asm volatile(
@@ -562,7 +581,7 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
 __device__ __forceinline__ uint32_t xoff(uint32_t row, uint32_t c) { return row * 256 + ((c ^ (row & 15)) << 4); }
 
 struct Row {
-    uint32_t row, half, quad, lane_base, tid;
+    uint32_t row, part, quad, lane_base, tid;
     float m_used, l;
 };
 
@@ -572,56 +591,57 @@ template <int KV>
 __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r, uint32_t t, uint32_t jj, float *s,
                             int32_t ntok) {
     constexpr bool kQuant = KV != CT_KV_BF16;
-    const float *tok_scale = reinterpret_cast<const float *>(c.smem + kOffScale + (t % kStages) * 256) + r.half * 32;
+    const float *tok_scale = reinterpret_cast<const float *>(c.smem + kOffScale + (t % kStages) * 256) + r.part * kTPT;
     const uint32_t lane = threadIdx.x & 31;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
     const uint32_t slot = t & 1;
     if (!wait_warp(c, bar(c, B_X_FULL + slot), (t >> 1) & 1, true, 10)) return false;
     const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn + slot * kXBytes);
     #pragma unroll
-    for (int q4 = 0; q4 < 8; q4++) {
-        const float4 w = xin[xoff(r.row, r.half * 8 + q4) >> 4];
+    for (int q4 = 0; q4 < kTPT / 4; q4++) {
+        const float4 w = xin[xoff(r.row, r.part * (kTPT / 4) + q4) >> 4];
         s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY + slot), c.peer));
     if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL + slot), kXBytes);   /* arm for tile t + 2 */
-    /* scaled scores, masked beyond the page's tokens; row maximum over both halves */
+    /* scaled scores, masked beyond the page's tokens; row maximum over all parts */
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     #pragma unroll
-    for (int i = 0; i < 32; i++) {
+    for (int i = 0; i < kTPT; i++) {
         /* quantised pages: the scores are code dot products; times the token's scale */
         const float v = kQuant ? s[i] * tok_scale[i] : s[i];
-        s[i] = ((int32_t)(r.half * 32 + i) < ntok) ? v * p.qk_scale : -INFINITY;
+        s[i] = ((int32_t)(r.part * kTPT + i) < ntok) ? v * p.qk_scale : -INFINITY;
         m4[i & 3] = fmaxf(m4[i & 3], s[i]);
     }
     float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-    /* the other half of each row is in the partner warp of this quadrant */
-    float *rm = red + (t & 1) * 2 * kH;
-    rm[r.half * kH + r.row] = mx;
+    /* the other parts of each row are in the other warps of this quadrant */
+    float *rm = red + (t & 1) * kParts * kH;
+    rm[r.part * kH + r.row] = mx;
     const uint32_t rb = bar(c, B_RED + (t & 1) * 4 + r.quad);
-    tc_fence_before();      /* the partner half writes P over scores this thread has read */
+    tc_fence_before();      /* the other parts write P over scores this thread has read */
     warp_arrive(rb);
     if (!wait_warp(c, rb, (t >> 1) & 1, false, 16)) return false;
     tc_fence_after();
-    mx = fmaxf(mx, rm[(r.half ^ 1) * kH + r.row]);
+    #pragma unroll
+    for (int k = 1; k < kParts; k++) mx = fmaxf(mx, rm[((r.part + k) % kParts) * kH + r.row]);
     const bool grow = mx > r.m_used + kRescaleThreshold;   /* also true for the first tile */
     const float m_new = grow ? mx : r.m_used;
     const float alpha = grow ? exp2f(r.m_used - m_new) : 1.0f;   /* 0 on the first tile */
     if (__any_sync(0xFFFFFFFFu, grow && jj > 0)) {
-        /* O holds tiles before t: wait for GEMM2(t-1), rescale this thread's half row */
+        /* O holds tiles before t: wait for GEMM2(t-1), rescale this thread's part of the row */
         if (!wait_warp(c, bar(c, B_O_READY), (t - 1) & 1, false, 11)) return false;
         tc_fence_after();
         const float a = grow ? alpha : 1.0f;
         #pragma unroll 1
-        for (int cc = 0; cc < 4; cc++) {
-            float o[32];
-            uint32_t u[32];
-            tmem_ld32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, o);
+        for (int cc = 0; cc < kOCols / 16; cc++) {
+            float o[16];
+            uint32_t u[16];
+            tmem_ld16(tmem + r.lane_base + kTmemO + r.part * kOCols + cc * 16, o);
             tmem_wait_ld();
             #pragma unroll
-            for (int i = 0; i < 32; i++) u[i] = __float_as_uint(o[i] * a);
-            tmem_st32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, u);
+            for (int i = 0; i < 16; i++) u[i] = __float_as_uint(o[i] * a);
+            tmem_st16(tmem + r.lane_base + kTmemO + r.part * kOCols + cc * 16, u);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -631,26 +651,26 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     /* P = bf16(2^(s - m)) into the first 32 score columns of tile t (this
      * thread read its scores in stage_tile; GEMM2 of tile t-2, which read
      * the previous P there, completed before GEMM1 of tile t did) */
-    uint32_t w[16];
+    uint32_t w[kTPT / 2];
     float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (!kQuant) {
         #pragma unroll
-        for (int k = 0; k < 16; k++) {
+        for (int k = 0; k < kTPT / 2; k++) {
             w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
             l4[k & 3] += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
         }
     } else {
         /* V = scale x codes: the scale folds into P; the normaliser sums P itself */
         #pragma unroll
-        for (int k = 0; k < 16; k++) {
+        for (int k = 0; k < kTPT / 2; k++) {
             const float p0 = exp2f(s[2 * k] - r.m_used), p1 = exp2f(s[2 * k + 1] - r.m_used);
             l4[k & 3] += p0 + p1;
-            const bool in0 = (int32_t)(r.half * 32 + 2 * k) < ntok, in1 = (int32_t)(r.half * 32 + 2 * k + 1) < ntok;
+            const bool in0 = (int32_t)(r.part * kTPT + 2 * k) < ntok, in1 = (int32_t)(r.part * kTPT + 2 * k + 1) < ntok;
             w[k] = bf16x2_rn(in0 ? p0 * tok_scale[2 * k] : 0.0f, in1 ? p1 * tok_scale[2 * k + 1] : 0.0f);
         }
     }
     r.l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-    tmem_st16(tmem + r.lane_base + kTmemS + (t & 1) * 64 + r.half * 16, w);
+    tmem_st8(tmem + r.lane_base + kTmemS + (t & 1) * 64 + r.part * (kTPT / 2), w);
     /* a partial page: zero the V rows past its tokens (stale slots may hold
      * anything; the converter already wrote zeros there for quantised pages) */
     if (!kQuant && ntok < kP) {
@@ -675,13 +695,13 @@ __device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t g
     const uint32_t sb = gt & 1;
     if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) return false;
     tc_fence_after();
-    tmem_ld32(tmem + r.lane_base + kTmemS + sb * 64 + r.half * 32, s);
+    tmem_ld16(tmem + r.lane_base + kTmemS + sb * 64 + r.part * kTPT, s);
     tmem_wait_ld();
     if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) return false;
     float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
     #pragma unroll
-    for (int q4 = 0; q4 < 8; q4++)
-        xout[xoff(r.row, r.half * 8 + q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
+    for (int q4 = 0; q4 < kTPT / 4; q4++)
+        xout[xoff(r.row, r.part * (kTPT / 4) + q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
     proxy_fence();
     warp_arrive(bar(c, B_SO_FULL));
     return true;
@@ -692,7 +712,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3;                     /* TMEM lane quadrant this warp may access */
     Row r;
-    r.half = (warp - kFirstSoftmaxWarp) >> 2;           /* tokens [32h, 32h+32) of a tile, O columns [128h, +128) */
+    r.part = (warp - kFirstSoftmaxWarp) >> 2;           /* tokens [16k, 16k+16) of a tile, O columns [64k, +64) */
     r.row = quad * 32 + lane;                           /* head */
     r.quad = quad;
     r.lane_base = (quad * 32) << 16;
@@ -706,17 +726,17 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
         it.init(ch, p);
         int32_t pg, ntok;
         const size_t oh = (size_t)ch.seq * kH + r.row;
-        const uint32_t d_base = rank * 256 + r.half * 128;
+        const uint32_t d_base = rank * 256 + r.part * kOCols;
         if (!it.next(pg, ntok)) {
             /* nothing readable: zero output */
             if (ch.part < 0) {
                 uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d_base);
-                for (int k = 0; k < 16; k++) dst[k] = make_uint4(0, 0, 0, 0);
+                for (int k = 0; k < kOCols / 8; k++) dst[k] = make_uint4(0, 0, 0, 0);
             } else {
                 float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + r.row) * kDv + d_base);
-                for (int k = 0; k < 32; k++) dst[k] = make_float4(0, 0, 0, 0);
+                for (int k = 0; k < kOCols / 4; k++) dst[k] = make_float4(0, 0, 0, 0);
             }
-            if (rank == 0 && r.half == 0) {
+            if (rank == 0 && r.part == 0) {
                 if (ch.part < 0) {
                     if (p.lse) p.lse[oh] = -INFINITY;
                 } else {
@@ -727,31 +747,31 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             continue;
         }
         /* the latent dims of this CTA's half of Q into TMEM, once the
-         * previous chunk's GEMM1s are done: this thread's 128 dims */
+         * previous chunk's GEMM1s are done: this thread's 256 / kParts dims */
         if (!wait_warp(c, bar(c, B_Q_EMPTY), (nchunk & 1) ^ 1, false, 17)) { ok = false; break; }
         tc_fence_after();
         #pragma unroll 1
-        for (int part = 0; part < 2; part++) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.half * 128 + part * 64);
+        for (int q64 = 0; q64 < kOCols / 64; q64++) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.part * kOCols + q64 * 64);
             uint32_t u[32];
             #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const uint4 v = __ldg(src + k);
                 u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
             }
-            tmem_st32(tmem + r.lane_base + kTmemQ + r.half * 64 + part * 32, u);
+            tmem_st32(tmem + r.lane_base + kTmemQ + r.part * (kOCols / 2) + q64 * 32, u);
         }
         tmem_wait_st();
         tc_fence_before();
         warp_arrive(bar(c, B_QT_FULL));
         r.m_used = -INFINITY;
         r.l = 0.0f;
-        float s_prev[32];
+        float s_prev[kTPT];
         int32_t prev_ntok = 0;
         uint32_t j = 0;
         do {
             const uint32_t gt = g + j;
-            float s_cur[32];
+            float s_cur[kTPT];
             if (j == 0) {
                 if (!stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
             } else {
@@ -780,26 +800,28 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                 }
             }
             #pragma unroll
-            for (int i = 0; i < 32; i++) s_prev[i] = s_cur[i];
+            for (int i = 0; i < kTPT; i++) s_prev[i] = s_cur[i];
             prev_ntok = ntok;
             j++;
         } while (it.next(pg, ntok));
         if (!ok) break;
         if (!finish_tile<KV>(c, p, tmem, r, g + j - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
         g += j;
-        /* epilogue: the row sum over both halves, then O of this CTA's 256 value dims */
-        float *rl = red + 4 * kH;
-        rl[r.half * kH + r.row] = r.l;
+        /* epilogue: the row sum over all parts, then O of this CTA's 256 value dims */
+        float *rl = red + 2 * kParts * kH;
+        rl[r.part * kH + r.row] = r.l;
         warp_arrive(bar(c, B_RED_L + r.quad));
         if (!wait_warp(c, bar(c, B_RED_L + r.quad), nchunk & 1, false, 18)) { ok = false; break; }
-        const float l_tot = r.l + rl[(r.half ^ 1) * kH + r.row];
+        float l_tot = r.l;
+        #pragma unroll
+        for (int k = 1; k < kParts; k++) l_tot += rl[((r.part + k) % kParts) * kH + r.row];
         if (!wait_warp(c, bar(c, B_O_FINAL), nchunk & 1, false, 13)) { ok = false; break; }
         tc_fence_after();
         const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
         #pragma unroll 1
-        for (int cc = 0; cc < 4; cc++) {
+        for (int cc = 0; cc < kOCols / 32; cc++) {
             float o[32];
-            tmem_ld32(tmem + r.lane_base + kTmemO + r.half * 128 + cc * 32, o);
+            tmem_ld32(tmem + r.lane_base + kTmemO + r.part * kOCols + cc * 32, o);
             tmem_wait_ld();
             const uint32_t d0 = d_base + cc * 32;
             if (ch.part < 0) {
@@ -822,7 +844,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
         tc_fence_before();
         warp_arrive(bar(c, B_O_FREE));
         /* statistics that one thread per row writes */
-        if (rank == 0 && r.half == 0) {
+        if (rank == 0 && r.part == 0) {
             if (ch.part < 0) {
                 if (p.lse) p.lse[oh] = l_tot > 0.0f ? r.m_used * kLn2 + logf(l_tot) : -INFINITY;
             } else {
@@ -952,8 +974,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
             mbar_init(bar(c, B_X_FULL + i), 1);
             mbar_init(bar(c, B_X_EMPTY + i), kSoftmaxWarps);
         }
-        for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), 2);      /* the two warps of a quadrant */
-        for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), 2);
+        for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), kParts);     /* the warps of a quadrant */
+        for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), kParts);
         mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
         mbar_init(bar(c, B_SO_FULL), kSoftmaxWarps); mbar_init(bar(c, B_SO_EMPTY), 1);
