@@ -570,6 +570,14 @@ __device__ __forceinline__ void warp_arrive(uint32_t b) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(b);
 }
 
+/* 2^x by the hardware approximation (relative error ~2^-22; the result is
+ * rounded to bf16 for the tensor cores anyway); -inf gives 0. */
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 /* Two floats -> packed bf16 pair (lo in the low half), round to nearest even. */
 __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
     uint32_t d;
@@ -605,15 +613,23 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     __syncwarp();
     if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY + slot), c.peer));
     if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL + slot), kXBytes);   /* arm for tile t + 2 */
-    /* scaled scores, masked beyond the page's tokens; row maximum over all parts */
+    /* quantised pages: the scores are code dot products; times the token's scale */
+    if (kQuant) {
+        #pragma unroll
+        for (int i = 0; i < kTPT; i++) s[i] *= tok_scale[i];
+    }
+    /* the last page of a sequence masks the slots past its end (warp-uniform) */
+    const bool partial = ntok < kP;
+    if (partial) {
+        #pragma unroll
+        for (int i = 0; i < kTPT; i++)
+            if ((int32_t)(r.part * kTPT + i) >= ntok) s[i] = -INFINITY;
+    }
+    /* row maximum over all parts, of the unscaled scores (the softmax scale is
+     * positive, so it commutes with the maximum) */
     float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     #pragma unroll
-    for (int i = 0; i < kTPT; i++) {
-        /* quantised pages: the scores are code dot products; times the token's scale */
-        const float v = kQuant ? s[i] * tok_scale[i] : s[i];
-        s[i] = ((int32_t)(r.part * kTPT + i) < ntok) ? v * p.qk_scale : -INFINITY;
-        m4[i & 3] = fmaxf(m4[i & 3], s[i]);
-    }
+    for (int i = 0; i < kTPT; i++) m4[i & 3] = fmaxf(m4[i & 3], s[i]);
     float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
     /* the other parts of each row are in the other warps of this quadrant */
     float *rm = red + (t & 1) * kParts * kH;
@@ -625,9 +641,10 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     tc_fence_after();
     #pragma unroll
     for (int k = 1; k < kParts; k++) mx = fmaxf(mx, rm[((r.part + k) % kParts) * kH + r.row]);
+    mx *= p.qk_scale;                                       /* log2 domain */
     const bool grow = mx > r.m_used + kRescaleThreshold;   /* also true for the first tile */
     const float m_new = grow ? mx : r.m_used;
-    const float alpha = grow ? exp2f(r.m_used - m_new) : 1.0f;   /* 0 on the first tile */
+    const float alpha = grow ? ex2_approx(r.m_used - m_new) : 1.0f;   /* 0 on the first tile */
     if (__any_sync(0xFFFFFFFFu, grow && jj > 0)) {
         /* O holds tiles before t: wait for GEMM2(t-1), rescale this thread's part of the row */
         if (!wait_warp(c, bar(c, B_O_READY), (t - 1) & 1, false, 11)) return false;
@@ -648,23 +665,23 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     }
     r.l *= alpha;
     r.m_used = m_new;
-    /* P = bf16(2^(s - m)) into the first 32 score columns of tile t (this
-     * thread read its scores in stage_tile; GEMM2 of tile t-2, which read
-     * the previous P there, completed before GEMM1 of tile t did) */
+    /* P = bf16(2^(scale * s - m)) into the first 32 score columns of tile t
+     * (this thread read its scores in stage_tile; GEMM2 of tile t-2, which
+     * read the previous P there, completed before GEMM1 of tile t did).  The
+     * normaliser sums the fp32 probabilities. */
     uint32_t w[kTPT / 2];
     float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (!kQuant) {
-        #pragma unroll
-        for (int k = 0; k < kTPT / 2; k++) {
-            w[k] = bf16x2_rn(exp2f(s[2 * k] - r.m_used), exp2f(s[2 * k + 1] - r.m_used));
-            l4[k & 3] += __uint_as_float(w[k] << 16) + __uint_as_float(w[k] & 0xFFFF0000u);
-        }
-    } else {
-        /* V = scale x codes: the scale folds into P; the normaliser sums P itself */
-        #pragma unroll
-        for (int k = 0; k < kTPT / 2; k++) {
-            const float p0 = exp2f(s[2 * k] - r.m_used), p1 = exp2f(s[2 * k + 1] - r.m_used);
-            l4[k & 3] += p0 + p1;
+    const float qk = p.qk_scale, nm = -r.m_used;
+    #pragma unroll
+    for (int k = 0; k < kTPT / 2; k++) {
+        const float p0 = ex2_approx(fmaf(s[2 * k], qk, nm)), p1 = ex2_approx(fmaf(s[2 * k + 1], qk, nm));
+        l4[k & 3] += p0 + p1;
+        if (!kQuant) {
+            w[k] = bf16x2_rn(p0, p1);
+        } else if (!partial) {
+            /* V = scale x codes: the scale folds into P */
+            w[k] = bf16x2_rn(p0 * tok_scale[2 * k], p1 * tok_scale[2 * k + 1]);
+        } else {
             const bool in0 = (int32_t)(r.part * kTPT + 2 * k) < ntok, in1 = (int32_t)(r.part * kTPT + 2 * k + 1) < ntok;
             w[k] = bf16x2_rn(in0 ? p0 * tok_scale[2 * k] : 0.0f, in1 ? p1 * tok_scale[2 * k + 1] : 0.0f);
         }
@@ -1050,7 +1067,7 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint32_t box_cols
 
 bool shape_ok(const ct_mla_dims_t *d) {
     return d->n_heads == (uint32_t)kH && d->entry_dim == (uint32_t)kE && d->v_dim == (uint32_t)kDv &&
-           d->page_tokens == (uint32_t)kP &&
+           d->page_tokens == (uint32_t)kP && d->scale > 0.0f &&
            (d->kv_dtype == CT_KV_BF16 || d->kv_dtype == CT_KV_INT8 || d->kv_dtype == CT_KV_E4M3);
 }
 
