@@ -106,6 +106,8 @@ SIGNATURES = {
     "ct_kv_paged_compact": (I, [P]),
     "ct_kv_paged_gather": (I, [P, U32, U32, U32, P, U32]),
     "ct_kv_paged_gather_batch": (I, [P, P, P, P, U32, P, U32]),
+    "ct_kv_paged_save": (I, [P, C.c_char_p]),
+    "ct_kv_paged_load": (P, [C.c_char_p, C.c_int]),
     "ct_kv_paged_block_table": (I, [P, P]),
     "ct_kv_paged_seq_lens": (I, [P, P]),
     "ct_kv_paged_last_access": (I, [P, P]),
@@ -281,14 +283,26 @@ class PagedKV:
     """ct_kv_paged_* handle."""
 
     def __init__(self, n_seqs, max_pages_per_seq, n_pages, page_tokens=64, entry_dim=576, window_tokens=0,
-                 dtype=CT_KV_BF16, device=0, stream=None):
+                 dtype=CT_KV_BF16, device=0, stream=None, _handle=None):
         self.cfg = PagedConfig(n_seqs, max_pages_per_seq, n_pages, page_tokens, entry_dim, window_tokens, dtype,
                                device)
-        self.h = lib().ct_kv_paged_create(C.byref(self.cfg))
+        self.h = _handle if _handle is not None else lib().ct_kv_paged_create(C.byref(self.cfg))
         if not self.h:
             raise RuntimeError("ct_kv_paged_create failed: " + lib().ct_hal_cuda_last_error().decode())
         if stream is not None:
             check(lib().ct_kv_paged_set_stream(self.h, stream), "set_stream")
+
+    def save(self, path):
+        check(lib().ct_kv_paged_save(self.h, str(path).encode()), "ct_kv_paged_save")
+
+    @classmethod
+    def load(cls, path, device=0, stream=None):
+        h = lib().ct_kv_paged_load(str(path).encode(), device)
+        if not h:
+            raise RuntimeError("ct_kv_paged_load failed: " + lib().ct_hal_cuda_last_error().decode())
+        c = lib().ct_kv_paged_config(h).contents
+        return cls(c.n_seqs, c.max_pages_per_seq, c.n_pages, c.page_tokens, c.entry_dim, c.window_tokens, c.dtype,
+                   device, stream, _handle=h)
 
     def close(self):
         if self.h:

@@ -30,6 +30,7 @@
 #include "../csrc/ct_internal.h"
 
 #include <cuda_runtime_api.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -609,3 +610,223 @@ void *ct_kv_paged_pool(ct_kv_paged_t *h) { return h ? h->pool : NULL; }
 float *ct_kv_paged_scales(ct_kv_paged_t *h) { return h ? h->scales : NULL; }
 const int32_t *ct_kv_paged_block_table_dev(const ct_kv_paged_t *h) { return h ? h->bt_dev : NULL; }
 const int32_t *ct_kv_paged_seq_lens_dev(const ct_kv_paged_t *h) { return h ? h->len_dev : NULL; }
+
+/* ---- checkpoint --------------------------------------------------------- */
+
+/* File layout (little-endian, no padding): "CTKVPAGE", u32 version (1),
+ * u32 flags (bit 0: page bytes present); the 8 config words; the statistics
+ * (5 x u64, 2 x u32, u64); per sequence len, lo, hi (u32) and last_access
+ * (u64); the block table (i32, n_seqs x max_pages); the free-order rank of
+ * every page (u32); the free set (u32 count, i32 ids); the eviction log (u32
+ * count, 5 x u32 each); the live pages (u32 count, then per page its id (i32),
+ * page bytes, and page_tokens fp32 scales for int8 / e4m3 pools); last an
+ * FNV-1a 64 of everything before it. */
+
+#define CKPT_MAGIC "CTKVPAGE"
+#define CKPT_VERSION 1u
+
+typedef struct {
+    FILE *f;
+    uint64_t fnv;
+    int err;
+} ckpt_io_t;
+
+static void fnv_feed(ckpt_io_t *io, const void *p, size_t n) {
+    const uint8_t *b = (const uint8_t *)p;
+    for (size_t i = 0; i < n; i++) { io->fnv ^= b[i]; io->fnv *= 0x100000001B3ull; }
+}
+static void ck_write(ckpt_io_t *io, const void *p, size_t n) {
+    if (io->err || n == 0) return;
+    if (fwrite(p, 1, n, io->f) != n) { io->err = 1; return; }
+    fnv_feed(io, p, n);
+}
+static void ck_read(ckpt_io_t *io, void *p, size_t n) {
+    if (io->err || n == 0) return;
+    if (fread(p, 1, n, io->f) != n) { io->err = 1; return; }
+    fnv_feed(io, p, n);
+}
+
+int ct_kv_paged_save(ct_kv_paged_t *h, const char *path) {
+    if (!h || !path) return CT_ERR_ARG;
+    const uint32_t S = h->cfg.n_seqs, MP = h->cfg.max_pages_per_seq, NP = h->cfg.n_pages, P = h->cfg.page_tokens;
+    if (!h->host_only) {                               /* every queued write has landed */
+        int rc = ct__cuda_status(cudaStreamSynchronize(h->stream), "ct_kv_paged_save");
+        if (rc) return rc;
+    }
+    FILE *f = fopen(path, "wb");
+    if (!f) { ct__set_error("ct_kv_paged_save: cannot open the file"); return CT_ERR_IO; }
+    ckpt_io_t io = {f, 0xCBF29CE484222325ull, 0};
+    const uint32_t ver = CKPT_VERSION, flags = h->host_only ? 0u : 1u;
+    ck_write(&io, CKPT_MAGIC, 8);
+    ck_write(&io, &ver, 4);
+    ck_write(&io, &flags, 4);
+    const uint32_t cfgw[8] = {h->cfg.n_seqs, h->cfg.max_pages_per_seq, h->cfg.n_pages, h->cfg.page_tokens,
+                              h->cfg.entry_dim, h->cfg.window_tokens, h->cfg.dtype, (uint32_t)h->cfg.device};
+    ck_write(&io, cfgw, sizeof cfgw);
+    const uint64_t st64[5] = {h->st.n_appends, h->st.n_evict_window, h->st.n_evict_lru, h->st.n_compactions,
+                              h->st.bytes_compacted};
+    const uint32_t st32[2] = {h->st.n_pages_live, h->st.n_pages_free};
+    ck_write(&io, st64, sizeof st64);
+    ck_write(&io, st32, sizeof st32);
+    ck_write(&io, &h->st.clock, 8);
+    ck_write(&io, h->len, (size_t)S * 4);
+    ck_write(&io, h->lo, (size_t)S * 4);
+    ck_write(&io, h->hi, (size_t)S * 4);
+    ck_write(&io, h->last_access, (size_t)S * 8);
+    ck_write(&io, h->bt, (size_t)S * MP * 4);
+    ck_write(&io, h->rank, (size_t)NP * 4);
+    ck_write(&io, &h->heap_n, 4);
+    ck_write(&io, h->heap, (size_t)h->heap_n * 4);
+    ck_write(&io, &h->log_n, 4);
+    for (uint32_t i = 0; i < h->log_n && !io.err; i++) {
+        const uint32_t e[5] = {h->log[i].round, h->log[i].seq, h->log[i].lpage, (uint32_t)h->log[i].phys,
+                               h->log[i].reason};
+        ck_write(&io, e, sizeof e);
+    }
+    uint32_t n_live = 0;
+    for (size_t i = 0; i < (size_t)S * MP; i++) n_live += h->bt[i] >= 0;
+    ck_write(&io, &n_live, 4);
+    int rc = CT_OK;
+    if (!h->host_only && n_live) {
+        const size_t sc_bytes = h->scales ? (size_t)P * sizeof(float) : 0;
+        uint8_t *buf = (uint8_t *)malloc(h->page_bytes + sc_bytes);
+        if (!buf) { fclose(f); return CT_ERR_NOMEM; }
+        for (size_t i = 0; i < (size_t)S * MP && !rc && !io.err; i++) {
+            const int32_t pg = h->bt[i];
+            if (pg < 0) continue;
+            rc = ct__cuda_status(cudaMemcpy(buf, (const uint8_t *)h->pool + (size_t)pg * h->page_bytes,
+                                            h->page_bytes, cudaMemcpyDeviceToHost), "ct_kv_paged_save page");
+            if (!rc && sc_bytes)
+                rc = ct__cuda_status(cudaMemcpy(buf + h->page_bytes, h->scales + (size_t)pg * P, sc_bytes,
+                                                cudaMemcpyDeviceToHost), "ct_kv_paged_save scales");
+            ck_write(&io, &pg, 4);
+            ck_write(&io, buf, h->page_bytes + sc_bytes);
+        }
+        free(buf);
+    }
+    const uint64_t sum = io.fnv;
+    if (!io.err && fwrite(&sum, 8, 1, f) != 1) io.err = 1;
+    if (fclose(f) != 0) io.err = 1;
+    if (rc) return rc;
+    if (io.err) { ct__set_error("ct_kv_paged_save: write failed"); return CT_ERR_IO; }
+    return CT_OK;
+}
+
+ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
+    if (!path) return NULL;
+    FILE *f = fopen(path, "rb");
+    if (!f) { ct__set_error("ct_kv_paged_load: cannot open the file"); return NULL; }
+    ckpt_io_t io = {f, 0xCBF29CE484222325ull, 0};
+    char magic[8];
+    uint32_t ver = 0, flags = 0, cfgw[8];
+    ck_read(&io, magic, 8);
+    ck_read(&io, &ver, 4);
+    ck_read(&io, &flags, 4);
+    ck_read(&io, cfgw, sizeof cfgw);
+    if (io.err || memcmp(magic, CKPT_MAGIC, 8) != 0 || ver != CKPT_VERSION) {
+        fclose(f);
+        ct__set_error("ct_kv_paged_load: not a paged KV checkpoint of version 1");
+        return NULL;
+    }
+    ct_kv_paged_config_t cfg = {cfgw[0], cfgw[1], cfgw[2], cfgw[3], cfgw[4], cfgw[5], cfgw[6], device};
+    if ((flags & 1u) == 0 && device >= 0) {
+        fclose(f);
+        ct__set_error("ct_kv_paged_load: the checkpoint holds tables only (load it with device -1)");
+        return NULL;
+    }
+    ct_kv_paged_t *h = ct_kv_paged_create(&cfg);
+    if (!h) { fclose(f); return NULL; }
+    const uint32_t S = h->cfg.n_seqs, MP = h->cfg.max_pages_per_seq, NP = h->cfg.n_pages, P = h->cfg.page_tokens;
+    uint64_t st64[5];
+    uint32_t st32[2];
+    ck_read(&io, st64, sizeof st64);
+    ck_read(&io, st32, sizeof st32);
+    ck_read(&io, &h->st.clock, 8);
+    h->st.n_appends = st64[0]; h->st.n_evict_window = st64[1]; h->st.n_evict_lru = st64[2];
+    h->st.n_compactions = st64[3]; h->st.bytes_compacted = st64[4];
+    h->st.n_pages_live = st32[0]; h->st.n_pages_free = st32[1];
+    ck_read(&io, h->len, (size_t)S * 4);
+    ck_read(&io, h->lo, (size_t)S * 4);
+    ck_read(&io, h->hi, (size_t)S * 4);
+    ck_read(&io, h->last_access, (size_t)S * 8);
+    ck_read(&io, h->bt, (size_t)S * MP * 4);
+    ck_read(&io, h->rank, (size_t)NP * 4);
+    uint32_t free_n = 0, log_n = 0, n_live = 0;
+    ck_read(&io, &free_n, 4);
+    int bad = io.err || free_n > NP;
+    for (uint32_t i = 0; i < S && !bad; i++) bad = h->len[i] > MP * P || h->lo[i] > h->hi[i] || h->hi[i] > MP;
+    for (uint32_t p = 0; p < NP && !bad; p++) bad = h->rank[p] >= NP;
+    for (size_t i = 0; i < (size_t)S * MP && !bad; i++) bad = h->bt[i] < -1 || h->bt[i] >= (int32_t)NP;
+    if (!bad) {
+        ck_read(&io, h->heap, (size_t)free_n * 4);
+        for (uint32_t i = 0; i < free_n && !bad; i++) bad = h->heap[i] < 0 || h->heap[i] >= (int32_t)NP;
+    }
+    if (!bad) {                                        /* the free set back into rank order */
+        int32_t *ids = (int32_t *)malloc((size_t)(free_n ? free_n : 1) * 4);
+        bad = !ids;
+        if (ids) {
+            memcpy(ids, h->heap, (size_t)free_n * 4);
+            heap_rebuild(h, ids, free_n);
+            free(ids);
+        }
+        ck_read(&io, &log_n, 4);
+        bad = bad || io.err;
+    }
+    for (uint32_t i = 0; i < log_n && !bad; i++) {
+        uint32_t e[5];
+        ck_read(&io, e, sizeof e);
+        if (io.err) { bad = 1; break; }
+        if (h->log_n == h->log_cap) {
+            uint32_t cap = h->log_cap ? 2 * h->log_cap : 1024;
+            ct_kv_evict_event_t *nl = (ct_kv_evict_event_t *)realloc(h->log, (size_t)cap * sizeof *nl);
+            if (!nl) { bad = 1; break; }
+            h->log = nl;
+            h->log_cap = cap;
+        }
+        h->log[h->log_n++] = (ct_kv_evict_event_t){e[0], e[1], e[2], (int32_t)e[3], e[4]};
+    }
+    if (!bad) {
+        ck_read(&io, &n_live, 4);
+        bad = io.err || n_live > NP;
+    }
+    if (!bad && (flags & 1u) && n_live) {
+        const size_t sc_bytes = h->scales ? (size_t)P * sizeof(float) : 0;
+        uint8_t *buf = (uint8_t *)malloc(h->page_bytes + sc_bytes);
+        bad = !buf;
+        for (uint32_t i = 0; i < n_live && !bad; i++) {
+            int32_t pg = -1;
+            ck_read(&io, &pg, 4);
+            ck_read(&io, buf, h->page_bytes + sc_bytes);
+            if (io.err || pg < 0 || pg >= (int32_t)NP) { bad = 1; break; }
+            if (!h->host_only) {
+                bad = ct__cuda_status(cudaMemcpy((uint8_t *)h->pool + (size_t)pg * h->page_bytes, buf, h->page_bytes,
+                                                 cudaMemcpyHostToDevice), "ct_kv_paged_load page") != CT_OK;
+                if (!bad && sc_bytes)
+                    bad = ct__cuda_status(cudaMemcpy(h->scales + (size_t)pg * P, buf + h->page_bytes, sc_bytes,
+                                                     cudaMemcpyHostToDevice), "ct_kv_paged_load scales") != CT_OK;
+            }
+        }
+        free(buf);
+    }
+    if (!bad) {
+        const uint64_t want = io.fnv;
+        uint64_t sum = 0;
+        bad = fread(&sum, 8, 1, f) != 1 || sum != want;
+        if (bad) ct__set_error("ct_kv_paged_load: checksum mismatch");
+    } else {
+        ct__set_error("ct_kv_paged_load: truncated or inconsistent checkpoint");
+    }
+    fclose(f);
+    if (!bad && !h->host_only) {                       /* device mirrors of the tables */
+        int32_t *len32 = (int32_t *)malloc((size_t)S * 4);
+        bad = !len32;
+        if (len32) {
+            for (uint32_t i = 0; i < S; i++) len32[i] = (int32_t)h->len[i];
+            bad = ct__cuda_status(cudaMemcpy(h->bt_dev, h->bt, (size_t)S * MP * 4, cudaMemcpyHostToDevice), "load bt") ||
+                  ct__cuda_status(cudaMemcpy(h->len_dev, len32, (size_t)S * 4, cudaMemcpyHostToDevice), "load len");
+            free(len32);
+        }
+    }
+    if (bad) { ct_kv_paged_destroy(h); return NULL; }
+    return h;
+}

@@ -170,6 +170,17 @@ int  ct_kv_paged_compact(ct_kv_paged_t *h);
 int  ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t n,
                         void *out, uint32_t out_dtype);
 
+/* Checkpoint of a paged cache (new; no reference counterpart -- it extends
+ * the raw format of kv_cache.c:82-111, which ct_kv_save / ct_kv_load keep
+ * unchanged): a versioned header ("CTKVPAGE", version 1), the configuration,
+ * statistics, lengths, page ranges, LRU clocks, block table, free order, free
+ * set and eviction log, then the bytes (and scales) of every live page, and a
+ * checksum.  Loading restores the same state: later appends, evictions and
+ * reads behave exactly as on the saved handle.  A handle with device < 0
+ * saves tables only, which load with device -1. */
+int            ct_kv_paged_save(ct_kv_paged_t *h, const char *path);
+ct_kv_paged_t *ct_kv_paged_load(const char *path, int device);   /* NULL on failure */
+
 /* The same for n ranges at once (host arrays): tokens [starts[i],
  * starts[i] + counts[i]) of sequence seqs[i], written back to back in range
  * order into out (device).  One launch per 65,535 ranges.  New; no reference

@@ -208,3 +208,58 @@ def test_product_allocator_free_and_evict_api():
     assert h.seq_lens().tolist() == [0, 4, 6] and (h.block_table()[0] < 0).all()
     assert h.stats().n_pages_free == 6 - 1
     h.close()
+
+
+# ---- paged checkpoint (tables only: host-only handle) ------------------------
+
+def _state(h):
+    st = h.stats()
+    return (h.block_table().tolist(), h.seq_lens().tolist(), h.last_access().tolist(), h.evict_log(),
+            (st.n_appends, st.n_evict_window, st.n_evict_lru, st.n_pages_live, st.n_pages_free, st.clock))
+
+
+def test_paged_checkpoint_round_trip_and_resume(tmp_path):
+    """Save mid-run under window and LRU pressure, load into a new handle:
+    same tables, lengths, clocks, eviction log and statistics, and the same
+    future -- further appends evict and place pages exactly as on the
+    original handle."""
+    S, P, NP, W = 33, 4, 50, 20
+    lens = oracle.lengths_loguniform(oracle.key(3, S), S, 1, 200)
+    MP = (200 + P - 1) // P + 1
+    h = host_paged(S, MP, NP, P, W)
+    h.set_free_order(oracle.permutation(oracle.key(9, 1), NP))
+    half = [int(n) // 2 for n in lens]
+    ids = [s for s in range(S) if half[s] > 0]
+    h.append(ids, [half[s] for s in ids])
+    path = tmp_path / "kv.ckpt"
+    h.save(path)
+    g = ct.PagedKV.load(path, device=-1)
+    assert _state(g) == _state(h)
+    rest = [int(n) - half[s] for s, n in enumerate(lens)]
+    ids2 = [s for s in range(S) if rest[s] > 0]
+    for handle in (h, g):
+        handle.append(ids2, [rest[s] for s in ids2])
+    assert _state(g) == _state(h)
+    assert ct.lib().ct_kv_paged_compact(h.h) == 0 and ct.lib().ct_kv_paged_compact(g.h) == 0
+    assert _state(g) == _state(h)
+    h.close()
+    g.close()
+
+
+def test_paged_checkpoint_rejects_damage(tmp_path):
+    h = host_paged(4, 8, 10, 4, 0)
+    h.append([0, 1, 2], [5, 9, 1])
+    path = tmp_path / "kv.ckpt"
+    h.save(path)
+    raw = bytearray(path.read_bytes())
+    L = ct.lib()
+    for pos in (0, 20, len(raw) // 2, len(raw) - 1):       # magic, config, tables, checksum
+        bad = bytearray(raw)
+        bad[pos] ^= 0x5A
+        (tmp_path / "bad.ckpt").write_bytes(bytes(bad))
+        assert not L.ct_kv_paged_load(str(tmp_path / "bad.ckpt").encode(), -1)
+    (tmp_path / "short.ckpt").write_bytes(bytes(raw[:-9]))
+    assert not L.ct_kv_paged_load(str(tmp_path / "short.ckpt").encode(), -1)
+    assert not L.ct_kv_paged_load(str(tmp_path / "missing.ckpt").encode(), -1)
+    assert L.ct_kv_paged_save(h.h, str(tmp_path / "no_such_dir" / "x").encode()) == ct.CT_ERR_IO
+    h.close()
