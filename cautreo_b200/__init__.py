@@ -107,6 +107,8 @@ SIGNATURES = {
     "ct_kv_paged_gather": (I, [P, U32, U32, U32, P, U32]),
     "ct_kv_paged_gather_batch": (I, [P, P, P, P, U32, P, U32]),
     "ct_kv_paged_save": (I, [P, C.c_char_p]),
+    "ct_kv_paged_fork": (I, [P, U32, U32, U32]),
+    "ct_kv_paged_page_refs": (U32, [P, I32]),
     "ct_kv_paged_load": (P, [C.c_char_p, C.c_int]),
     "ct_kv_paged_block_table": (I, [P, P]),
     "ct_kv_paged_seq_lens": (I, [P, P]),
@@ -291,6 +293,12 @@ class PagedKV:
             raise RuntimeError("ct_kv_paged_create failed: " + lib().ct_hal_cuda_last_error().decode())
         if stream is not None:
             check(lib().ct_kv_paged_set_stream(self.h, stream), "set_stream")
+
+    def fork(self, src, dst, n_tokens):
+        check(lib().ct_kv_paged_fork(self.h, src, dst, n_tokens), "ct_kv_paged_fork")
+
+    def page_refs(self, page):
+        return int(lib().ct_kv_paged_page_refs(self.h, page))
 
     def save(self, path):
         check(lib().ct_kv_paged_save(self.h, str(path).encode()), "ct_kv_paged_save")

@@ -60,6 +60,7 @@ struct ct_kv_paged {
     uint32_t *len, *lo, *hi;
     uint64_t *last_access;
     uint32_t *rank;             /* free-order rank of each physical page */
+    uint32_t *refc;             /* sequences mapping each physical page (prefix sharing) */
     int32_t *heap;              /* free pages, min-heap by rank */
     uint32_t heap_n;
     ct_kv_evict_event_t *log;
@@ -144,25 +145,30 @@ static int log_event(ct_kv_paged_t *h, uint32_t s, uint32_t lp, int32_t ph, uint
     return CT_OK;
 }
 
-/* Frees logical page lo[s] of sequence s. */
+/* Unmaps logical page lo[s] of sequence s; the physical page returns to the
+ * free set when no other sequence maps it. */
 static int free_low_page(ct_kv_paged_t *h, uint32_t s, uint32_t reason) {
     uint32_t lp = h->lo[s];
     int32_t ph = h->bt[(size_t)s * h->cfg.max_pages_per_seq + lp];
     if (reason && log_event(h, s, lp, ph, reason)) return CT_ERR_NOMEM;
     if (set_bt(h, s, lp, -1)) return CT_ERR_NOMEM;
     h->lo[s]++;
-    heap_push(h, ph);
-    h->st.n_pages_live--;
+    if (--h->refc[ph] == 0) {
+        heap_push(h, ph);
+        h->st.n_pages_live--;
+    }
     return CT_OK;
 }
 
-/* LRU victim: sequence with a full lowest page, minimising (last_access, seq). */
+/* LRU victim: sequence with a full lowest page that no other sequence maps
+ * (evicting it frees memory), minimising (last_access, seq). */
 static int64_t lru_victim(const ct_kv_paged_t *h) {
     int64_t best = -1;
-    const uint32_t P = h->cfg.page_tokens;
+    const uint32_t P = h->cfg.page_tokens, MP = h->cfg.max_pages_per_seq;
     for (uint32_t c = 0; c < h->cfg.n_seqs; c++) {
         if (h->lo[c] >= h->hi[c]) continue;
         if ((uint64_t)(h->lo[c] + 1) * P > h->len[c]) continue;      /* partial tail page */
+        if (h->refc[h->bt[(size_t)c * MP + h->lo[c]]] > 1) continue;   /* shared prefix page */
         if (best < 0 || h->last_access[c] < h->last_access[best]) best = c;
     }
     return best;
@@ -179,7 +185,7 @@ void ct_kv_paged_destroy(ct_kv_paged_t *h) {
         cudaFree(h->pool); cudaFree(h->scales); cudaFree(h->bt_dev); cudaFree(h->len_dev); cudaFree(h->stage_dev);
         if (h->stage_host) cudaFreeHost(h->stage_host);
     }
-    free(h->bt); free(h->len); free(h->lo); free(h->hi); free(h->last_access); free(h->rank);
+    free(h->bt); free(h->len); free(h->lo); free(h->hi); free(h->last_access); free(h->rank); free(h->refc);
     free(h->heap); free(h->log); free(h->claimed); free(h->pairs);
     free(h);
 }
@@ -207,9 +213,10 @@ ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg) {
     h->hi = (uint32_t *)calloc(S, sizeof(uint32_t));
     h->last_access = (uint64_t *)calloc(S, sizeof(uint64_t));
     h->rank = (uint32_t *)malloc((size_t)NP * sizeof(uint32_t));
+    h->refc = (uint32_t *)calloc(NP, sizeof(uint32_t));
     h->heap = (int32_t *)malloc((size_t)NP * sizeof(int32_t));
     h->claimed = (uint8_t *)calloc(((size_t)NP * P + 7) / 8, 1);
-    if (!h->bt || !h->len || !h->lo || !h->hi || !h->last_access || !h->rank || !h->heap || !h->claimed) {
+    if (!h->bt || !h->len || !h->lo || !h->hi || !h->last_access || !h->rank || !h->refc || !h->heap || !h->claimed) {
         ct_kv_paged_destroy(h);
         return NULL;
     }
@@ -362,6 +369,7 @@ int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t
                     if ((rc = free_low_page(h, (uint32_t)c, 2))) break;
                 }
                 int32_t ph = heap_pop(h);
+                h->refc[ph] = 1;
                 if ((rc = set_bt(h, s, lp, ph))) break;
                 if (h->lo[s] == h->hi[s]) h->lo[s] = lp;
                 h->hi[s] = lp + 1;
@@ -444,6 +452,72 @@ int ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n) {
     return rc ? rc : (int)done;
 }
 
+/* ---- prefix sharing ------------------------------------------------------ */
+
+int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_tokens) {
+    if (!h || src >= h->cfg.n_seqs || dst >= h->cfg.n_seqs || src == dst) return CT_ERR_ARG;
+    if (h->len[dst] != 0 || h->lo[dst] != h->hi[dst] || n_tokens > h->len[src]) return CT_ERR_ARG;
+    const uint32_t P = h->cfg.page_tokens, MP = h->cfg.max_pages_per_seq;
+    const uint32_t full = n_tokens / P, rem = n_tokens % P;
+    if (n_tokens && h->lo[src] != 0) {                /* the window already dropped part of the prefix */
+        ct__set_error("ct_kv_paged_fork: the prefix is no longer mapped");
+        return CT_ERR_UNMAPPED;
+    }
+    h->n_bt_pairs = h->n_len_pairs = 0;
+    int rc = CT_OK;
+    for (uint32_t lp = 0; lp < full && !rc; lp++) {   /* full pages: shared, never written again */
+        const int32_t ph = h->bt[(size_t)src * MP + lp];
+        h->refc[ph]++;
+        rc = set_bt(h, dst, lp, ph);
+    }
+    int32_t copy_from = -1, copy_to = -1;
+    if (!rc && rem) {                                 /* the partial page: dst's own copy */
+        if (h->heap_n == 0) {
+            int64_t c = lru_victim(h);
+            if (c < 0) { ct__set_error("fork: no evictable page"); rc = CT_ERR_FULL; }
+            else rc = free_low_page(h, (uint32_t)c, 2);
+        }
+        if (!rc) {
+            copy_from = h->bt[(size_t)src * MP + full];
+            copy_to = heap_pop(h);
+            h->refc[copy_to] = 1;
+            h->st.n_pages_live++;
+            rc = set_bt(h, dst, full, copy_to);
+        }
+    }
+    if (rc) {                                         /* undo the shared references, publish any eviction */
+        for (uint32_t lp = 0; lp < full; lp++) {
+            const int32_t ph = h->bt[(size_t)dst * MP + lp];
+            if (ph >= 0) { h->refc[ph]--; set_bt(h, dst, lp, -1); }
+        }
+        h->st.n_pages_free = h->heap_n;
+        flush(h, NULL, 0, NULL, 0);
+        return rc;
+    }
+    h->lo[dst] = 0;
+    h->hi[dst] = full + (rem ? 1 : 0);
+    h->len[dst] = n_tokens;
+    h->last_access[dst] = h->st.clock++;
+    if ((rc = push_len(h, dst))) return rc;
+    h->st.n_pages_free = h->heap_n;
+    if (!h->host_only && copy_to >= 0) {             /* first rem slots of the page, and their scales */
+        const size_t tok_bytes = h->page_bytes / P;
+        rc = ct__cuda_status(cudaMemcpyAsync((uint8_t *)h->pool + (size_t)copy_to * h->page_bytes,
+                                             (const uint8_t *)h->pool + (size_t)copy_from * h->page_bytes,
+                                             rem * tok_bytes, cudaMemcpyDeviceToDevice, h->stream), "fork copy");
+        if (!rc && h->scales)
+            rc = ct__cuda_status(cudaMemcpyAsync(h->scales + (size_t)copy_to * P, h->scales + (size_t)copy_from * P,
+                                                 rem * sizeof(float), cudaMemcpyDeviceToDevice, h->stream), "fork copy");
+        if (rc) return rc;
+    }
+    return flush(h, NULL, 0, NULL, 0);
+}
+
+uint32_t ct_kv_paged_page_refs(const ct_kv_paged_t *h, int32_t page) {
+    if (!h || page < 0 || (uint32_t)page >= h->cfg.n_pages) return 0;
+    return h->refc[page];
+}
+
 /* ---- compaction ----------------------------------------------------------- */
 
 int ct_kv_paged_compact(ct_kv_paged_t *h) {
@@ -458,13 +532,25 @@ int ct_kv_paged_compact(ct_kv_paged_t *h) {
         if (rc) return rc;
         map = h->stage_host;                      /* [n_live] new -> old, then the bt image */
     }
+    /* a page shared by several sequences gets one new id, at its first use */
+    int32_t *new_id = (int32_t *)malloc((size_t)NP * sizeof(int32_t));
+    uint32_t *refc2 = (uint32_t *)calloc(NP, sizeof(uint32_t));
+    if (!new_id || !refc2) { free(new_id); free(refc2); return CT_ERR_NOMEM; }
+    for (uint32_t p = 0; p < NP; p++) new_id[p] = -1;
     uint32_t n_live = 0;
     for (uint32_t s = 0; s < S; s++)
         for (uint32_t lp = h->lo[s]; lp < h->hi[s]; lp++) {
             int32_t *e = h->bt + (size_t)s * MP + lp;
-            map[n_live] = *e;
-            *e = (int32_t)n_live++;
+            if (new_id[*e] < 0) {
+                new_id[*e] = (int32_t)n_live;
+                refc2[n_live] = h->refc[*e];
+                map[n_live++] = *e;
+            }
+            *e = new_id[*e];
         }
+    memcpy(h->refc, refc2, (size_t)NP * sizeof(uint32_t));
+    free(new_id);
+    free(refc2);
     if (h->host_only) goto renumbered;
     void *new_pool = NULL;
     float *new_scales = NULL;
@@ -683,17 +769,22 @@ int ct_kv_paged_save(ct_kv_paged_t *h, const char *path) {
                                h->log[i].reason};
         ck_write(&io, e, sizeof e);
     }
-    uint32_t n_live = 0;
-    for (size_t i = 0; i < (size_t)S * MP; i++) n_live += h->bt[i] >= 0;
+    uint32_t n_live = 0;                              /* distinct mapped pages (shared ones once) */
+    uint8_t *seen = (uint8_t *)calloc(NP, 1);
+    if (!seen) { fclose(f); return CT_ERR_NOMEM; }
+    for (size_t i = 0; i < (size_t)S * MP; i++)
+        if (h->bt[i] >= 0 && !seen[h->bt[i]]) { seen[h->bt[i]] = 1; n_live++; }
+    memset(seen, 0, NP);
     ck_write(&io, &n_live, 4);
     int rc = CT_OK;
     if (!h->host_only && n_live) {
         const size_t sc_bytes = h->scales ? (size_t)P * sizeof(float) : 0;
         uint8_t *buf = (uint8_t *)malloc(h->page_bytes + sc_bytes);
-        if (!buf) { fclose(f); return CT_ERR_NOMEM; }
+        if (!buf) { free(seen); fclose(f); return CT_ERR_NOMEM; }
         for (size_t i = 0; i < (size_t)S * MP && !rc && !io.err; i++) {
             const int32_t pg = h->bt[i];
-            if (pg < 0) continue;
+            if (pg < 0 || seen[pg]) continue;
+            seen[pg] = 1;
             rc = ct__cuda_status(cudaMemcpy(buf, (const uint8_t *)h->pool + (size_t)pg * h->page_bytes,
                                             h->page_bytes, cudaMemcpyDeviceToHost), "ct_kv_paged_save page");
             if (!rc && sc_bytes)
@@ -704,6 +795,7 @@ int ct_kv_paged_save(ct_kv_paged_t *h, const char *path) {
         }
         free(buf);
     }
+    free(seen);
     const uint64_t sum = io.fnv;
     if (!io.err && fwrite(&sum, 8, 1, f) != 1) io.err = 1;
     if (fclose(f) != 0) io.err = 1;
@@ -757,7 +849,9 @@ ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
     for (uint32_t i = 0; i < S && !bad; i++) bad = h->len[i] > MP * P || h->lo[i] > h->hi[i] || h->hi[i] > MP;
     for (uint32_t p = 0; p < NP && !bad; p++) bad = h->rank[p] >= NP;
     for (size_t i = 0; i < (size_t)S * MP && !bad; i++) bad = h->bt[i] < -1 || h->bt[i] >= (int32_t)NP;
-    if (!bad) {
+    if (!bad) {                                        /* reference counts follow from the table */
+        memset(h->refc, 0, (size_t)NP * sizeof(uint32_t));
+        for (size_t i = 0; i < (size_t)S * MP; i++) if (h->bt[i] >= 0) h->refc[h->bt[i]]++;
         ck_read(&io, h->heap, (size_t)free_n * 4);
         for (uint32_t i = 0; i < free_n && !bad; i++) bad = h->heap[i] < 0 || h->heap[i] >= (int32_t)NP;
     }

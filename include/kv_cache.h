@@ -170,6 +170,18 @@ int  ct_kv_paged_compact(ct_kv_paged_t *h);
 int  ct_kv_paged_gather(ct_kv_paged_t *h, uint32_t seq, uint32_t start, uint32_t n,
                         void *out, uint32_t out_dtype);
 
+/* Prefix sharing (new; the reference's ct_engine_kv_reuse is a no-op,
+ * engine.c:653-657): sequence dst (empty) takes the first n_tokens of src.
+ * Full pages are shared -- both block tables map them and a page returns to
+ * the free set only when no sequence maps it -- and a partial last page is
+ * copied into a page of dst's own, so appends never write a shared page.
+ * Shared pages are not LRU victims; a sequence's window releases its
+ * references; compaction keeps them shared.  CT_ERR_UNMAPPED if the window
+ * already dropped part of src's prefix. */
+int      ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_tokens);
+/* Number of sequences mapping a physical page (0 = free). */
+uint32_t ct_kv_paged_page_refs(const ct_kv_paged_t *h, int32_t page);
+
 /* Checkpoint of a paged cache (new; no reference counterpart -- it extends
  * the raw format of kv_cache.c:82-111, which ct_kv_save / ct_kv_load keep
  * unchanged): a versioned header ("CTKVPAGE", version 1), the configuration,

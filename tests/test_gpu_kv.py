@@ -12,6 +12,7 @@ import torch
 import cautreo_b200 as ct
 import oracle
 from gpu_util import dev, empty, host, stream
+from helpers import MLA_H
 
 pytestmark = pytest.mark.gpu
 GOLD = Path(__file__).resolve().parent / "golden"
@@ -351,3 +352,44 @@ def test_paged_checkpoint_restores_pages(pool_dtype, tmp_path):
         assert np.array_equal(a, b)
     h.close()
     g.close()
+
+
+@pytest.mark.parametrize("pool_dtype", [ct.CT_KV_BF16, ct.CT_KV_INT8])
+def test_fork_shares_pages_on_device(pool_dtype):
+    """A forked sequence reads the same prefix (shared full pages, a copied
+    partial page), appends stay private to each sequence, and MLA decode over
+    the fork equals decode over the original."""
+    S, P, E, NP = 3, 64, 576, 16
+    h = ct.PagedKV(S, 6, NP, P, E, 0, pool_dtype, 0, stream())
+    h.set_free_order(oracle.permutation(oracle.key(31, 1), NP))
+    ent, _, sdt = entries_for(150, E, 31, "bf16")
+    h.append([0], [150], ent.data_ptr(), sdt)
+    h.fork(0, 1, 150)
+    bt = h.block_table()
+    assert bt[0, 0] == bt[1, 0] and bt[0, 1] == bt[1, 1] and bt[0, 2] != bt[1, 2]
+    L = ct.lib()
+
+    def gather(s, lo, n):
+        o = empty((n, E), np.uint16)
+        ct.check(L.ct_kv_paged_gather(h.h, s, lo, n, o.data_ptr(), ct.CT_KV_BF16))
+        return host(o, np.uint16)
+
+    assert np.array_equal(gather(0, 0, 150), gather(1, 0, 150))
+    # identical queries: identical outputs
+    q = oracle.normal_bf16(oracle.key(31, 2), 0, 2 * MLA_H * E).reshape(2, MLA_H, E)
+    q[1] = q[0]
+    qd, out = dev(q), empty((2, MLA_H, 512), np.uint16)
+    plan = ct.MlaPlan(np.array([150, 150], np.int32), NP, max_pages_per_seq=6, kv_dtype=pool_dtype,
+                      seq_rows=np.array([0, 1], np.uint32))
+    plan.decode(qd.data_ptr(), h.pool, h.scales, h.block_table_dev, h.seq_lens_dev, out.data_ptr(), None, stream())
+    o = host(out, np.uint16)
+    assert np.array_equal(o[0], o[1])
+    # private appends: each sequence's new tokens land in its own pages
+    a, _, _ = entries_for(5, E, 32, "bf16")
+    b, _, _ = entries_for(5, E, 33, "bf16")
+    prefix0 = gather(0, 0, 150)
+    h.append([0], [5], a.data_ptr(), ct.CT_KV_BF16)
+    h.append([1], [5], b.data_ptr(), ct.CT_KV_BF16)
+    assert np.array_equal(gather(0, 0, 150), prefix0) and np.array_equal(gather(1, 0, 150), prefix0)
+    assert not np.array_equal(gather(0, 150, 5), gather(1, 150, 5))
+    h.close()

@@ -263,3 +263,89 @@ def test_paged_checkpoint_rejects_damage(tmp_path):
     assert not L.ct_kv_paged_load(str(tmp_path / "missing.ckpt").encode(), -1)
     assert L.ct_kv_paged_save(h.h, str(tmp_path / "no_such_dir" / "x").encode()) == ct.CT_ERR_IO
     h.close()
+
+
+# ---- prefix sharing (tables only) ---------------------------------------------
+
+def test_fork_shares_full_pages_copies_the_partial_one():
+    h = host_paged(4, 8, 20, 4, 0)
+    h.append([0], [10])                                   # pages 0, 1 full, page 2 holds 2 tokens
+    bt = h.block_table()
+    p0, p1, p2 = bt[0, :3]
+    h.fork(0, 1, 10)
+    bt = h.block_table()
+    assert bt[1, 0] == p0 and bt[1, 1] == p1 and bt[1, 2] not in (p0, p1, p2)
+    assert [h.page_refs(p) for p in (p0, p1, p2, bt[1, 2])] == [2, 2, 1, 1]
+    h.fork(0, 2, 8)                                       # page-aligned prefix: nothing copied
+    bt = h.block_table()
+    assert bt[2, :3].tolist() == [p0, p1, -1] and h.page_refs(p0) == 3
+    assert h.seq_lens()[:3].tolist() == [10, 10, 8]
+    live = h.stats().n_pages_live
+    h.append([2], [1])                                    # opens its own page 2
+    assert h.block_table()[2, 2] not in (p0, p1, p2) and h.stats().n_pages_live == live + 1
+    ct.check(ct.lib().ct_kv_paged_free_seq(h.h, 0))
+    assert h.page_refs(p0) == 2 and h.page_refs(p2) == 0  # shared pages stay; seq 0's own page is free
+    ct.check(ct.lib().ct_kv_paged_free_seq(h.h, 1))
+    ct.check(ct.lib().ct_kv_paged_free_seq(h.h, 2))
+    assert h.stats().n_pages_live == 0 and h.stats().n_pages_free == 20
+    h.close()
+
+
+def test_fork_errors():
+    h = host_paged(4, 8, 20, 4, 8)                        # window 8
+    h.append([0, 1], [6, 30])
+    L = ct.lib()
+    assert L.ct_kv_paged_fork(h.h, 0, 0, 2) == ct.CT_ERR_ARG         # src == dst
+    assert L.ct_kv_paged_fork(h.h, 0, 1, 2) == ct.CT_ERR_ARG         # dst not empty
+    assert L.ct_kv_paged_fork(h.h, 0, 2, 7) == ct.CT_ERR_ARG         # longer than src
+    assert L.ct_kv_paged_fork(h.h, 1, 2, 30) == ct.CT_ERR_UNMAPPED   # window dropped src's prefix
+    h.close()
+
+
+def test_fork_pages_are_not_lru_victims():
+    """Under pool pressure LRU takes only pages one sequence maps."""
+    h = host_paged(3, 8, 6, 4, 0)
+    h.append([0], [12])                                   # 3 full pages, oldest access
+    h.fork(0, 1, 8)                                       # shares pages 0 and 1 of seq 0
+    h.append([2], [12])                                   # 3 more pages: the pool is full
+    bt0 = h.block_table()[0].copy()
+    h.append([2], [1])                                    # needs a page: seq 0's lowest is shared...
+    ev = h.evict_log()
+    assert len(ev) == 1 and ev[0][1] == 2 and ev[0][4] == 2   # ...so seq 2's own oldest page goes
+    assert np.array_equal(h.block_table()[0], bt0)
+    h.close()
+
+
+def test_fork_window_releases_references():
+    h = host_paged(2, 16, 30, 4, 8)                       # window 8
+    h.append([0], [8])
+    h.fork(0, 1, 8)
+    p0, p1 = h.block_table()[0, :2]
+    h.append([1], [8])                                    # seq 1's window moves past the shared pages
+    assert h.block_table()[1, :2].tolist() == [-1, -1]
+    assert h.page_refs(p0) == 1 and h.page_refs(p1) == 1  # still seq 0's
+    h.close()
+
+
+def test_fork_survives_compaction_and_checkpoint(tmp_path):
+    h = host_paged(3, 8, 24, 4, 0)
+    h.set_free_order(oracle.permutation(oracle.key(5, 1), 24))
+    h.append([0, 2], [9, 5])
+    h.fork(0, 1, 9)
+    h.append([1], [3])
+    assert ct.lib().ct_kv_paged_compact(h.h) == 0
+    bt = h.block_table()
+    assert bt[0, 0] == bt[1, 0] and bt[0, 1] == bt[1, 1] and bt[0, 2] != bt[1, 2]
+    refs = [h.page_refs(p) for p in range(24)]
+    assert sorted(set(bt[bt >= 0].tolist())) == list(range(sum(r > 0 for r in refs)))   # dense after compaction
+    path = tmp_path / "kv.ckpt"
+    h.save(path)
+    g = ct.PagedKV.load(path, device=-1)
+    assert [g.page_refs(p) for p in range(24)] == refs
+    assert np.array_equal(g.block_table(), bt)
+    for handle in (h, g):
+        ct.check(ct.lib().ct_kv_paged_free_seq(handle.h, 0))
+        handle.append([2], [6])
+    assert np.array_equal(g.block_table(), h.block_table())
+    h.close()
+    g.close()
