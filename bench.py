@@ -116,14 +116,38 @@ def committed_traffic(workload_name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of one GPU, read through
+    NVML every 5 ms by a thread that runs across the timed region (reads
+    only; no setting is changed).  Falls back to `nvidia-smi -lms` when NVML
+    cannot be loaded."""
+
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []          # (sm MHz, reason bits)
+        self.smax = None
+        self.stop_flag = threading.Event()
+        self.t = None
 
     def start(self):
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            self.nvml = N
+            self.handle = N.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.smax = float(N.nvmlDeviceGetMaxClockInfo(self.handle, N.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 2.0:      # live before the timed region starts
+                time.sleep(0.001)
+            return
+        except Exception:
+            self.nvml = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -136,20 +160,46 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def _poll(self):
+        N = self.nvml
+        get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((float(N.nvmlDeviceGetClockInfo(self.handle, N.NVML_CLOCK_SM)),
+                                     int(get_reasons(self.handle))))
+            except Exception:
+                return
+            time.sleep(0.005)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            n0 = len(self.samples)
+            t0 = time.time()
+            while len(self.samples) == n0 and time.time() - t0 < 1.0:  # one sample after the region
+                time.sleep(0.001)
+            self.stop_flag.set()
+            self.t.join(timeout=2)
+            sm = [c for c, _ in self.samples]
+            bits = 0
+            for _, b in self.samples:
+                bits |= b
+            reasons = sorted(n for n, m in self.NAMES.items() if bits & m)
+            return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.smax, "reasons": reasons,
+                    "samples": len(sm), "source": "nvml, 5 ms"}
         if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = list(self.NAMES)
         for line in self.lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
@@ -163,7 +213,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 100 ms"}
 
 
 # ---------------------------------------------------------------------------

@@ -424,6 +424,15 @@ class MlaPlan:
                                             ptr(seq_lens), ptr(out), ptr(lse), stream)
         check(rc, "ct_attn_mla_decode_paged")
 
+    def step_host(self, q_host, entries_host, dest_slot, pool, scales, block_table, seq_lens, out_host,
+                  stream=None):
+        """One step with host buffers (ct_attn_mla_decode_step_host): append
+        entries_host at dest_slot (device; None skips), decode, fill out_host."""
+        rc = lib().ct_attn_mla_decode_step_host(self.h, ptr(q_host), ptr(entries_host), ptr(dest_slot), ptr(pool),
+                                                ptr(scales), ptr(block_table), ptr(seq_lens), ptr(out_host),
+                                                stream)
+        check(rc, "ct_attn_mla_decode_step_host")
+
 
 def lpt_shard(lengths, n_ranks):
     lengths = np.ascontiguousarray(lengths, np.uint32)

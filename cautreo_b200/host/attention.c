@@ -68,6 +68,12 @@ void ct_attn_softmax(float *x, uint32_t n) {
 
 /* ---- Part 2: MLA plans ---------------------------------------------------- */
 
+/* ct_attn_mla_decode_step_host splits a step into up to this many sequence
+ * groups, so that the copies of one group overlap the decode of another;
+ * steps that move less than CT_STEP_PIPELINE_MIN_BYTES stay one group. */
+#define CT_STEP_GROUPS 8
+#define CT_STEP_PIPELINE_MIN_BYTES (16u << 20)
+
 struct ct_mla_plan {
     ct_mla_dims_t dims;
     uint32_t n_seq, n_workers, n_chunks, n_combines, n_parts;
@@ -80,6 +86,19 @@ struct ct_mla_plan {
     size_t scratch_bytes;
     void *stage_q, *stage_e, *stage_o;   /* device staging of ct_attn_mla_decode_step_host */
     uint32_t last_launches;
+    /* Host copies of the inputs the plan was made from, so that
+     * ct_attn_mla_decode_step_host can re-plan sequence groups. */
+    ct_mla_shape_t shape;
+    uint32_t *rows_h;
+    int32_t *lens_h;
+    /* ct_attn_mla_decode_step_host's pipeline: sequence groups
+     * [group_begin[g], group_begin[g + 1]) with one sub-plan each, a copy-in
+     * and a copy-out stream, and the events that order them. */
+    uint32_t n_groups;
+    uint32_t group_begin[CT_STEP_GROUPS + 1];
+    ct_mla_plan_t *group_plan[CT_STEP_GROUPS];
+    cudaStream_t copy_in, copy_out;
+    cudaEvent_t ev_in[CT_STEP_GROUPS], ev_dec[CT_STEP_GROUPS];
 };
 
 /* Declared in mla_tc.cu: whether the tensor-core kernel takes these dims on
@@ -91,6 +110,14 @@ void ct_mla_plan_destroy(ct_mla_plan_t *p) {
     cudaFree(p->chunks); cudaFree(p->worker_begin); cudaFree(p->combines);
     cudaFree(p->part_o); cudaFree(p->part_ml);
     cudaFree(p->stage_q); cudaFree(p->stage_e); cudaFree(p->stage_o);
+    for (uint32_t g = 0; g < CT_STEP_GROUPS; g++) {
+        ct_mla_plan_destroy(p->group_plan[g]);
+        if (p->ev_in[g]) cudaEventDestroy(p->ev_in[g]);
+        if (p->ev_dec[g]) cudaEventDestroy(p->ev_dec[g]);
+    }
+    if (p->copy_in) cudaStreamDestroy(p->copy_in);
+    if (p->copy_out) cudaStreamDestroy(p->copy_out);
+    free(p->rows_h); free(p->lens_h);
     free(p);
 }
 
@@ -114,6 +141,7 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
     p->dims.n_seq = n_seq;
     p->n_seq = n_seq;
     p->device = device;
+    p->shape = *shape;
     const uint32_t P = shape->page_tokens;
 
     int n_sms = 148;
@@ -134,6 +162,17 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
             return NULL;
         }
         total += (uint64_t)seq_lens[s];
+    }
+    p->rows_h = (uint32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(uint32_t));
+    p->lens_h = (int32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(int32_t));
+    if (!p->rows_h || !p->lens_h) {
+        ct__set_error("ct_mla_plan_create: out of memory");
+        free(p->rows_h); free(p->lens_h); free(p);
+        return NULL;
+    }
+    for (uint32_t s = 0; s < n_seq; s++) {
+        p->rows_h[s] = seq_rows ? seq_rows[s] : s;
+        p->lens_h[s] = seq_lens[s];
     }
     const uint32_t W = p->n_workers;
     const uint64_t quota = total / W + 1;
@@ -206,6 +245,7 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
 fail:
     ct__set_error("ct_mla_plan_create: out of memory");
     free(ch); free(wb); free(first_chunk); free(n_of);
+    free(p->rows_h); free(p->lens_h);
     free(p);
     return NULL;
 }
@@ -230,6 +270,41 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
     return rc;
 }
 
+/* Split p's sequences into contiguous groups and give each its own plan,
+ * copy streams and events.  Called once per plan.  The copy-in of the first
+ * group and the copy-out of the last overlap no decode, so those two groups
+ * get half the KV tokens of the others: with G groups the cuts fall at
+ * (g + 1/2) / (G - 1) of the step's tokens. */
+static int step_host_pipeline(ct_mla_plan_t *p, size_t step_bytes) {
+    uint32_t G = CT_STEP_GROUPS;
+    if (step_bytes < CT_STEP_PIPELINE_MIN_BYTES || p->n_seq < 2 * G) G = 1;
+    uint64_t total = 0;
+    for (uint32_t s = 0; s < p->n_seq; s++) total += (uint64_t)p->lens_h[s];
+    p->group_begin[0] = 0;
+    uint32_t g = 0;
+    uint64_t acc = 0;
+    for (uint32_t s = 0; s < p->n_seq && g + 1 < G; s++) {
+        acc += (uint64_t)p->lens_h[s];
+        if (acc * 2 * (G - 1) >= total * (2 * g + 1)) p->group_begin[++g] = s + 1;
+    }
+    while (g < G) p->group_begin[++g] = p->n_seq;
+    p->n_groups = G;
+    if (G == 1) return CT_OK;
+    int rc = ct__cuda_status(cudaStreamCreateWithFlags(&p->copy_in, cudaStreamNonBlocking), "step_host streams");
+    if (!rc) rc = ct__cuda_status(cudaStreamCreateWithFlags(&p->copy_out, cudaStreamNonBlocking), "step_host streams");
+    for (g = 0; g < G && !rc; g++) {
+        const uint32_t a = p->group_begin[g], b = p->group_begin[g + 1];
+        rc = ct__cuda_status(cudaEventCreateWithFlags(&p->ev_in[g], cudaEventDisableTiming), "step_host events");
+        if (!rc) rc = ct__cuda_status(cudaEventCreateWithFlags(&p->ev_dec[g], cudaEventDisableTiming), "step_host events");
+        if (!rc && b > a) {
+            p->group_plan[g] = ct_mla_plan_create(&p->shape, p->rows_h + a, p->lens_h + a, b - a, p->device);
+            if (!p->group_plan[g]) rc = CT_ERR_CUDA;
+        }
+    }
+    if (rc) p->n_groups = 0;             /* the next call retries */
+    return rc;
+}
+
 int ct_attn_mla_decode_step_host(ct_mla_plan_t *p, const void *q_host, const void *entries_host,
                                  const int32_t *dest_slot, void *pool, float *scales,
                                  const int32_t *block_table, const int32_t *seq_lens, void *out_host,
@@ -238,22 +313,74 @@ int ct_attn_mla_decode_step_host(ct_mla_plan_t *p, const void *q_host, const voi
     if (dest_slot && !entries_host) return CT_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t n = p->n_seq, H = p->dims.n_heads, E = p->dims.entry_dim, Dv = p->dims.v_dim;
-    const size_t qb = n * H * E * 2, eb = n * E * 2, ob = n * H * Dv * 2;
+    const size_t qr = H * E * 2, er = E * 2, orow = H * Dv * 2;   /* bytes per sequence */
     int rc = CT_OK;
     if (!p->stage_q) {
-        rc = ct__cuda_status(cudaMalloc(&p->stage_q, qb ? qb : 16), "step_host staging");
-        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_e, eb ? eb : 16), "step_host staging");
-        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_o, ob ? ob : 16), "step_host staging");
+        rc = ct__cuda_status(cudaMalloc(&p->stage_q, n ? n * qr : 16), "step_host staging");
+        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_e, n ? n * er : 16), "step_host staging");
+        if (!rc) rc = ct__cuda_status(cudaMalloc(&p->stage_o, n ? n * orow : 16), "step_host staging");
         if (rc) return rc;
     }
-    rc = ct__cuda_status(cudaMemcpyAsync(p->stage_q, q_host, qb, cudaMemcpyHostToDevice, st), "step_host q");
+    if (p->n_groups == 0 && (rc = step_host_pipeline(p, n * (qr + er + orow)))) return rc;
+
+    if (p->n_groups == 1) {              /* one group: everything in order on the caller's stream */
+        rc = ct__cuda_status(cudaMemcpyAsync(p->stage_q, q_host, n * qr, cudaMemcpyHostToDevice, st), "step_host q");
+        if (!rc && dest_slot) {
+            rc = ct__cuda_status(cudaMemcpyAsync(p->stage_e, entries_host, n * er, cudaMemcpyHostToDevice, st),
+                                 "step_host e");
+            if (!rc) rc = ct_kv_paged_write_slots(pool, scales, p->dims.kv_dtype, p->stage_e, CT_KV_BF16, dest_slot,
+                                                  (uint32_t)n, (uint32_t)E, stream);
+        }
+        if (!rc) rc = ct_attn_mla_decode_paged(p, p->stage_q, pool, scales, block_table, seq_lens, p->stage_o, NULL,
+                                               stream);
+        if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(out_host, p->stage_o, n * orow, cudaMemcpyDeviceToHost, st),
+                                      "step_host out");
+        if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(st), "step_host sync");
+        return rc;
+    }
+
+    /* Groups: the copy-in of group g+1 runs during the decode of group g, and
+     * the copy-out of group g during the decode of group g+1.  All new tokens
+     * (n_seq x entry_dim bf16, small) are copied and appended before the
+     * first decode, as in the one-group order. */
+    uint32_t launches = 0;
+    char *oh = (char *)out_host, *sq = (char *)p->stage_q, *so = (char *)p->stage_o;
+    const char *qh = (const char *)q_host;
+    /* The copies start after the work already queued on the caller's stream. */
+    rc = ct__cuda_status(cudaEventRecord(p->ev_dec[0], st), "step_host");
+    if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(p->copy_in, p->ev_dec[0], 0), "step_host");
     if (!rc && dest_slot) {
-        rc = ct__cuda_status(cudaMemcpyAsync(p->stage_e, entries_host, eb, cudaMemcpyHostToDevice, st), "step_host e");
+        rc = ct__cuda_status(cudaMemcpyAsync(p->stage_e, entries_host, n * er, cudaMemcpyHostToDevice, p->copy_in),
+                             "step_host e");
+        if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_in[0], p->copy_in), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(st, p->ev_in[0], 0), "step_host");
         if (!rc) rc = ct_kv_paged_write_slots(pool, scales, p->dims.kv_dtype, p->stage_e, CT_KV_BF16, dest_slot,
                                               (uint32_t)n, (uint32_t)E, stream);
     }
-    if (!rc) rc = ct_attn_mla_decode_paged(p, p->stage_q, pool, scales, block_table, seq_lens, p->stage_o, NULL, stream);
-    if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(out_host, p->stage_o, ob, cudaMemcpyDeviceToHost, st), "step_host out");
-    if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(st), "step_host sync");
+    uint32_t g = 0;
+    for (; g < p->n_groups && !rc; g++) {
+        const size_t a = p->group_begin[g], m = p->group_begin[g + 1] - a;
+        if (m == 0) continue;
+        rc = ct__cuda_status(cudaMemcpyAsync(sq + a * qr, qh + a * qr, m * qr, cudaMemcpyHostToDevice, p->copy_in),
+                             "step_host q");
+        if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_in[g], p->copy_in), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(st, p->ev_in[g], 0), "step_host");
+        if (!rc) {
+            rc = ct_attn_mla_decode_paged(p->group_plan[g], sq + a * qr, pool, scales, block_table, seq_lens,
+                                          so + a * orow, NULL, stream);
+            launches += p->group_plan[g]->last_launches;
+        }
+        if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_dec[g], st), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(p->copy_out, p->ev_dec[g], 0), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(oh + a * orow, so + a * orow, m * orow, cudaMemcpyDeviceToHost,
+                                                      p->copy_out), "step_host out");
+    }
+    p->last_launches = launches;
+    /* On an error part of the work may be queued: wait for all of it, so no
+     * copy is still reading or writing the caller's buffers on return. */
+    int rs = ct__cuda_status(cudaStreamSynchronize(p->copy_in), "step_host sync");
+    int rt = ct__cuda_status(cudaStreamSynchronize(st), "step_host sync");
+    int ro = ct__cuda_status(cudaStreamSynchronize(p->copy_out), "step_host sync");
+    if (!rc) rc = rs ? rs : rt ? rt : ro;
     return rc;
 }

@@ -247,3 +247,46 @@ def test_mla_through_paged_handle():
     ok, mx, rel = close(got, want)
     assert ok, (mx, rel)
     h.close()
+
+
+def _pinned(a):
+    t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16).copy())
+    return t.pin_memory()
+
+
+@pytest.mark.parametrize("n_seq", [4, 96])
+def test_mla_step_host(n_seq):
+    """ct_attn_mla_decode_step_host: append each sequence's new token from
+    host memory, decode, copy the outputs to host memory.  96 sequences move
+    about 27 MB per step, enough for the copies of one sequence group to run
+    during the decode of another; 4 sequences run in one group."""
+    k = oracle.key(21, n_seq)
+    lens = oracle.lengths_loguniform(k, n_seq, 64, 3000).astype(np.int32)
+    lens_after = lens + 1
+    pool, bt, q = mla_case(lens_after, seed=21)
+    slots = np.array([bt[s, n // PAGE] * PAGE + n % PAGE for s, n in enumerate(lens)], np.int32)
+    new = np.stack([pool[sl // PAGE, sl % PAGE] for sl in slots])
+    before = pool.copy()
+    for sl in slots:
+        before[sl // PAGE, sl % PAGE] = 0x7FC0          # NaN until the step writes the token
+    plan = ct.MlaPlan(lens_after, pool.shape[0], max_pages_per_seq=bt.shape[1], scale=MLA_SCALE)
+    pd, btd, ld, sd = dev(before), dev(bt), dev(lens_after), dev(slots)
+    qh, eh = _pinned(q), _pinned(new)
+    oh = torch.empty((n_seq, MLA_H, MLA_DV), dtype=torch.int16).pin_memory()
+    plan.step_host(qh, eh, sd, pd, None, btd, ld, oh, stream())
+    assert np.array_equal(host(pd, np.uint16), pool)              # every new token landed bit-exactly
+    got = oracle.bf16_to_f32(oh.numpy().view(np.uint16)).reshape(n_seq, MLA_H, MLA_DV)
+    # the same decode on the device path
+    ref_dev, _ = run_decode(pool, bt, lens_after, q)
+    ok, mx, rel = close(got, ref_dev)
+    assert ok, (mx, rel)
+    sub = sorted(set(np.argsort(lens)[[0, n_seq // 2, n_seq - 1]].tolist()))
+    want = oracle.mla_decode_paged(pool, bt[sub], lens_after[sub], q[sub], MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got[sub], want)
+    assert ok, (mx, rel)
+    if n_seq == 4:                                               # one group: the plan's own chunks
+        assert np.array_equal(got, ref_dev)
+    # a second call on the same plan, without appends, repeats the outputs
+    oh2 = torch.empty_like(oh).pin_memory()
+    plan.step_host(qh, None, None, pd, None, btd, ld, oh2, stream())
+    assert torch.equal(oh, oh2)
