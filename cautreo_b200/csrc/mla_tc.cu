@@ -18,15 +18,17 @@
  *          CTAs, so both run the identical softmax on identical scores;
  *   softmax in the log2 domain with a lazily updated row maximum (O is
  *          rescaled only when a row's maximum grows by more than 2^8);
- *          P = bf16 probabilities, written over the tile's scores in TMEM;
+ *          P = bf16 probabilities, written into the shared-memory slot the
+ *          peer's partial scores arrived in;
  *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
- *          from TMEM, V read MN-major from the same shared-memory page tile.
+ *          from that slot, V read MN-major from the same page tile.
  * The softmax warps keep one tile in flight: they finish tile j-1 (once the
  * peer's half is in) and stage tile j for the peer in whichever order their
- * inputs arrive, and the MMA warp issues each GEMM as soon as its operands
- * are ready, GEMM1 one tile ahead of GEMM2.  The peer's partial scores land
- * in one of two receive slots, so the copy of tile j+1 does not wait for
- * tile j to be consumed.
+ * inputs arrive.  The scores in TMEM are free once staged, so the MMA warp
+ * issues GEMM1 up to two tiles ahead of GEMM2.  The peer's partial scores
+ * land in one of two receive slots; a slot is handed back to the peer by the
+ * commit of the GEMM2 that read P from it, which arrives on the peer's
+ * barrier directly.
  *
  * Roles per CTA (608 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
@@ -34,9 +36,9 @@
  * head row (TMEM lane), one per 16-token quarter of a tile.
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
- * 36 KB, an exchange out buffer and two in slots of 32 KB, a 6 KB
- * row-statistics buffer, barriers.  TMEM: S / P at columns 0 and 64, Q at
- * 128, O at 256..511.
+ * 36 KB, an exchange out buffer and two in slots of 32 KB (partial scores,
+ * then P), a 6 KB row-statistics buffer, barriers.  TMEM: S at columns 0 and
+ * 64, Q at 128, O at 256..511.
  *
  * Every wait is bounded (about two seconds of clock); on expiry the kernel
  * records an error word, drains its own TMA loads, copies and MMAs, frees
@@ -83,7 +85,7 @@ constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the ba
 static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
 static_assert(kOffKv % 1024 == 0 && kOffOut % 1024 == 0 && kOffIn % 1024 == 0, "swizzle atoms need 1 KB alignment");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns: fp32 scores, then bf16 P in the first 32 */
+constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns: fp32 scores */
 constexpr uint32_t kTmemQ = 128;    /* 128 columns, bf16 query latent dims of the half */
 constexpr uint32_t kTmemO = 256;    /* 256 columns, fp32 output accumulator */
 constexpr float kLog2e = 1.4426950408889634f;
@@ -96,7 +98,8 @@ enum : uint32_t {
     B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_P_FULL = 11,
     B_O_READY = 13, B_O_FINAL = 14, B_O_FREE = 15, B_SO_FULL = 16, B_SO_EMPTY = 17, B_X_FULL = 18 /* [slot] */,
     B_X_EMPTY = 20 /* [slot] */, B_DRAIN = 22, B_RED = 23 /* [parity][quad] */, B_RED_L = 31 /* [quad] */,
-    B_CONV_FULL = 35 /* [stage]: page converted to bf16 (quantised pools) */
+    B_CONV_FULL = 35 /* [stage]: page converted to bf16 (quantised pools) */,
+    B_S_EMPTY = 38 /* [score buffer]: the softmax warps have read the scores */
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -151,13 +154,6 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
-/* Arrive on the peer's barrier without release semantics: it only signals
- * that this thread's loads of the receive buffer have returned, which every
- * later instruction already depends on (a release at cluster scope costs about
- * a microsecond here). */
-__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t remote_bar) {
-    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -203,6 +199,12 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+/* Arrive on the barrier at the same offset in the CTAs of `mask` (here: the
+ * peer) once this thread's MMAs so far are complete. */
+__device__ __forceinline__ void mma_commit_to(uint32_t bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"(mask) : "memory");
+}
 
 /* 32 consecutive TMEM columns of this thread's lane <-> registers. */
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
@@ -238,11 +240,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
         : "r"(taddr));
     #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
-                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
     asm volatile(
@@ -448,11 +445,14 @@ __device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t s
         mma_ss(d, sdesc(q + k * 32, 1, 32, kSw64), sdesc(kv + 4 * 8192 + k * 32, 1, 32, kSw64), kIdescS, 1);
 }
 
-__device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t pbuf, bool first) {
-    const uint32_t v = c.s + kOffKv + st * kKvBytes;
+/* P of a tile sits in the receive slot its peer scores came in: rows of 8
+ * heads (8 x 128 B, SW128 K-major) every 2048 B, so that the rows a TMEM
+ * lane quadrant writes lie over partial scores that quadrant has read. */
+__device__ void issue_gemm2(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t slot, bool first) {
+    const uint32_t v = c.s + kOffKv + st * kKvBytes, pa = c.s + kOffIn + slot * kXBytes;
     #pragma unroll
     for (int k = 0; k < 4; k++)
-        mma_ts(tmem + kTmemO, tmem + kTmemS + pbuf * 64 + k * 8, sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
+        mma_ss(tmem + kTmemO, sdesc(pa + k * 32, 1, 2048 / 16, kSw128), sdesc(v + k * 2048, 512, 64, kSw128), kIdescO,
                (first && k == 0) ? 0u : 1u);
 }
 
@@ -472,10 +472,9 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
                  wait_bar(c, bar(c, B_QT_FULL), nchunk & 1, false, 3);
             tc_fence_after();
             /* Issue whichever GEMM is ready, GEMM2 first (it frees a page
-             * stage).  P of tile t sits in the score columns of tile t, so
-             * GEMM1 of tile t+2 (same columns) is issued after GEMM2 of tile
-             * t; tcgen05.mma instructions of one thread execute in issue
-             * order, so GEMM2 has read P before GEMM1 overwrites it. */
+             * stage and the peer's copy into a receive slot).  GEMM1 of tile
+             * t+2 reuses the score columns of tile t once the softmax warps
+             * have read them, and runs at most two tiles ahead of GEMM2. */
             uint32_t n1 = 0, n2 = 0;
             long long t0 = clock64();
             while (ok && n2 < n) {
@@ -488,13 +487,15 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
                         issue_gemm2(c, tmem, gt % kStages, gt & 1, n2 == 0);
                         mma_commit(bar(c, B_KV_EMPTY + gt % kStages));
                         mma_commit(bar(c, B_O_READY));
+                        mma_commit_to(bar(c, B_X_EMPTY + (gt & 1)), (uint16_t)(1u << c.peer));   /* P read */
                         n2++;
                         did = true;
                     }
                 }
-                if (n1 < n && n1 <= n2 + 1) {
+                if (n1 < n && n1 <= n2 + 2) {
                     const uint32_t gt = g + n1;
-                    if (mbar_test(bar(c, kPageReady + gt % kStages), (gt / kStages) & 1)) {
+                    if (mbar_test(bar(c, kPageReady + gt % kStages), (gt / kStages) & 1) &&
+                        mbar_test(bar(c, B_S_EMPTY + (gt & 1)), ((gt >> 1) & 1) ^ 1)) {
                         tc_fence_after();
                         issue_gemm1(c, tmem, gt % kStages, gt & 1);
                         mma_commit(bar(c, B_S_FULL + (gt & 1)));
@@ -552,7 +553,13 @@ __device__ void exchanger(const Ctx &c, const Params &p, int wbeg, int wend) {
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         }
     }
-    if (leader) bulk_wait_all();                    /* every copy has landed in the peer */
+    if (leader) {
+        bulk_wait_all();                            /* every copy has landed in the peer */
+        /* the peer's GEMM2 of the last two tiles releases their slots here
+         * by a remote arrive; wait for it so none lands after exit */
+        for (uint32_t u = t >= 2 ? t - 2 : 0; u < t && ok; u++)
+            ok = wait_bar(c, bar(c, B_X_EMPTY + (u & 1)), (u >> 1) & 1, true, 20);
+    }
 }
 
 /* ---- warps 3-10: scores, softmax, epilogue -------------------------------- */
@@ -600,7 +607,6 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
                             int32_t ntok) {
     constexpr bool kQuant = KV != CT_KV_BF16;
     const float *tok_scale = reinterpret_cast<const float *>(c.smem + kOffScale + (t % kStages) * 256) + r.part * kTPT;
-    const uint32_t lane = threadIdx.x & 31;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
     const uint32_t slot = t & 1;
     if (!wait_warp(c, bar(c, B_X_FULL + slot), (t >> 1) & 1, true, 10)) return false;
@@ -610,8 +616,6 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
         const float4 w = xin[xoff(r.row, r.part * (kTPT / 4) + q4) >> 4];
         s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_remote_relaxed(mapa(bar(c, B_X_EMPTY + slot), c.peer));
     if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL + slot), kXBytes);   /* arm for tile t + 2 */
     /* quantised pages: the scores are code dot products; times the token's scale */
     if (kQuant) {
@@ -635,10 +639,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     float *rm = red + (t & 1) * kParts * kH;
     rm[r.part * kH + r.row] = mx;
     const uint32_t rb = bar(c, B_RED + (t & 1) * 4 + r.quad);
-    tc_fence_before();      /* the other parts write P over scores this thread has read */
-    warp_arrive(rb);
+    warp_arrive(rb);        /* also: the other parts may now write P over the partials this thread read */
     if (!wait_warp(c, rb, (t >> 1) & 1, false, 16)) return false;
-    tc_fence_after();
     #pragma unroll
     for (int k = 1; k < kParts; k++) mx = fmaxf(mx, rm[((r.part + k) % kParts) * kH + r.row]);
     mx *= p.qk_scale;                                       /* log2 domain */
@@ -665,10 +667,9 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     }
     r.l *= alpha;
     r.m_used = m_new;
-    /* P = bf16(2^(scale * s - m)) into the first 32 score columns of tile t
-     * (this thread read its scores in stage_tile; GEMM2 of tile t-2, which
-     * read the previous P there, completed before GEMM1 of tile t did).  The
-     * normaliser sums the fp32 probabilities. */
+    /* P = bf16(2^(scale * s - m)) into the receive slot, over partial
+     * scores of this quadrant's rows (all four parts have read theirs: the
+     * maximum exchange above).  The normaliser sums the fp32 probabilities. */
     uint32_t w[kTPT / 2];
     float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const float qk = p.qk_scale, nm = -r.m_used;
@@ -687,7 +688,12 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
         }
     }
     r.l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-    tmem_st8(tmem + r.lane_base + kTmemS + (t & 1) * 64 + r.part * (kTPT / 2), w);
+    {
+        uint8_t *pr = c.smem + kOffIn + slot * kXBytes + (r.row >> 3) * 2048 + (r.row & 7) * 128;
+        const uint32_t c0 = 2 * r.part, sw = r.row & 7;
+        *reinterpret_cast<uint4 *>(pr + ((c0 ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(pr + (((c0 + 1) ^ sw) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+    }
     /* a partial page: zero the V rows past its tokens (stale slots may hold
      * anything; the converter already wrote zeros there for quantised pages) */
     if (!kQuant && ntok < kP) {
@@ -698,9 +704,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
             const uint32_t rr = (uint32_t)ntok + rem / 8, w16 = rem % 8;
             *reinterpret_cast<uint4 *>(kvs + blk * 8192 + rr * 128 + w16 * 16) = make_uint4(0, 0, 0, 0);
         }
-        proxy_fence();
     }
-    tmem_wait_st();
+    proxy_fence();                                  /* P and zeroed rows -> the tensor core's view */
     tc_fence_before();
     warp_arrive(bar(c, B_P_FULL + (t & 1)));
     return true;
@@ -714,6 +719,8 @@ __device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t g
     tc_fence_after();
     tmem_ld16(tmem + r.lane_base + kTmemS + sb * 64 + r.part * kTPT, s);
     tmem_wait_ld();
+    tc_fence_before();
+    warp_arrive(bar(c, B_S_EMPTY + sb));            /* GEMM1 of tile gt+2 may overwrite them */
     if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) return false;
     float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
     #pragma unroll
@@ -989,7 +996,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
             mbar_init(bar(c, B_S_FULL + i), 1);
             mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
             mbar_init(bar(c, B_X_FULL + i), 1);
-            mbar_init(bar(c, B_X_EMPTY + i), kSoftmaxWarps);
+            mbar_init(bar(c, B_X_EMPTY + i), 1);            /* the peer's GEMM2 commit */
+            mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps);
         }
         for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), kParts);     /* the warps of a quadrant */
         for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), kParts);
