@@ -673,6 +673,46 @@ def run_quant(args):
         res[name]["gather_frac"] = res[name]["gather_gbs"] / hbm
         plan.close()
         kv.close()
+    # cold-tier block codecs (quant.h Q8_0 / Q4_0 / Q2_0 / Q1_0): append and gather only
+    for name, dt in (("q8_0", ct.CT_KV_Q8_0), ("q4_0", ct.CT_KV_Q4_0), ("q2_0", ct.CT_KV_Q2_0),
+                     ("q1_0", ct.CT_KV_Q1_0)):
+        kv = ct.PagedKV(B, pages_per, n_pages, PAGE, E, 0, dt, 0, sp)
+        kv.set_free_order(perm)
+        kv.append(list(range(B)), [T] * B, None)
+        bt = kv.block_table()
+        dest = (bt[:, :, None] * PAGE + np.arange(PAGE)[None, None, :]).reshape(-1).astype(np.int32)
+        dest_dev = torch.from_numpy(dest).cuda()
+        g_seqs = np.arange(B, dtype=np.uint32)
+        g_starts = np.zeros(B, np.uint32)
+        g_counts = np.full(B, T, np.uint32)
+
+        def append_b():
+            ct.check(L.ct_kv_paged_write_slots(kv.pool, None, dt, src.data_ptr(), ct.CT_KV_BF16,
+                                               dest_dev.data_ptr(), n_tok, E, sp))
+
+        def gather_b():
+            ct.check(L.ct_kv_paged_gather_batch(kv.h, g_seqs.ctypes.data, g_starts.ctypes.data, g_counts.ctypes.data,
+                                                B, gat.data_ptr(), ct.CT_KV_BF16))
+
+        r = {}
+        for what, fn in (("append", append_b), ("gather", gather_b)):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = _events(torch, 2)
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            r[what] = e0.elapsed_time(e1) / args.steps
+        code_bytes = n_tok * ct.entry_bytes(dt, E)
+        res[name] = {"append_ms": r["append"], "append_gbs": (n_tok * E * 2 + code_bytes) / (r["append"] * 1e-3) / 1e9,
+                     "gather_ms": r["gather"], "gather_gbs": (code_bytes + n_tok * E * 2) / (r["gather"] * 1e-3) / 1e9,
+                     "bytes_per_token": ct.entry_bytes(dt, E)}
+        res[name]["append_frac"] = res[name]["append_gbs"] / hbm
+        res[name]["gather_frac"] = res[name]["gather_gbs"] / hbm
+        kv.close()
     line = {"metric": "quantised paged KV: append / gather GB/s and decode KV tokens/s", "value": res["int8"]["append_gbs"],
             "unit": "GB/s (int8 quantise-on-append)", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "dtype": "int8 / e4m3 codes + fp32 per-token scale", "data": "synthetic (seed 2)",

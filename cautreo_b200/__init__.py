@@ -24,6 +24,15 @@ CT_OK, CT_ERR_ARG, CT_ERR_CUDA, CT_ERR_NOMEM, CT_ERR_FULL, CT_ERR_UNMAPPED, CT_E
     0, -1, -2, -3, -4, -5, -6, -7)
 # ct_kv_dtype_t
 CT_KV_BF16, CT_KV_F32, CT_KV_INT8, CT_KV_E4M3 = 0, 1, 2, 3
+CT_KV_Q8_0, CT_KV_Q4_0, CT_KV_Q2_0, CT_KV_Q1_0 = 4, 5, 6, 7      # block codecs of quant.h, 32 values per block
+BLOCK_BYTES = {CT_KV_Q8_0: 34, CT_KV_Q4_0: 18, CT_KV_Q2_0: 10, CT_KV_Q1_0: 6}
+
+
+def entry_bytes(dtype: int, dim: int) -> int:
+    """Bytes of one token's entry in a pool of `dtype`."""
+    if dtype in BLOCK_BYTES:
+        return dim // 32 * BLOCK_BYTES[dtype]
+    return dim * {CT_KV_BF16: 2, CT_KV_F32: 4, CT_KV_INT8: 1, CT_KV_E4M3: 1}[dtype]
 # ct_quant_type_t
 CT_QUANT_FP16, CT_QUANT_Q8_0, CT_QUANT_Q4_0, CT_QUANT_Q2_0, CT_QUANT_Q1_0 = 0, 1, 2, 3, 4
 QUANT_BLOCK_BYTES = {CT_QUANT_Q8_0: 34, CT_QUANT_Q4_0: 18, CT_QUANT_Q2_0: 10, CT_QUANT_Q1_0: 6}
@@ -337,6 +346,22 @@ class PagedKV:
         out = np.zeros((self.cfg.n_seqs, self.cfg.max_pages_per_seq), np.int32)
         check(lib().ct_kv_paged_block_table(self.h, ptr(out)))
         return out
+
+    def gather(self, seq, start, n, out, out_dtype=CT_KV_BF16):
+        """Tokens [start, start+n) of `seq` into device rows `out`."""
+        check(lib().ct_kv_paged_gather(self.h, seq, start, n, ptr(out), out_dtype), "ct_kv_paged_gather")
+
+    def gather_batch(self, seqs, starts, counts, out, out_dtype=CT_KV_BF16):
+        """Several (seq, start, count) ranges, back to back, in one launch."""
+        seqs, starts, counts = (np.ascontiguousarray(a, np.uint32) for a in (seqs, starts, counts))
+        check(lib().ct_kv_paged_gather_batch(self.h, ptr(seqs), ptr(starts), ptr(counts), len(seqs), ptr(out),
+                                              out_dtype), "ct_kv_paged_gather_batch")
+
+    def free_seq(self, seq):
+        check(lib().ct_kv_paged_free_seq(self.h, seq), "ct_kv_paged_free_seq")
+
+    def compact(self):
+        check(lib().ct_kv_paged_compact(self.h), "ct_kv_paged_compact")
 
     def seq_lens(self):
         out = np.zeros(self.cfg.n_seqs, np.uint32)

@@ -135,6 +135,79 @@ CT_DEV int ct_q8_code(float x, float id) {
     return q > 127 ? 127 : (q < -127 ? -127 : q);
 }
 
+/* ---- block codecs of quant.c (32 values per block) ---------------------
+ * Type: 1 = Q8_0 (34 B), 2 = Q4_0 (18 B), 3 = Q2_0 (10 B), 4 = Q1_0 (6 B),
+ * the ct_quant_type_t values.  Block = u16 reference-fp16 scale, then the
+ * packed codes (quant.c:77-249): d = amax / qmax in fp32 (qmax 127 / 7 / 1),
+ * codes floor(x * (1/d) + 0.5) clamped to +/-qmax from the fp32 d, Q4_0 two
+ * 4-bit two's-complement codes per byte (low nibble first), Q2_0 four
+ * (code + 1) per byte (low bits first), Q1_0 the sign bits (x >= 0) with the
+ * fp16 of amax as the scale.  Decoding multiplies by the fp16-rounded d. */
+template <int Type> struct CtBlock {
+    static constexpr int kBytes = Type == 1 ? 34 : Type == 2 ? 18 : Type == 3 ? 10 : 6;
+};
+
+CT_DEV int ct_block_code(float x, float id, int lim) {
+    int q = (int)floorf(__fadd_rn(__fmul_rn(x, id), 0.5f));
+    return q > lim ? lim : (q < -lim ? -lim : q);
+}
+
+template <int Type>
+CT_DEV void ct_block_encode(const float *x, uint8_t *blk) {
+    float amax = 0.0f;
+    #pragma unroll
+    for (int i = 0; i < 32; i++) { const float a = fabsf(x[i]); if (a > amax) amax = a; }
+    if (Type == 4) {
+        const uint16_t h = ct_ref_f32_to_fp16(amax);
+        blk[0] = (uint8_t)h; blk[1] = (uint8_t)(h >> 8);
+        #pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+            uint32_t byte = 0;
+            #pragma unroll
+            for (int j = 0; j < 8; j++) if (x[i + j] >= 0) byte |= 1u << j;
+            blk[2 + i / 8] = (uint8_t)byte;
+        }
+        return;
+    }
+    const float qmax = Type == 1 ? 127.0f : Type == 2 ? 7.0f : 1.0f;
+    const float d = __fdiv_rn(amax, qmax);
+    const uint16_t h = ct_ref_f32_to_fp16(d);
+    blk[0] = (uint8_t)h; blk[1] = (uint8_t)(h >> 8);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    if (Type == 1) {
+        #pragma unroll
+        for (int i = 0; i < 32; i++) blk[2 + i] = (uint8_t)(int8_t)ct_block_code(x[i], id, 127);
+    } else if (Type == 2) {
+        #pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+            const int q0 = ct_block_code(x[i], id, 7), q1 = ct_block_code(x[i + 1], id, 7);
+            blk[2 + i / 2] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
+        }
+    } else {
+        #pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            uint32_t byte = 0;
+            #pragma unroll
+            for (int j = 0; j < 4; j++) byte |= (uint32_t)((ct_block_code(x[i + j], id, 1) + 1) & 3) << (2 * j);
+            blk[2 + i / 4] = (uint8_t)byte;
+        }
+    }
+}
+
+template <int Type>
+CT_DEV void ct_block_decode(const uint8_t *blk, float *x) {
+    const float d = ct_ref_fp16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+    #pragma unroll
+    for (int i = 0; i < 32; i++) {
+        int q;
+        if (Type == 1) q = (int8_t)blk[2 + i];
+        else if (Type == 2) { q = (blk[2 + i / 2] >> (4 * (i & 1))) & 0xF; if (q >= 8) q -= 16; }
+        else if (Type == 3) q = (int)((blk[2 + i / 4] >> (2 * (i & 3))) & 3) - 1;
+        else { x[i] = (blk[2 + i / 8] >> (i & 7)) & 1 ? d : -d; continue; }
+        x[i] = __fmul_rn((float)q, d);
+    }
+}
+
 /* e4m3 code of x * id, round-to-nearest-even, saturating to +/-448. */
 CT_DEV uint8_t ct_e4m3_code(float x, float id) {
     return (uint8_t)__nv_cvt_float_to_fp8(__fmul_rn(x, id), __NV_SATFINITE, __NV_E4M3);

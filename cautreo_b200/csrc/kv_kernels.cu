@@ -9,10 +9,14 @@
  * (bf16 / fp32 / int8 / e4m3); quantised pools add scales
  * [n_pages][page_tokens] fp32.  A token entry of the MLA cache is 576 bf16
  * = 1152 B (9 x 128 B lines); int8/e4m3 entries are 576 B + a 4 B scale.
- * Every kernel moves data in 16-byte vectors and requires dim % 16 == 0.
+ * Block-quantised pools (Q8_0 / Q4_0 / Q2_0 / Q1_0) hold dim/32 blocks per
+ * token (612 / 324 / 180 / 108 B for 576 values) and no scales array.
+ * Element pools move data in 16-byte vectors and require dim % 16 == 0;
+ * block pools require dim % 32 == 0 and stage each entry in shared memory.
  */
 #include "../../include/hal.h"
 #include "../../include/kv_cache.h"
+#include "../../include/quant.h"
 #include "ct_internal.h"
 
 namespace {
@@ -223,6 +227,141 @@ __global__ void __launch_bounds__(256) k_gather_batch(const void *pool, const fl
     gather_token<PoolDtype, OutBf16, MaxChunks>(pool, scales, slot, dim, static_cast<uint8_t *>(out) + out_elt);
 }
 
+/* K1b / K3c: block-quantised pools, one warp per token.  Lane l owns blocks
+ * l, l+32, ...; an entry is staged in shared memory so that it moves to or
+ * from HBM in 4-byte (or, for entries of odd word count, 2-byte) words. */
+constexpr int kMaxBlocks = 128;                 /* dim <= 4096 */
+
+__device__ __forceinline__ void copy_entry(uint8_t *dst, const uint8_t *src, uint32_t bytes, uint32_t lane) {
+    if ((bytes & 3) == 0) {
+        for (uint32_t i = lane; i < bytes / 4; i += 32)
+            reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
+    } else {
+        for (uint32_t i = lane; i < bytes / 2; i += 32)
+            reinterpret_cast<uint16_t *>(dst)[i] = reinterpret_cast<const uint16_t *>(src)[i];
+    }
+}
+
+template <bool SrcBf16, int Type>
+__global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void *src, const int32_t *dest,
+                                                      uint32_t n, uint32_t dim) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    __shared__ __align__(16) uint8_t stage[kWarps][kB * kMaxBlocks];
+    const uint32_t warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
+    const uint32_t lane = threadIdx.x & 31;
+    if (warp >= n) return;
+    const int32_t slot = dest[warp];
+    if (slot < 0) return;
+    const uint32_t nb = dim / 32, eb = nb * kB;
+    uint8_t *buf = stage[threadIdx.x >> 5];
+    for (uint32_t b = lane; b < nb; b += 32) {
+        float x[32];
+        if (SrcBf16) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + (size_t)warp * dim + b * 32);
+            #pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint4 v = __ldg(p + i);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                #pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    x[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+                    x[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+                }
+            }
+        } else {
+            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(src) + (size_t)warp * dim + b * 32);
+            #pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 v = __ldg(p + i);
+                x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+            }
+        }
+        ct_block_encode<Type>(x, buf + b * kB);
+    }
+    __syncwarp();
+    copy_entry(pool + (size_t)slot * eb, buf, eb, lane);
+}
+
+template <int Type, bool OutBf16>
+__device__ __forceinline__ void gather_block_token(const uint8_t *pool, size_t slot, uint32_t dim, uint8_t *buf,
+                                                   void *out_row) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t nb = dim / 32, eb = nb * kB;
+    copy_entry(buf, pool + slot * eb, eb, lane);
+    __syncwarp();
+    for (uint32_t b = lane; b < nb; b += 32) {
+        float x[32];
+        ct_block_decode<Type>(buf + b * kB, x);
+        if (OutBf16) {
+            uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_row) + b * 32);
+            #pragma unroll
+            for (int i = 0; i < 4; i++) {
+                uint32_t o[4];
+                #pragma unroll
+                for (int j = 0; j < 4; j++)
+                    o[j] = (uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j]) | ((uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j + 1]) << 16);
+                __stcs(p + i, make_uint4(o[0], o[1], o[2], o[3]));
+            }
+        } else {
+            float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(out_row) + b * 32);
+            #pragma unroll
+            for (int i = 0; i < 8; i++) __stcs(p + i, make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
+        }
+    }
+}
+
+/* Tokens [start, start+n) of one sequence (desc == nullptr), or desc[y] =
+ * (seq, start, count, first output row) for blockIdx.y. */
+template <int Type, bool OutBf16>
+__global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, const int32_t *bt, uint32_t max_pages,
+                                                       uint32_t page_tokens, uint32_t dim, uint32_t start, uint32_t n,
+                                                       const int4 *desc, void *out) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    __shared__ __align__(16) uint8_t stage[kWarps][kB * kMaxBlocks];
+    const uint32_t t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+    const int32_t *bt_row = bt;
+    uint32_t pos = start + t;
+    size_t row = t;
+    if (desc) {
+        const int4 d = desc[blockIdx.y];
+        if (t >= (uint32_t)d.z) return;
+        bt_row = bt + (size_t)d.x * max_pages;
+        pos = (uint32_t)d.y + t;
+        row = (size_t)(uint32_t)d.w + t;
+    } else if (t >= n) {
+        return;
+    }
+    const int32_t pg = bt_row[pos / page_tokens];
+    const size_t slot = (size_t)pg * page_tokens + pos % page_tokens;
+    gather_block_token<Type, OutBf16>(pool, slot, dim, stage[threadIdx.x >> 5],
+                                      static_cast<uint8_t *>(out) + row * dim * (OutBf16 ? 2 : 4));
+}
+
+template <bool SrcBf16>
+int launch_write_blocks(uint32_t type, void *pool, const void *src, const int32_t *dest, uint32_t n, uint32_t dim,
+                        cudaStream_t st) {
+    const int blocks = (int)((n + kWarps - 1) / kWarps);
+    uint8_t *p = static_cast<uint8_t *>(pool);
+    switch (type) {
+        case CT_KV_Q8_0: k_write_blocks<SrcBf16, CT_QUANT_Q8_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
+        case CT_KV_Q4_0: k_write_blocks<SrcBf16, CT_QUANT_Q4_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
+        case CT_KV_Q2_0: k_write_blocks<SrcBf16, CT_QUANT_Q2_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
+        default:         k_write_blocks<SrcBf16, CT_QUANT_Q1_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
+    }
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "write_slots");
+}
+
+template <int Type>
+void launch_gather_blocks(bool ob, const void *pool, const int32_t *bt, uint32_t maxp, uint32_t P, uint32_t dim,
+                          uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc, void *out, cudaStream_t st) {
+    const dim3 grid((n + kWarps - 1) / kWarps, desc ? n_desc : 1);
+    const uint8_t *p = static_cast<const uint8_t *>(pool);
+    if (ob) k_gather_blocks<Type, true><<<grid, 256, 0, st>>>(p, bt, maxp, P, dim, start, n, desc, out);
+    else    k_gather_blocks<Type, false><<<grid, 256, 0, st>>>(p, bt, maxp, P, dim, start, n, desc, out);
+}
+
 /* K4 (pages): block b copies whole page map[b] -> b; 16-byte vectors with
  * four loads in flight per thread. */
 __global__ void __launch_bounds__(256) k_move_pages(const uint4 *src, const float *src_sc, uint4 *dst,
@@ -288,10 +427,15 @@ extern "C" int ct_kv_paged_write_slots(void *pool, float *scales, uint32_t pool_
                                        uint32_t dim, void *stream) {
     if (!pool || !entries || !dest_slot || dim == 0 || dim % 16 != 0) return CT_ERR_ARG;
     if ((pool_dtype == CT_KV_INT8 || pool_dtype == CT_KV_E4M3) && !scales) return CT_ERR_ARG;
+    const bool blocks = pool_dtype >= CT_KV_Q8_0 && pool_dtype <= CT_KV_Q1_0;
+    if (blocks && (dim % 32 != 0 || dim / 32 > (uint32_t)kMaxBlocks)) return CT_ERR_ARG;
     if (n == 0) return CT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     const bool bf = src_dtype == CT_KV_BF16;
     if (!bf && src_dtype != CT_KV_F32) return CT_ERR_ARG;
+    if (blocks)
+        return bf ? launch_write_blocks<true>(pool_dtype, pool, entries, dest_slot, n, dim, st)
+                  : launch_write_blocks<false>(pool_dtype, pool, entries, dest_slot, n, dim, st);
     switch (pool_dtype) {
         case CT_KV_BF16: return bf ? launch_write<true, CT_KV_BF16>(pool, scales, entries, dest_slot, n, dim, st)
                                    : launch_write<false, CT_KV_BF16>(pool, scales, entries, dest_slot, n, dim, st);
@@ -350,7 +494,18 @@ int gather_any(uint32_t pool_dtype, bool ob, const void *pool, const float *scal
                uint32_t P, uint32_t dim, uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc, void *out,
                cudaStream_t st) {
     const uint32_t chunks = dim / 16;
-    int rc;
+    int rc = CT_OK;
+    if (pool_dtype >= CT_KV_Q8_0 && pool_dtype <= CT_KV_Q1_0) {
+        if (dim % 32 != 0 || dim / 32 > (uint32_t)kMaxBlocks) return CT_ERR_ARG;
+        switch (pool_dtype) {
+            case CT_KV_Q8_0: launch_gather_blocks<CT_QUANT_Q8_0>(ob, pool, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+            case CT_KV_Q4_0: launch_gather_blocks<CT_QUANT_Q4_0>(ob, pool, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+            case CT_KV_Q2_0: launch_gather_blocks<CT_QUANT_Q2_0>(ob, pool, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+            default:         launch_gather_blocks<CT_QUANT_Q1_0>(ob, pool, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
+        }
+        ct__count_launches(1);
+        return ct__cuda_status(cudaGetLastError(), "gather");
+    }
     switch (pool_dtype) {
         case CT_KV_BF16: rc = gather_dispatch<CT_KV_BF16>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;
         case CT_KV_F32:  rc = gather_dispatch<CT_KV_F32>(ob, chunks, pool, scales, bt, maxp, P, dim, start, n, desc, n_desc, out, st); break;

@@ -247,7 +247,9 @@ extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chu
                 case CT_KV_F32: CT_SIMT(CT_KV_F32)
                 case CT_KV_INT8: CT_SIMT(CT_KV_INT8)
                 case CT_KV_E4M3: CT_SIMT(CT_KV_E4M3)
-                default: return CT_ERR_ARG;
+                default:
+                    ct__set_error("MLA decode: block-quantised pools are gathered to bf16 before decoding");
+                    return CT_ERR_UNSUPPORTED;
 #undef CT_SIMT
             }
             rc = ct__cuda_status(cudaGetLastError(), "mla_simt");

@@ -17,75 +17,27 @@
 
 namespace {
 
-__device__ __forceinline__ float block_amax(const float *x) {
-    float amax = 0.0f;
-    #pragma unroll 8
-    for (int i = 0; i < 32; i++) { float a = fabsf(x[i]); if (a > amax) amax = a; }
-    return amax;
-}
-
-__device__ __forceinline__ int qround(float x, float id, int lim) {
-    int q = (int)floorf(__fadd_rn(__fmul_rn(x, id), 0.5f));
-    return q > lim ? lim : (q < -lim ? -lim : q);
-}
-
-__device__ __forceinline__ void put_scale(uint8_t *blk, uint16_t h) { blk[0] = (uint8_t)h; blk[1] = (uint8_t)(h >> 8); }
-__device__ __forceinline__ float get_scale(const uint8_t *blk) {
-    return ct_ref_fp16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
-}
-
+/* One thread per block; the arithmetic is ct_block_encode / ct_block_decode,
+ * shared with the block-quantised page pools of the paged cache. */
 template <int Type>
 __global__ void k_quant_blocks(const float *src, uint8_t *dst, int64_t nb) {
-    constexpr int kBytes = Type == CT_QUANT_Q8_0 ? 34 : Type == CT_QUANT_Q4_0 ? 18 : Type == CT_QUANT_Q2_0 ? 10 : 6;
+    constexpr int kBytes = CtBlock<Type>::kBytes;
     for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
-        const float *x = src + b * 32;
-        uint8_t *blk = dst + b * kBytes;
-        const float amax = block_amax(x);
-        if (Type == CT_QUANT_Q1_0) {
-            put_scale(blk, ct_ref_f32_to_fp16(amax));
-            for (int i = 0; i < 32; i += 8) {
-                uint32_t byte = 0;
-                for (int j = 0; j < 8; j++) if (x[i + j] >= 0) byte |= 1u << j;
-                blk[2 + i / 8] = (uint8_t)byte;
-            }
-            continue;
-        }
-        const float qmax = Type == CT_QUANT_Q8_0 ? 127.0f : Type == CT_QUANT_Q4_0 ? 7.0f : 1.0f;
-        const float d = __fdiv_rn(amax, qmax);
-        put_scale(blk, ct_ref_f32_to_fp16(d));
-        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        if (Type == CT_QUANT_Q8_0) {
-            for (int i = 0; i < 32; i++) blk[2 + i] = (uint8_t)(int8_t)qround(x[i], id, 127);
-        } else if (Type == CT_QUANT_Q4_0) {
-            for (int i = 0; i < 32; i += 2) {
-                int q0 = qround(x[i], id, 7), q1 = qround(x[i + 1], id, 7);
-                blk[2 + i / 2] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
-            }
-        } else {
-            for (int i = 0; i < 32; i += 4) {
-                uint32_t byte = 0;
-                for (int j = 0; j < 4; j++) byte |= (uint32_t)((qround(x[i + j], id, 1) + 1) & 3) << (2 * j);
-                blk[2 + i / 4] = (uint8_t)byte;
-            }
-        }
+        float x[32];
+        #pragma unroll
+        for (int i = 0; i < 32; i++) x[i] = src[b * 32 + i];
+        ct_block_encode<Type>(x, dst + b * kBytes);
     }
 }
 
 template <int Type>
 __global__ void k_dequant_blocks(const uint8_t *src, float *dst, int64_t nb) {
-    constexpr int kBytes = Type == CT_QUANT_Q8_0 ? 34 : Type == CT_QUANT_Q4_0 ? 18 : Type == CT_QUANT_Q2_0 ? 10 : 6;
+    constexpr int kBytes = CtBlock<Type>::kBytes;
     for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
-        const uint8_t *blk = src + b * kBytes;
-        float *x = dst + b * 32;
-        const float d = get_scale(blk);
-        for (int i = 0; i < 32; i++) {
-            int q;
-            if (Type == CT_QUANT_Q8_0) q = (int8_t)blk[2 + i];
-            else if (Type == CT_QUANT_Q4_0) { q = (blk[2 + i / 2] >> (4 * (i & 1))) & 0xF; if (q >= 8) q -= 16; }
-            else if (Type == CT_QUANT_Q2_0) q = (int)((blk[2 + i / 4] >> (2 * (i & 3))) & 3) - 1;
-            else { x[i] = (blk[2 + i / 8] >> (i & 7)) & 1 ? d : -d; continue; }
-            x[i] = __fmul_rn((float)q, d);
-        }
+        float x[32];
+        ct_block_decode<Type>(src + b * kBytes, x);
+        #pragma unroll
+        for (int i = 0; i < 32; i++) dst[b * 32 + i] = x[i];
     }
 }
 

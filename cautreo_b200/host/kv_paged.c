@@ -41,7 +41,7 @@ struct ct_kv_paged {
     ct_kv_paged_config_t cfg;
     int host_only;              /* device < 0: tables only, no device memory */
     cudaStream_t stream;
-    size_t elt;                 /* bytes per value in the pool */
+    size_t entry_bytes;         /* bytes of one token's entry in the pool */
     size_t page_bytes;          /* page_tokens * entry_dim * elt */
     /* device */
     void *pool;
@@ -191,7 +191,7 @@ void ct_kv_paged_destroy(ct_kv_paged_t *h) {
 }
 
 ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg) {
-    if (!cfg || cfg->n_seqs == 0 || cfg->n_pages == 0 || cfg->max_pages_per_seq == 0 || cfg->dtype > CT_KV_E4M3) {
+    if (!cfg || cfg->n_seqs == 0 || cfg->n_pages == 0 || cfg->max_pages_per_seq == 0 || cfg->dtype > CT_KV_Q1_0) {
         ct__set_error("ct_kv_paged_create: bad config");
         return NULL;
     }
@@ -204,8 +204,20 @@ ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg) {
     h->host_only = cfg->device < 0;
     if (!h->host_only && ct__cuda_status(cudaSetDevice(cfg->device), "ct_kv_paged_create")) { free(h); return NULL; }
     const uint32_t S = h->cfg.n_seqs, MP = h->cfg.max_pages_per_seq, NP = h->cfg.n_pages, P = h->cfg.page_tokens;
-    h->elt = h->cfg.dtype == CT_KV_BF16 ? 2 : h->cfg.dtype == CT_KV_F32 ? 4 : 1;
-    h->page_bytes = (size_t)P * h->cfg.entry_dim * h->elt;
+    const uint32_t dt = h->cfg.dtype, D = h->cfg.entry_dim;
+    if (dt >= CT_KV_Q8_0) {
+        /* block codecs: D/32 blocks of 34 / 18 / 10 / 6 bytes per token */
+        static const uint32_t blk[4] = {34, 18, 10, 6};
+        h->entry_bytes = (size_t)(D / 32) * blk[dt - CT_KV_Q8_0];
+        if (D % 32 != 0 || D > 4096 || ((size_t)P * h->entry_bytes) % 16 != 0) {
+            ct__set_error("ct_kv_paged_create: block pools need entry_dim % 32 == 0, <= 4096, and 16-byte pages");
+            free(h);
+            return NULL;
+        }
+    } else {
+        h->entry_bytes = (size_t)D * (dt == CT_KV_BF16 ? 2 : dt == CT_KV_F32 ? 4 : 1);
+    }
+    h->page_bytes = (size_t)P * h->entry_bytes;
     const size_t bt_n = (size_t)S * MP;
     h->bt = (int32_t *)malloc(bt_n * sizeof(int32_t));
     h->len = (uint32_t *)calloc(S, sizeof(uint32_t));

@@ -100,6 +100,20 @@ typedef enum {
     CT_KV_F32  = 1,   /* 4 B per value */
     CT_KV_INT8 = 2,   /* int8 codes + one fp32 scale per token (amax/127) */
     CT_KV_E4M3 = 3,   /* fp8 e4m3 codes + one fp32 scale per token (amax/448) */
+    /* Cold-tier block codecs of quant.h (src/quant/quant.c:77-249): a token's
+     * entry is entry_dim/32 blocks, byte for byte what ct_quant_q8_0 / _q4_0 /
+     * _q2_0 / _q1_0 write for the token's values (a fp16 scale per 32 values
+     * inside each block, no separate scales array).  entry_dim must be a
+     * multiple of 32 (at most 4096) and page_tokens x entry bytes a multiple
+     * of 16.  Append quantises, gather dequantises to bf16 or fp32 exactly as
+     * ct_quant_deq*_0 (then rounds to bf16); compaction, fork and checkpoints
+     * move the bytes.  The decode kernels do not read these pools (gather
+     * them to bf16 first): ct_attn_mla_decode_paged over one returns
+     * CT_ERR_UNSUPPORTED. */
+    CT_KV_Q8_0 = 4,   /* 34 B per 32 values */
+    CT_KV_Q4_0 = 5,   /* 18 B per 32 values */
+    CT_KV_Q2_0 = 6,   /* 10 B per 32 values */
+    CT_KV_Q1_0 = 7,   /*  6 B per 32 values */
 } ct_kv_dtype_t;
 
 typedef struct {

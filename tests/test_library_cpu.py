@@ -349,3 +349,20 @@ def test_fork_survives_compaction_and_checkpoint(tmp_path):
     assert np.array_equal(g.block_table(), h.block_table())
     h.close()
     g.close()
+
+
+def test_block_pool_creation_rules():
+    """Block-quantised pools (quant.h codecs): entry_dim a multiple of 32 and
+    at most 4096, pages a multiple of 16 bytes; the entry sizes follow the
+    block structs (34 / 18 / 10 / 6 B per 32 values)."""
+    assert [ct.entry_bytes(d, 576) for d in (ct.CT_KV_Q8_0, ct.CT_KV_Q4_0, ct.CT_KV_Q2_0, ct.CT_KV_Q1_0)] == \
+        [612, 324, 180, 108]
+    ok = ct.PagedKV(2, 4, 8, page_tokens=64, entry_dim=576, dtype=ct.CT_KV_Q4_0, device=-1)
+    ok.close()
+    L = ct.lib()
+    for dim, P, dt in ((48, 64, ct.CT_KV_Q4_0),      # not a multiple of 32
+                       (8192, 64, ct.CT_KV_Q8_0),    # more than 4096 values
+                       (32, 4, ct.CT_KV_Q4_0),       # 4 x 18 B pages are not 16-byte multiples
+                       (576, 64, 8)):                # no such dtype
+        cfg = ct.PagedConfig(2, 4, 8, P, dim, 0, dt, -1)
+        assert not L.ct_kv_paged_create(C.byref(cfg)), (dim, P, dt)
