@@ -12,7 +12,8 @@
  * Block-quantised pools (Q8_0 / Q4_0 / Q2_0 / Q1_0) hold dim/32 blocks per
  * token (612 / 324 / 180 / 108 B for 576 values) and no scales array.
  * Element pools move data in 16-byte vectors and require dim % 16 == 0;
- * block pools require dim % 32 == 0 and stage each entry in shared memory.
+ * block pools require dim % 32 == 0 and stage tiles of entries in shared
+ * memory.
  */
 #include "../../include/hal.h"
 #include "../../include/kv_cache.h"
@@ -227,127 +228,190 @@ __global__ void __launch_bounds__(256) k_gather_batch(const void *pool, const fl
     gather_token<PoolDtype, OutBf16, MaxChunks>(pool, scales, slot, dim, static_cast<uint8_t *>(out) + out_elt);
 }
 
-/* K1b / K3c: block-quantised pools, one warp per token.  Lane l owns blocks
- * l, l+32, ...; an entry is staged in shared memory so that it moves to or
- * from HBM in 4-byte (or, for entries of odd word count, 2-byte) words. */
+/* K1b / K3c: block-quantised pools.  A CTA takes a tile of `tile` tokens
+ * and spreads its (token, block) pairs over all 256 threads; the tile's
+ * entries are staged in shared memory ([tile][entry bytes]) so that they
+ * move to or from HBM as consecutive 4-byte words (2-byte words when an
+ * entry is an odd number of them), and every thread reads or writes whole
+ * 64-byte (bf16) / 128-byte (fp32) runs of values. */
 constexpr int kMaxBlocks = 128;                 /* dim <= 4096 */
+constexpr uint32_t kBlkSmem = 48 * 1024;        /* stage bytes per CTA */
 
-__device__ __forceinline__ void copy_entry(uint8_t *dst, const uint8_t *src, uint32_t bytes, uint32_t lane) {
-    if ((bytes & 3) == 0) {
-        for (uint32_t i = lane; i < bytes / 4; i += 32)
-            reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
-    } else {
-        for (uint32_t i = lane; i < bytes / 2; i += 32)
-            reinterpret_cast<uint16_t *>(dst)[i] = reinterpret_cast<const uint16_t *>(src)[i];
-    }
+__host__ __device__ inline uint32_t block_tile(uint32_t eb) {
+    const uint32_t t = kBlkSmem / eb;
+    return t > 64 ? 64 : (t < 1 ? 1 : t);
 }
 
-template <bool SrcBf16, int Type>
-__global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void *src, const int32_t *dest,
-                                                      uint32_t n, uint32_t dim) {
+/* One block between shared memory (2-byte aligned) and registers. */
+template <int Type>
+__device__ __forceinline__ void block_load(const uint8_t *s, uint8_t *b) {
     constexpr int kB = CtBlock<Type>::kBytes;
-    __shared__ __align__(16) uint8_t stage[kWarps][kB * kMaxBlocks];
-    const uint32_t warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    const uint32_t lane = threadIdx.x & 31;
-    if (warp >= n) return;
-    const int32_t slot = dest[warp];
-    if (slot < 0) return;
-    const uint32_t nb = dim / 32, eb = nb * kB;
-    uint8_t *buf = stage[threadIdx.x >> 5];
-    for (uint32_t b = lane; b < nb; b += 32) {
-        float x[32];
-        if (SrcBf16) {
-            const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + (size_t)warp * dim + b * 32);
+    #pragma unroll
+    for (int i = 0; i < kB / 2; i++) {
+        const uint16_t h = reinterpret_cast<const uint16_t *>(s)[i];
+        b[2 * i] = (uint8_t)h;
+        b[2 * i + 1] = (uint8_t)(h >> 8);
+    }
+}
+template <int Type>
+__device__ __forceinline__ void block_store(uint8_t *s, const uint8_t *b) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    #pragma unroll
+    for (int i = 0; i < kB / 2; i++)
+        reinterpret_cast<uint16_t *>(s)[i] = (uint16_t)(b[2 * i] | (b[2 * i + 1] << 8));
+}
+
+/* The 32 source values of block b of token tok, as raw 16-byte vectors. */
+template <bool SrcBf16>
+struct BlockSrc {
+    uint4 v[SrcBf16 ? 4 : 8];
+    __device__ __forceinline__ void load(const void *src, size_t tok, uint32_t dim, uint32_t b) {
+        const uint4 *q = SrcBf16 ? reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + tok * dim + b * 32)
+                                 : reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + tok * dim + b * 32);
+        #pragma unroll
+        for (int i = 0; i < (SrcBf16 ? 4 : 8); i++) v[i] = __ldcs(q + i);
+    }
+    __device__ __forceinline__ void values(float *x) const {
+        #pragma unroll
+        for (int i = 0; i < (SrcBf16 ? 4 : 8); i++) {
+            const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
             #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint4 v = __ldg(p + i);
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                #pragma unroll
-                for (int j = 0; j < 4; j++) {
+            for (int j = 0; j < 4; j++) {
+                if (SrcBf16) {
                     x[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
                     x[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+                } else {
+                    x[4 * i + j] = __uint_as_float(w[j]);
                 }
             }
-        } else {
-            const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(src) + (size_t)warp * dim + b * 32);
-            #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float4 v = __ldg(p + i);
-                x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
-            }
         }
-        ct_block_encode<Type>(x, buf + b * kB);
     }
-    __syncwarp();
-    copy_entry(pool + (size_t)slot * eb, buf, eb, lane);
+};
+
+/* A CTA takes `tile` consecutive source tokens; threads take (token, block)
+ * pairs (many CTAs per SM keep the loads in flight). */
+template <bool SrcBf16, int Type>
+__global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void *src, const int32_t *dest,
+                                                      uint32_t n, uint32_t dim, uint32_t tile) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    extern __shared__ __align__(16) uint8_t stage[];
+    const uint32_t nb = dim / 32, eb = nb * kB;
+    const uint32_t t0 = blockIdx.x * tile, cnt = min(tile, n - t0);
+    for (uint32_t p = threadIdx.x; p < cnt * nb; p += 256) {
+        const uint32_t t = p / nb, b = p - t * nb;
+        if (dest[t0 + t] < 0) continue;
+        BlockSrc<SrcBf16> in;
+        in.load(src, t0 + t, dim, b);
+        float x[32];
+        in.values(x);
+        uint8_t blk[kB];
+        ct_block_encode<Type>(x, blk);
+        block_store<Type>(stage + t * eb + b * kB, blk);
+    }
+    __syncthreads();
+    if ((eb & 3) == 0) {
+        const uint32_t W = eb / 4;
+        for (uint32_t p = threadIdx.x; p < cnt * W; p += 256) {
+            const uint32_t t = p / W, w = p - t * W;
+            const int32_t slot = dest[t0 + t];
+            if (slot >= 0)
+                reinterpret_cast<uint32_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint32_t *>(stage + t * eb)[w];
+        }
+    } else {
+        const uint32_t W = eb / 2;
+        for (uint32_t p = threadIdx.x; p < cnt * W; p += 256) {
+            const uint32_t t = p / W, w = p - t * W;
+            const int32_t slot = dest[t0 + t];
+            if (slot >= 0)
+                reinterpret_cast<uint16_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint16_t *>(stage + t * eb)[w];
+        }
+    }
 }
 
+/* Tokens [start, start+n) of one sequence (desc == nullptr), or of desc[y]
+ * = (seq, start, count, first output row) for blockIdx.y.  A CTA takes
+ * `tile` consecutive tokens of one page: x = page index within the range x
+ * tiles per page + tile within the page.  Those entries are one contiguous
+ * run of the page, copied to shared memory as 16-byte vectors (rounded out
+ * to 16-byte boundaries inside the page), four in flight per thread. */
 template <int Type, bool OutBf16>
-__device__ __forceinline__ void gather_block_token(const uint8_t *pool, size_t slot, uint32_t dim, uint8_t *buf,
-                                                   void *out_row) {
+__global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, const int32_t *bt, uint32_t max_pages,
+                                                       uint32_t page_tokens, uint32_t dim, uint32_t start, uint32_t n,
+                                                       const int4 *desc, void *out, uint32_t tile) {
     constexpr int kB = CtBlock<Type>::kBytes;
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t nb = dim / 32, eb = nb * kB;
-    copy_entry(buf, pool + slot * eb, eb, lane);
-    __syncwarp();
-    for (uint32_t b = lane; b < nb; b += 32) {
+    extern __shared__ __align__(16) uint8_t stage[];
+    const uint32_t nb = dim / 32, eb = nb * kB, P = page_tokens;
+    const int32_t *bt_row = bt;
+    size_t row0 = 0;
+    if (desc) {
+        const int4 d = desc[blockIdx.y];
+        bt_row = bt + (size_t)d.x * max_pages;
+        start = (uint32_t)d.y;
+        n = (uint32_t)d.z;
+        row0 = (uint32_t)d.w;
+    }
+    if (n == 0) return;
+    const uint32_t per_page = (P + tile - 1) / tile;
+    const uint32_t lp = start / P + blockIdx.x / per_page;
+    const uint32_t sub = blockIdx.x % per_page;
+    const uint32_t lo = max(start, lp * P + sub * tile);
+    const uint32_t hi = min(min(start + n, lp * P + P), lp * P + sub * tile + tile);
+    if (lo >= hi) return;
+    const uint8_t *page = pool + (size_t)bt_row[lp] * P * eb;
+    const uint32_t b_lo = (lo - lp * P) * eb, b_hi = (hi - lp * P) * eb;
+    const uint32_t a = b_lo & ~15u, nvec = (((b_hi + 15u) & ~15u) - a) / 16;
+    const uint4 *src = reinterpret_cast<const uint4 *>(page + a);
+    uint4 *dst = reinterpret_cast<uint4 *>(stage);
+    for (uint32_t v0 = threadIdx.x; v0 < nvec; v0 += 4 * 256) {
+        uint4 r[4];
+        #pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (v0 + 256 * k < nvec) r[k] = __ldcs(src + v0 + 256 * k);
+        #pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (v0 + 256 * k < nvec) dst[v0 + 256 * k] = r[k];
+    }
+    __syncthreads();
+    const uint32_t cnt = hi - lo, off = b_lo - a;
+    row0 += lo - start;
+    for (uint32_t p = threadIdx.x; p < cnt * nb; p += 256) {
+        const uint32_t t = p / nb, b = p - t * nb;
+        uint8_t blk[kB];
+        block_load<Type>(stage + off + t * eb + b * kB, blk);
         float x[32];
-        ct_block_decode<Type>(buf + b * kB, x);
+        ct_block_decode<Type>(blk, x);
+        uint8_t *orow = static_cast<uint8_t *>(out) + (row0 + t) * dim * (OutBf16 ? 2 : 4);
         if (OutBf16) {
-            uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_row) + b * 32);
+            uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(orow) + b * 32);
             #pragma unroll
             for (int i = 0; i < 4; i++) {
                 uint32_t o[4];
                 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     o[j] = (uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j]) | ((uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j + 1]) << 16);
-                __stcs(p + i, make_uint4(o[0], o[1], o[2], o[3]));
+                __stcs(q + i, make_uint4(o[0], o[1], o[2], o[3]));
             }
         } else {
-            float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(out_row) + b * 32);
+            float4 *q = reinterpret_cast<float4 *>(reinterpret_cast<float *>(orow) + b * 32);
             #pragma unroll
-            for (int i = 0; i < 8; i++) __stcs(p + i, make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
+            for (int i = 0; i < 8; i++) __stcs(q + i, make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
         }
     }
-}
-
-/* Tokens [start, start+n) of one sequence (desc == nullptr), or desc[y] =
- * (seq, start, count, first output row) for blockIdx.y. */
-template <int Type, bool OutBf16>
-__global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, const int32_t *bt, uint32_t max_pages,
-                                                       uint32_t page_tokens, uint32_t dim, uint32_t start, uint32_t n,
-                                                       const int4 *desc, void *out) {
-    constexpr int kB = CtBlock<Type>::kBytes;
-    __shared__ __align__(16) uint8_t stage[kWarps][kB * kMaxBlocks];
-    const uint32_t t = blockIdx.x * kWarps + (threadIdx.x >> 5);
-    const int32_t *bt_row = bt;
-    uint32_t pos = start + t;
-    size_t row = t;
-    if (desc) {
-        const int4 d = desc[blockIdx.y];
-        if (t >= (uint32_t)d.z) return;
-        bt_row = bt + (size_t)d.x * max_pages;
-        pos = (uint32_t)d.y + t;
-        row = (size_t)(uint32_t)d.w + t;
-    } else if (t >= n) {
-        return;
-    }
-    const int32_t pg = bt_row[pos / page_tokens];
-    const size_t slot = (size_t)pg * page_tokens + pos % page_tokens;
-    gather_block_token<Type, OutBf16>(pool, slot, dim, stage[threadIdx.x >> 5],
-                                      static_cast<uint8_t *>(out) + row * dim * (OutBf16 ? 2 : 4));
 }
 
 template <bool SrcBf16>
 int launch_write_blocks(uint32_t type, void *pool, const void *src, const int32_t *dest, uint32_t n, uint32_t dim,
                         cudaStream_t st) {
-    const int blocks = (int)((n + kWarps - 1) / kWarps);
+    static const uint32_t kB[4] = {34, 18, 10, 6};
+    const uint32_t eb = dim / 32 * kB[type - CT_KV_Q8_0], tile = block_tile(eb);
+    const int blocks = (int)((n + tile - 1) / tile);
+    const size_t sm = (size_t)tile * eb;
     uint8_t *p = static_cast<uint8_t *>(pool);
     switch (type) {
-        case CT_KV_Q8_0: k_write_blocks<SrcBf16, CT_QUANT_Q8_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
-        case CT_KV_Q4_0: k_write_blocks<SrcBf16, CT_QUANT_Q4_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
-        case CT_KV_Q2_0: k_write_blocks<SrcBf16, CT_QUANT_Q2_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
-        default:         k_write_blocks<SrcBf16, CT_QUANT_Q1_0><<<blocks, 256, 0, st>>>(p, src, dest, n, dim); break;
+        case CT_KV_Q8_0: k_write_blocks<SrcBf16, CT_QUANT_Q8_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
+        case CT_KV_Q4_0: k_write_blocks<SrcBf16, CT_QUANT_Q4_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
+        case CT_KV_Q2_0: k_write_blocks<SrcBf16, CT_QUANT_Q2_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
+        default:         k_write_blocks<SrcBf16, CT_QUANT_Q1_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
     }
     ct__count_launches(1);
     return ct__cuda_status(cudaGetLastError(), "write_slots");
@@ -356,10 +420,14 @@ int launch_write_blocks(uint32_t type, void *pool, const void *src, const int32_
 template <int Type>
 void launch_gather_blocks(bool ob, const void *pool, const int32_t *bt, uint32_t maxp, uint32_t P, uint32_t dim,
                           uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc, void *out, cudaStream_t st) {
-    const dim3 grid((n + kWarps - 1) / kWarps, desc ? n_desc : 1);
+    const uint32_t eb = dim / 32 * CtBlock<Type>::kBytes, tile = block_tile(eb + 32);
+    const uint32_t per_page = (P + tile - 1) / tile;
+    /* n tokens starting anywhere in a page span at most n / P + 2 pages */
+    const dim3 grid((n / P + 2) * per_page, desc ? n_desc : 1);
+    const size_t sm = (size_t)tile * eb + 32;
     const uint8_t *p = static_cast<const uint8_t *>(pool);
-    if (ob) k_gather_blocks<Type, true><<<grid, 256, 0, st>>>(p, bt, maxp, P, dim, start, n, desc, out);
-    else    k_gather_blocks<Type, false><<<grid, 256, 0, st>>>(p, bt, maxp, P, dim, start, n, desc, out);
+    if (ob) k_gather_blocks<Type, true><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, out, tile);
+    else    k_gather_blocks<Type, false><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, out, tile);
 }
 
 /* K4 (pages): block b copies whole page map[b] -> b; 16-byte vectors with
