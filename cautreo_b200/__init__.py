@@ -111,6 +111,9 @@ SIGNATURES = {
     "ct_kv_paged_set_free_order": (I, [P, P]),
     "ct_kv_paged_append": (I, [P, P, P, U32, P, U32]),
     "ct_kv_paged_free_seq": (I, [P, U32]),
+    "ct_kv_paged_append_projected": (I, [P, P, P, U32, P, P, U32, P, F, U32]),
+    "ct_kv_project_write_slots": (I, [P, P, P, F, U32, U32, U32, U32, P, P, U32, P, P]),
+    "ct_kv_project_error": (I, [I]),
     "ct_kv_paged_evict_lru": (I, [P, U32]),
     "ct_kv_paged_compact": (I, [P]),
     "ct_kv_paged_gather": (I, [P, U32, U32, U32, P, U32]),
@@ -356,6 +359,13 @@ class PagedKV:
         seqs, starts, counts = (np.ascontiguousarray(a, np.uint32) for a in (seqs, starts, counts))
         check(lib().ct_kv_paged_gather_batch(self.h, ptr(seqs), ptr(starts), ptr(counts), len(seqs), ptr(out),
                                               out_dtype), "ct_kv_paged_gather_batch")
+
+    def append_projected(self, seq_ids, counts, x, w, n_in, norm_w=None, eps=1e-6, norm_dim=0):
+        """Append tokens whose entries are W . x (+ RMS norm), computed on the device."""
+        seq_ids = np.ascontiguousarray(seq_ids, np.uint32)
+        counts = np.ascontiguousarray(counts, np.uint32)
+        check(lib().ct_kv_paged_append_projected(self.h, ptr(seq_ids), ptr(counts), len(seq_ids), ptr(x), ptr(w),
+                                                 n_in, ptr(norm_w), eps, norm_dim), "ct_kv_paged_append_projected")
 
     def free_seq(self, seq):
         check(lib().ct_kv_paged_free_seq(self.h, seq), "ct_kv_paged_free_seq")

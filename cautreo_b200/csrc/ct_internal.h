@@ -20,6 +20,12 @@ int  ct__cuda_status(int code, const char *where);
 void ct__count_launches(uint32_t n);
 /* Sets the last-error message without a CUDA code. */
 void ct__set_error(const char *msg);
+/* Stream-ordered temporary device memory from a memory pool private to the
+ * library (one per device, keeping up to 1 GiB cached between calls, so a
+ * call repeated every step neither maps nor unmaps memory).  Free on the
+ * same stream. */
+int  ct__scratch_alloc(void **p, size_t bytes, void *stream);
+void ct__scratch_free(void *p, void *stream);
 
 /* ---- MLA decode work plan (shared by host/attention.c and the kernels) -- */
 typedef struct {

@@ -36,7 +36,7 @@ bool ct_attn_forward(const float *q, const float *k, const float *v, uint32_t n_
     const size_t sb = (size_t)n_kv_heads * n_tokens * sizeof(float);
     char *buf = NULL;
     const size_t total = 2 * qb + 2 * kb + sb;
-    if (ct__cuda_status(cudaMallocAsync((void **)&buf, total, 0), "ct_attn_forward")) return false;
+    if (ct__scratch_alloc((void **)&buf, total, NULL)) return false;
     float *dq = (float *)buf, *dout = (float *)(buf + qb), *dk = (float *)(buf + 2 * qb);
     float *dv = (float *)(buf + 2 * qb + kb), *dsc = (float *)(buf + 2 * qb + 2 * kb);
     int rc = ct__cuda_status(cudaMemcpyAsync(dq, q, qb, cudaMemcpyHostToDevice, 0), "ct_attn_forward");
@@ -44,7 +44,7 @@ bool ct_attn_forward(const float *q, const float *k, const float *v, uint32_t n_
     if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(dv, v, kb, cudaMemcpyHostToDevice, 0), "ct_attn_forward");
     if (!rc) rc = ct__launch_attn_shared(dq, dk, dv, n_tokens, n_kv_heads, head_dim, scale, dout, dsc, NULL);
     if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, 0), "ct_attn_forward");
-    cudaFreeAsync(buf, 0);
+    ct__scratch_free(buf, NULL);
     if (!rc) rc = ct__cuda_status(cudaStreamSynchronize(0), "ct_attn_forward");
     return rc == CT_OK;
 }
@@ -58,11 +58,11 @@ void ct_attn_softmax(float *x, uint32_t n) {
     if (!x || n == 0) return;
     float *d = NULL;
     const size_t b = (size_t)n * sizeof(float);
-    if (ct__cuda_status(cudaMallocAsync((void **)&d, b, 0), "ct_attn_softmax")) return;
+    if (ct__scratch_alloc((void **)&d, b, NULL)) return;
     int rc = ct__cuda_status(cudaMemcpyAsync(d, x, b, cudaMemcpyHostToDevice, 0), "ct_attn_softmax");
     if (!rc) rc = ct__launch_softmax(d, n, NULL);
     if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(x, d, b, cudaMemcpyDeviceToHost, 0), "ct_attn_softmax");
-    cudaFreeAsync(d, 0);
+    ct__scratch_free(d, NULL);
     cudaStreamSynchronize(0);
 }
 

@@ -296,14 +296,24 @@ static int stage_reserve(ct_kv_paged_t *h, size_t n) {
     return CT_OK;
 }
 
+/* Inputs of ct_kv_paged_append_projected: the entries are W . x[t]. */
+typedef struct {
+    const void *x, *w;
+    const float *norm_w;
+    float eps;
+    uint32_t norm_dim, n_in;
+} proj_args_t;
+
 /* Uploads n_dest token slots plus the pending bt / len (index, value) pairs
- * in one pinned staging copy, then runs the scatters and the token writes. */
-static int flush(ct_kv_paged_t *h, const int32_t *dest, uint32_t n_dest, const void *entries, uint32_t src_dtype) {
+ * in one pinned staging copy, then runs the scatters and the token writes
+ * (entries copied, or projected when pj is set). */
+static int flush(ct_kv_paged_t *h, const int32_t *dest, uint32_t n_dest, const void *entries, uint32_t src_dtype,
+                 const proj_args_t *pj) {
     const size_t n_pairs = (size_t)h->n_bt_pairs + h->n_len_pairs;
     const size_t total = n_dest + 2 * n_pairs;
     if (h->host_only) {
         h->n_bt_pairs = h->n_len_pairs = 0;
-        return entries ? CT_ERR_UNSUPPORTED : CT_OK;
+        return entries || pj ? CT_ERR_UNSUPPORTED : CT_OK;
     }
     if (total == 0) return CT_OK;
     int rc = stage_reserve(h, total);
@@ -328,7 +338,10 @@ static int flush(ct_kv_paged_t *h, const int32_t *dest, uint32_t n_dest, const v
     if (h->n_bt_pairs) rc = ct__launch_scatter_i32(h->bt_dev, h->stage_dev + n_dest, h->n_bt_pairs, h->stream);
     if (!rc && h->n_len_pairs)
         rc = ct__launch_scatter_i32(h->len_dev, h->stage_dev + n_dest + 2 * (size_t)h->n_bt_pairs, h->n_len_pairs, h->stream);
-    if (!rc && entries && n_dest)
+    if (!rc && pj && n_dest)
+        rc = ct_kv_project_write_slots(pj->x, pj->w, pj->norm_w, pj->eps, pj->norm_dim, n_dest, pj->n_in,
+                                       h->cfg.entry_dim, h->pool, h->scales, h->cfg.dtype, h->stage_dev, h->stream);
+    else if (!rc && entries && n_dest)
         rc = ct_kv_paged_write_slots(h->pool, h->scales, h->cfg.dtype, entries, src_dtype, h->stage_dev, n_dest,
                                      h->cfg.entry_dim, h->stream);
     h->n_bt_pairs = h->n_len_pairs = 0;
@@ -346,9 +359,10 @@ static int push_len(ct_kv_paged_t *h, uint32_t s) {
 
 /* ---- append --------------------------------------------------------------- */
 
-int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts, uint32_t n,
-                       const void *entries, uint32_t src_dtype) {
+static int append_impl(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts, uint32_t n,
+                       const void *entries, uint32_t src_dtype, const proj_args_t *pj) {
     if (!h || (n && (!seq_ids || !counts))) return CT_ERR_ARG;
+    if (pj && h->host_only) return CT_ERR_UNSUPPORTED;
     if (entries && h->host_only) return CT_ERR_UNSUPPORTED;
     if (entries && src_dtype != CT_KV_BF16 && src_dtype != CT_KV_F32) return CT_ERR_ARG;
     const uint32_t P = h->cfg.page_tokens, MP = h->cfg.max_pages_per_seq, W = h->cfg.window_tokens;
@@ -429,14 +443,27 @@ int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t
     if (rc != CT_OK) {
         /* Host state already advanced: publish what changed so the device
          * mirrors stay consistent, but write no token data. */
-        flush(h, NULL, 0, NULL, 0);
+        flush(h, NULL, 0, NULL, 0, NULL);
         free(dest);
         return rc;
     }
     /* Without entries only the tables change: the slots need not travel. */
-    rc = flush(h, dest, entries ? (uint32_t)total : 0u, entries, src_dtype);
+    rc = flush(h, dest, entries || pj ? (uint32_t)total : 0u, entries, src_dtype, pj);
     free(dest);
     return rc;
+}
+
+int ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts, uint32_t n,
+                       const void *entries, uint32_t src_dtype) {
+    return append_impl(h, seq_ids, counts, n, entries, src_dtype, NULL);
+}
+
+int ct_kv_paged_append_projected(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts, uint32_t n,
+                                 const void *x, const void *w, uint32_t n_in, const float *norm_w, float eps,
+                                 uint32_t norm_dim) {
+    if (!x || !w) return CT_ERR_ARG;
+    const proj_args_t pj = {x, w, norm_w, eps, norm_dim, n_in};
+    return append_impl(h, seq_ids, counts, n, NULL, 0, &pj);
 }
 
 int ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t s) {
@@ -447,7 +474,7 @@ int ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t s) {
     h->len[s] = 0;
     if ((rc = push_len(h, s))) return rc;
     h->st.n_pages_free = h->heap_n;
-    return flush(h, NULL, 0, NULL, 0);
+    return flush(h, NULL, 0, NULL, 0, NULL);
 }
 
 int ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n) {
@@ -460,7 +487,7 @@ int ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n) {
         if ((rc = free_low_page(h, (uint32_t)c, 2))) return rc;
     }
     h->st.n_pages_free = h->heap_n;
-    rc = flush(h, NULL, 0, NULL, 0);
+    rc = flush(h, NULL, 0, NULL, 0, NULL);
     return rc ? rc : (int)done;
 }
 
@@ -503,7 +530,7 @@ int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_to
             if (ph >= 0) { h->refc[ph]--; set_bt(h, dst, lp, -1); }
         }
         h->st.n_pages_free = h->heap_n;
-        flush(h, NULL, 0, NULL, 0);
+        flush(h, NULL, 0, NULL, 0, NULL);
         return rc;
     }
     h->lo[dst] = 0;
@@ -522,7 +549,7 @@ int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_to
                                                  rem * sizeof(float), cudaMemcpyDeviceToDevice, h->stream), "fork copy");
         if (rc) return rc;
     }
-    return flush(h, NULL, 0, NULL, 0);
+    return flush(h, NULL, 0, NULL, 0, NULL);
 }
 
 uint32_t ct_kv_paged_page_refs(const ct_kv_paged_t *h, int32_t page) {

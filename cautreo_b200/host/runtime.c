@@ -7,6 +7,7 @@
 #include "../csrc/ct_internal.h"
 
 #include <cuda_runtime_api.h>
+#include <pthread.h>
 #include <stdatomic.h>
 #include <stdio.h>
 #include <string.h>
@@ -26,6 +27,52 @@ void ct__set_error(const char *msg) {
 }
 
 void ct__count_launches(uint32_t n) { atomic_fetch_add(&g_launches, (uint64_t)n); }
+
+/* One private pool per device, created on first use.  The default pool of a
+ * device releases freed memory at every synchronisation (threshold 0), so a
+ * per-step cudaMallocAsync of megabytes remaps memory each time; this pool
+ * keeps up to 1 GiB and leaves the process's default pool as it is. */
+#define CT_MAX_DEVICES 64
+static cudaMemPool_t g_pools[CT_MAX_DEVICES];
+static pthread_mutex_t g_pool_lock = PTHREAD_MUTEX_INITIALIZER;
+
+static int scratch_pool(int dev, cudaMemPool_t *out) {
+    if (dev < 0 || dev >= CT_MAX_DEVICES) return ct__cuda_status(cudaErrorInvalidDevice, "scratch pool");
+    pthread_mutex_lock(&g_pool_lock);
+    int rc = CT_OK;
+    if (!g_pools[dev]) {
+        struct cudaMemPoolProps props;
+        memset(&props, 0, sizeof props);
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = NULL;
+        rc = ct__cuda_status(cudaMemPoolCreate(&pool, &props), "scratch pool");
+        if (!rc) {
+            uint64_t keep = 1ull << 30;
+            rc = ct__cuda_status(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "scratch pool");
+            if (rc) cudaMemPoolDestroy(pool);
+            else g_pools[dev] = pool;
+        }
+    }
+    *out = g_pools[dev];
+    pthread_mutex_unlock(&g_pool_lock);
+    return rc;
+}
+
+int ct__scratch_alloc(void **p, size_t bytes, void *stream) {
+    int dev = 0;
+    int rc = ct__cuda_status(cudaGetDevice(&dev), "scratch");
+    cudaMemPool_t pool = NULL;
+    if (!rc) rc = scratch_pool(dev, &pool);
+    if (!rc) rc = ct__cuda_status(cudaMallocFromPoolAsync(p, bytes ? bytes : 16, pool, (cudaStream_t)stream),
+                                  "scratch alloc");
+    return rc;
+}
+
+void ct__scratch_free(void *p, void *stream) {
+    if (p) cudaFreeAsync(p, (cudaStream_t)stream);
+}
 
 const char *ct_hal_cuda_last_error(void) { return g_last_error; }
 uint64_t ct_hal_cuda_launch_count(void) { return atomic_load(&g_launches); }

@@ -171,6 +171,14 @@ int  ct_kv_paged_append(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_
                         uint32_t n, const void *entries, uint32_t src_dtype);
 
 /* Releases every page of a sequence and sets its length to 0. */
+/* The same allocation as ct_kv_paged_append, with each new token's entry
+ * produced on the device from its hidden state by ct_kv_project_write_slots
+ * (x: device bf16 [sum(counts)][n_in], ordered like `entries`; W: device
+ * bf16 [entry_dim][n_in]; norm_w NULL skips the norm).  No counterpart in
+ * the reference. */
+int  ct_kv_paged_append_projected(ct_kv_paged_t *h, const uint32_t *seq_ids, const uint32_t *counts,
+                                  uint32_t n, const void *x, const void *w, uint32_t n_in,
+                                  const float *norm_w, float eps, uint32_t norm_dim);
 int  ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t seq);
 /* Frees up to n pages by LRU order; returns the number freed (>= 0). */
 int  ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n);
@@ -234,6 +242,27 @@ const int32_t *ct_kv_paged_seq_lens_dev(const ct_kv_paged_t *h);
 int ct_kv_paged_write_slots(void *pool, float *scales, uint32_t pool_dtype, const void *entries,
                             uint32_t src_dtype, const int32_t *dest_slot, uint32_t n,
                             uint32_t dim, void *stream);
+
+/* Fused producer (no counterpart in the reference, which projects one token
+ * at a time with matvec_bf16 and copies the fp32 result into the cache,
+ * ds4_forward.c:248-272 and 1548-1570): for n new tokens,
+ *   entry[t] = W . x[t]          x: device bf16 [n][n_in], W: device bf16
+ *                                [dim][n_in]; fp32 accumulation on the tensor
+ *                                cores (the reference's fp32 hidden state is
+ *                                rounded to bf16 first);
+ *   optional RMS norm of entry[t][0:norm_dim] as rmsnorm_ip
+ *   (ds4_forward.c:206-211): x * (1/sqrt(mean(x^2) + eps)) * norm_w;
+ *   then written / quantised into dest_slot as ct_kv_paged_write_slots.
+ * n_in % 64 == 0, dim % 64 == 0, norm_dim % 4 == 0 (norm_w NULL skips the
+ * norm); x and W 16-byte aligned.  Uses stream-ordered scratch of
+ * (ksplit + 1) x n x dim fp32 (ksplit <= 16).  sm_100 only. */
+int ct_kv_project_write_slots(const void *x, const void *w, const float *norm_w, float eps,
+                              uint32_t norm_dim, uint32_t n, uint32_t n_in, uint32_t dim, void *pool,
+                              float *scales, uint32_t pool_dtype, const int32_t *dest_slot,
+                              void *stream);
+/* Error word of the projection kernel (0 = every bounded wait completed);
+ * clear != 0 resets it.  Synchronises with the device. */
+int ct_kv_project_error(int clear);
 
 /* Page-level gather: dst page i <- src page map[i] (device int32), whole
  * pages of page_bytes (codes) and page_tokens scales (if scales != NULL). */
