@@ -22,18 +22,20 @@
  *          peer's partial scores arrived in;
  *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
  *          from that slot, V read MN-major from the same page tile.
- * The softmax warps keep one tile in flight: they finish tile j-1 (once the
- * peer's half is in) and stage tile j for the peer in whichever order their
- * inputs arrive.  The scores in TMEM are free once staged, so the MMA warp
- * issues GEMM1 up to two tiles ahead of GEMM2.  The peer's partial scores
+ * Four staging warps copy each tile's partial scores to the exchange buffer
+ * as soon as GEMM1 has written them, so the exchange of tile j+1 runs while
+ * the softmax warps finish tile j; a score buffer is free once the staging
+ * and softmax warps have read it, and the MMA warp issues GEMM1 up to two
+ * tiles ahead of GEMM2.  The peer's partial scores
  * land in one of two receive slots; a slot is handed back to the peer by the
  * commit of the GEMM2 that read P from it, which arrives on the peer's
  * barrier directly.
  *
- * Roles per CTA (608 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+ * Roles per CTA (736 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
  * each), warps 3-18 finish scores, softmax and epilogue: four threads per
- * head row (TMEM lane), one per 16-token quarter of a tile.
+ * head row (TMEM lane), one per 16-token quarter of a tile; warps 19-22 stage
+ * the partial scores (one TMEM lane quadrant each).
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
  * 36 KB, an exchange out buffer and two in slots of 32 KB (partial scores,
@@ -62,10 +64,11 @@ constexpr int kParts = kSoftmaxWarps / 4;               /* threads per head row 
 constexpr int kTPT = 64 / kParts;                       /* tokens of a page per thread */
 constexpr int kOCols = 256 / kParts;                    /* O columns (value dims) per thread */
 constexpr int kFirstSoftmaxWarp = 3;
-constexpr int kThreads = 32 * (kFirstSoftmaxWarp + kSoftmaxWarps);   /* 608 */
+constexpr int kFirstStageWarp = kFirstSoftmaxWarp + kSoftmaxWarps;   /* 4 warps, one per TMEM lane quadrant */
+constexpr int kThreads = 32 * (kFirstStageWarp + 4);   /* 736 */
 constexpr int kConvWarps = 2;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
-constexpr int kFirstConvWarp = kFirstSoftmaxWarp + kSoftmaxWarps;
-constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 672 */
+constexpr int kFirstConvWarp = kFirstStageWarp + 4;
+constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 800 */
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
 constexpr uint32_t kCodeBytes = 4 * 4096 + 2048 + 256;  /* quantised page half: codes + 64 scales */
@@ -455,12 +458,20 @@ struct Row {
 /* Finishes global tile t (index jj in its chunk): adds the peer's partial
  * scores, updates the running maximum, rescales O if needed, writes P. */
 template <int KV>
-__device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r, uint32_t t, uint32_t jj, float *s,
+__device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r, uint32_t t, uint32_t jj,
                             int32_t ntok) {
     constexpr bool kQuant = KV != CT_KV_BF16;
     const float *tok_scale = reinterpret_cast<const float *>(c.smem + kOffScale + (t % kStages) * 256) + r.part * kTPT;
     float *red = reinterpret_cast<float *>(c.smem + kOffRed);
     const uint32_t slot = t & 1;
+    /* this CTA's partial scores of the thread's 16 tokens */
+    float s[kTPT];
+    if (!wait_warp(c, bar(c, B_S_FULL + slot), (t >> 1) & 1, false, 12)) return false;
+    tc_fence_after();
+    tmem_ld16(tmem + r.lane_base + kTmemS + slot * 64 + r.part * kTPT, s);
+    tmem_wait_ld();
+    tc_fence_before();
+    warp_arrive(bar(c, B_S_EMPTY + slot));            /* with the stagers': GEMM1 of tile t+2 may overwrite */
     if (!wait_warp(c, bar(c, B_X_FULL + slot), (t >> 1) & 1, true, 10)) return false;
     const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn + slot * kXBytes);
     #pragma unroll
@@ -563,24 +574,39 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     return true;
 }
 
-/* Stages global tile gt: this CTA's partial scores to registers and to the
- * exchange buffer the bulk copy sends. */
-__device__ bool stage_tile(const Ctx &c, uint32_t tmem, const Row &r, uint32_t gt, float *s) {
-    const uint32_t sb = gt & 1;
-    if (!wait_warp(c, bar(c, B_S_FULL + sb), (gt >> 1) & 1, false, 8)) return false;
-    tc_fence_after();
-    tmem_ld16(tmem + r.lane_base + kTmemS + sb * 64 + r.part * kTPT, s);
-    tmem_wait_ld();
-    tc_fence_before();
-    warp_arrive(bar(c, B_S_EMPTY + sb));            /* GEMM1 of tile gt+2 may overwrite them */
-    if (!wait_warp(c, bar(c, B_SO_EMPTY), (gt & 1) ^ 1, false, 9)) return false;
-    float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
-    #pragma unroll
-    for (int q4 = 0; q4 < kTPT / 4; q4++)
-        xout[xoff(r.row, r.part * (kTPT / 4) + q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
-    proxy_fence();
-    warp_arrive(bar(c, B_SO_FULL));
-    return true;
+/* ---- warps 19-22: staging -------------------------------------------------- */
+
+/* Copies each tile's partial scores (this warp's 32 head rows, all 64
+ * tokens) from TMEM to the exchange buffer as soon as GEMM1 has written them,
+ * independently of the softmax warps, so that the exchange of tile t+1 runs
+ * while tile t is being finished. */
+__device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t quad = warp & 3, row = quad * 32 + lane, lane_base = (quad * 32) << 16;
+    uint32_t t = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        const uint32_t n = count_tiles(ch, p);
+        for (uint32_t j = 0; j < n && ok; j++, t++) {
+            const uint32_t sb = t & 1;
+            if (!(ok = wait_warp(c, bar(c, B_S_FULL + sb), (t >> 1) & 1, false, 8))) break;
+            tc_fence_after();
+            float s[64];
+            tmem_ld32(tmem + lane_base + kTmemS + sb * 64, s);
+            tmem_ld32(tmem + lane_base + kTmemS + sb * 64 + 32, s + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            warp_arrive(bar(c, B_S_EMPTY + sb));
+            if (!(ok = wait_warp(c, bar(c, B_SO_EMPTY), (t & 1) ^ 1, false, 9))) break;
+            float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
+            #pragma unroll
+            for (int q4 = 0; q4 < 16; q4++)
+                xout[xoff(row, q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
+            proxy_fence();
+            warp_arrive(bar(c, B_SO_FULL));
+        }
+    }
 }
 
 template <int KV>
@@ -642,46 +668,12 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
         warp_arrive(bar(c, B_QT_FULL));
         r.m_used = -INFINITY;
         r.l = 0.0f;
-        float s_prev[kTPT];
-        int32_t prev_ntok = 0;
         uint32_t j = 0;
         do {
-            const uint32_t gt = g + j;
-            float s_cur[kTPT];
-            if (j == 0) {
-                if (!stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
-            } else {
-                /* finish tile gt-1 once the peer's half is in, or stage tile
-                 * gt first if its scores are ready sooner */
-                bool finish_first = false;
-                long long t0 = clock64();
-                for (;;) {
-                    bool xr = false, sr = false;
-                    if (lane == 0) {
-                        xr = mbar_test_cluster(bar(c, B_X_FULL + ((gt - 1) & 1)), ((gt - 1) >> 1) & 1);
-                        sr = !xr && mbar_test(bar(c, B_S_FULL + (gt & 1)), (gt >> 1) & 1) &&
-                             mbar_test(bar(c, B_SO_EMPTY), (gt & 1) ^ 1);
-                    }
-                    xr = __shfl_sync(0xFFFFFFFFu, xr, 0);
-                    sr = __shfl_sync(0xFFFFFFFFu, sr, 0);
-                    if (xr) { finish_first = true; break; }
-                    if (sr || *c.abort || clock64() - t0 > kWaitCycles) break;   /* the waits below bound the rest */
-                }
-                if (finish_first) {
-                    if (!finish_tile<KV>(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok) ||
-                        !stage_tile(c, tmem, r, gt, s_cur)) { ok = false; break; }
-                } else {
-                    if (!stage_tile(c, tmem, r, gt, s_cur) ||
-                        !finish_tile<KV>(c, p, tmem, r, gt - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
-                }
-            }
-            #pragma unroll
-            for (int i = 0; i < kTPT; i++) s_prev[i] = s_cur[i];
-            prev_ntok = ntok;
+            if (!finish_tile<KV>(c, p, tmem, r, g + j, j, ntok)) { ok = false; break; }
             j++;
         } while (it.next(pg, ntok));
         if (!ok) break;
-        if (!finish_tile<KV>(c, p, tmem, r, g + j - 1, j - 1, s_prev, prev_ntok)) { ok = false; break; }
         g += j;
         /* epilogue: the row sum over all parts, then O of this CTA's 256 value dims */
         float *rl = red + 2 * kParts * kH;
@@ -849,13 +841,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
             mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
             mbar_init(bar(c, B_X_FULL + i), 1);
             mbar_init(bar(c, B_X_EMPTY + i), 1);            /* the peer's GEMM2 commit */
-            mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps);
+            mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps + 4);   /* softmax and staging warps */
         }
         for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), kParts);     /* the warps of a quadrant */
         for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), kParts);
         mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
-        mbar_init(bar(c, B_SO_FULL), kSoftmaxWarps); mbar_init(bar(c, B_SO_EMPTY), 1);
+        mbar_init(bar(c, B_SO_FULL), 4); mbar_init(bar(c, B_SO_EMPTY), 1);
         mbar_init(bar(c, B_DRAIN), 1);
         for (int i = 0; i < kStages; i++) mbar_init(bar(c, B_CONV_FULL + i), kConvWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -879,8 +871,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
         mma_issuer<KV>(c, p, tmem, wbeg, wend);
     } else if (warp == 2) {
         exchanger(c, p, wbeg, wend);
-    } else if (warp < (uint32_t)kFirstConvWarp) {
+    } else if (warp < (uint32_t)kFirstStageWarp) {
         softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
+    } else if (warp < (uint32_t)kFirstConvWarp) {
+        stager(c, p, tmem, wbeg, wend);
     } else if (KV != CT_KV_BF16) {
         converter<KV>(c, p, wbeg, wend);
     }
