@@ -114,6 +114,10 @@ SIGNATURES = {
     "ct_kv_paged_append_projected": (I, [P, P, P, U32, P, P, U32, P, F, U32]),
     "ct_kv_project_write_slots": (I, [P, P, P, F, U32, U32, U32, U32, P, P, U32, P, P]),
     "ct_kv_project_error": (I, [I]),
+    "ct_ds4_cache_create": (P, [U32, U32, U32, I]),
+    "ct_ds4_cache_destroy": (V, [P]),
+    "ct_ds4_cache_len": (U32, [P, U32]),
+    "ct_ds4_attend": (I, [P, U32, U32, P, P, P]),
     "ct_kv_paged_evict_lru": (I, [P, U32]),
     "ct_kv_paged_compact": (I, [P]),
     "ct_kv_paged_gather": (I, [P, U32, U32, U32, P, U32]),

@@ -13,6 +13,14 @@
 extern "C" {
 #endif
 
+/* fp32 -> bf16 bits on the host, the same round-to-nearest-even integer rule
+ * as the device's ct_f32_to_bf16 (ds4_forward.c:60-66). */
+static inline uint16_t ct_f32_to_bf16_host(float f) {
+    union { float f; uint32_t u; } v;
+    v.f = f;
+    return (uint16_t)((v.u + 0x7FFFu + ((v.u >> 16) & 1u)) >> 16);
+}
+
 /* ---- bookkeeping shared by every launcher (host/runtime.c) ------------- */
 /* Records a CUDA error (code from cudaError_t) with a location; returns
  * CT_ERR_CUDA (or CT_OK when code == 0). */

@@ -159,6 +159,29 @@ int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, const int32_t 
                                      const float *scales, const int32_t *block_table,
                                      const int32_t *seq_lens, void *out, float *lse, void *stream);
 
+/* ======================================================================== */
+/* Part 3 -- the MLA-lite cache of ds4_forward.c on the device               */
+/* ======================================================================== */
+
+/* Replaces the per-layer latent cache and attention of ds4_forward.c
+ * (store at :1565-1570, attention at :1572-1627; the reference's cache is a
+ * calloc'ed fp32 [n_layers][ctx][kv_dim] array) for an engine that keeps its
+ * hidden state on the host.  One handle holds every layer's cache (fp32
+ * pages on the device).  Not thread-safe, like the reference engine. */
+typedef struct ct_ds4_cache ct_ds4_cache_t;
+ct_ds4_cache_t *ct_ds4_cache_create(uint32_t n_layers, uint32_t ctx, uint32_t kv_dim, int device);
+void            ct_ds4_cache_destroy(ct_ds4_cache_t *c);
+/* Positions stored for `layer`. */
+uint32_t        ct_ds4_cache_len(const ct_ds4_cache_t *c, uint32_t layer);
+/* One layer, one token: when pos < ctx stores kv_a (host, kv_dim fp32) at
+ * pos (pos <= the stored length: positions arrive in order, or overwrite);
+ * then out (host, kv_dim fp32) = sum_p softmax_p(q . k_p / sqrt(kv_dim)) k_p
+ * over the first min(pos + 1, ctx) positions, q = the first kv_dim values of
+ * q_b (host fp32).  q is rounded to bf16 and out comes from bf16 (the
+ * attention tolerance of the MLA decode). */
+int ct_ds4_attend(ct_ds4_cache_t *c, uint32_t layer, uint32_t pos, const float *kv_a, const float *q,
+                  float *out);
+
 #ifdef __cplusplus
 }
 #endif
