@@ -114,6 +114,9 @@ SIGNATURES = {
     "ct_kv_paged_append_projected": (I, [P, P, P, U32, P, P, U32, P, F, U32]),
     "ct_kv_project_write_slots": (I, [P, P, P, F, U32, U32, U32, U32, P, P, U32, P, P]),
     "ct_kv_project_error": (I, [I]),
+    "ct_kv_paged_set_tokens": (I, [P, U32, U32, P, U32]),
+    "ct_kv_paged_tokens": (U32, [P, U32, P, U32]),
+    "ct_kv_paged_match_prefix": (I, [P, P, U32, P, P]),
     "ct_ds4_cache_create": (P, [U32, U32, U32, I]),
     "ct_ds4_cache_destroy": (V, [P]),
     "ct_ds4_cache_len": (U32, [P, U32]),
@@ -370,6 +373,24 @@ class PagedKV:
         counts = np.ascontiguousarray(counts, np.uint32)
         check(lib().ct_kv_paged_append_projected(self.h, ptr(seq_ids), ptr(counts), len(seq_ids), ptr(x), ptr(w),
                                                  n_in, ptr(norm_w), eps, norm_dim), "ct_kv_paged_append_projected")
+
+    def set_tokens(self, seq, start, ids):
+        ids = np.ascontiguousarray(ids, np.int32)
+        check(lib().ct_kv_paged_set_tokens(self.h, seq, start, ptr(ids), len(ids)), "ct_kv_paged_set_tokens")
+
+    def tokens(self, seq):
+        n = int(lib().ct_kv_paged_tokens(self.h, seq, None, 0))
+        out = np.zeros(n, np.int32)
+        lib().ct_kv_paged_tokens(self.h, seq, ptr(out), n)
+        return out
+
+    def match_prefix(self, ids):
+        """(seq, length) of the longest cached prefix of ids."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        s, n = C.c_uint32(0), C.c_uint32(0)
+        check(lib().ct_kv_paged_match_prefix(self.h, ptr(ids), len(ids), C.byref(s), C.byref(n)),
+              "ct_kv_paged_match_prefix")
+        return int(s.value), int(n.value)
 
     def free_seq(self, seq):
         check(lib().ct_kv_paged_free_seq(self.h, seq), "ct_kv_paged_free_seq")

@@ -67,6 +67,10 @@ struct ct_kv_paged {
     uint32_t log_n, log_cap;
     uint8_t *claimed;           /* per-call slot bitmap for last-writer-wins */
     ct_kv_paged_stats_t st;
+    /* token ids of each sequence's cached positions [0, tok_n), for prefix
+     * reuse (allocated per sequence on first use) */
+    int32_t **tok;
+    uint32_t *tok_n, *tok_cap;
     /* pending device updates of this call */
     int32_t *pairs;             /* (index, value) for bt_dev then len_dev */
     uint32_t n_bt_pairs, n_len_pairs, pairs_cap;
@@ -187,6 +191,8 @@ void ct_kv_paged_destroy(ct_kv_paged_t *h) {
     }
     free(h->bt); free(h->len); free(h->lo); free(h->hi); free(h->last_access); free(h->rank); free(h->refc);
     free(h->heap); free(h->log); free(h->claimed); free(h->pairs);
+    if (h->tok) for (uint32_t s = 0; s < h->cfg.n_seqs; s++) free(h->tok[s]);
+    free(h->tok); free(h->tok_n); free(h->tok_cap);
     free(h);
 }
 
@@ -228,7 +234,11 @@ ct_kv_paged_t *ct_kv_paged_create(const ct_kv_paged_config_t *cfg) {
     h->refc = (uint32_t *)calloc(NP, sizeof(uint32_t));
     h->heap = (int32_t *)malloc((size_t)NP * sizeof(int32_t));
     h->claimed = (uint8_t *)calloc(((size_t)NP * P + 7) / 8, 1);
-    if (!h->bt || !h->len || !h->lo || !h->hi || !h->last_access || !h->rank || !h->refc || !h->heap || !h->claimed) {
+    h->tok = (int32_t **)calloc(S, sizeof(int32_t *));
+    h->tok_n = (uint32_t *)calloc(S, sizeof(uint32_t));
+    h->tok_cap = (uint32_t *)calloc(S, sizeof(uint32_t));
+    if (!h->bt || !h->len || !h->lo || !h->hi || !h->last_access || !h->rank || !h->refc || !h->heap || !h->claimed ||
+        !h->tok || !h->tok_n || !h->tok_cap) {
         ct_kv_paged_destroy(h);
         return NULL;
     }
@@ -472,6 +482,7 @@ int ct_kv_paged_free_seq(ct_kv_paged_t *h, uint32_t s) {
     while (h->lo[s] < h->hi[s]) if ((rc = free_low_page(h, s, 0))) return rc;
     h->lo[s] = h->hi[s] = 0;
     h->len[s] = 0;
+    h->tok_n[s] = 0;
     if ((rc = push_len(h, s))) return rc;
     h->st.n_pages_free = h->heap_n;
     return flush(h, NULL, 0, NULL, 0, NULL);
@@ -492,6 +503,17 @@ int ct_kv_paged_evict_lru(ct_kv_paged_t *h, uint32_t n) {
 }
 
 /* ---- prefix sharing ------------------------------------------------------ */
+
+static int tok_reserve(ct_kv_paged_t *h, uint32_t s, uint32_t n) {
+    if (n <= h->tok_cap[s]) return CT_OK;
+    uint32_t cap = h->tok_cap[s] ? h->tok_cap[s] : 256;
+    while (cap < n) cap *= 2;
+    int32_t *t = (int32_t *)realloc(h->tok[s], (size_t)cap * sizeof(int32_t));
+    if (!t) return CT_ERR_NOMEM;
+    h->tok[s] = t;
+    h->tok_cap[s] = cap;
+    return CT_OK;
+}
 
 int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_tokens) {
     if (!h || src >= h->cfg.n_seqs || dst >= h->cfg.n_seqs || src == dst) return CT_ERR_ARG;
@@ -536,6 +558,14 @@ int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_to
     h->lo[dst] = 0;
     h->hi[dst] = full + (rem ? 1 : 0);
     h->len[dst] = n_tokens;
+    {                                                 /* the prefix's token ids come along */
+        const uint32_t nt = h->tok_n[src] < n_tokens ? h->tok_n[src] : n_tokens;
+        h->tok_n[dst] = 0;
+        if (nt && tok_reserve(h, dst, nt) == CT_OK) {
+            memcpy(h->tok[dst], h->tok[src], (size_t)nt * sizeof(int32_t));
+            h->tok_n[dst] = nt;
+        }
+    }
     h->last_access[dst] = h->st.clock++;
     if ((rc = push_len(h, dst))) return rc;
     h->st.n_pages_free = h->heap_n;
@@ -555,6 +585,39 @@ int ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t n_to
 uint32_t ct_kv_paged_page_refs(const ct_kv_paged_t *h, int32_t page) {
     if (!h || page < 0 || (uint32_t)page >= h->cfg.n_pages) return 0;
     return h->refc[page];
+}
+
+int ct_kv_paged_set_tokens(ct_kv_paged_t *h, uint32_t seq, uint32_t start, const int32_t *ids, uint32_t n) {
+    if (!h || seq >= h->cfg.n_seqs || (n && !ids)) return CT_ERR_ARG;
+    if (start > h->tok_n[seq] || (uint64_t)start + n > h->len[seq]) return CT_ERR_ARG;
+    int rc = tok_reserve(h, seq, start + n);
+    if (rc) return rc;
+    memcpy(h->tok[seq] + start, ids, (size_t)n * sizeof(int32_t));
+    if (start + n > h->tok_n[seq]) h->tok_n[seq] = start + n;
+    return CT_OK;
+}
+
+uint32_t ct_kv_paged_tokens(const ct_kv_paged_t *h, uint32_t seq, int32_t *ids, uint32_t max) {
+    if (!h || seq >= h->cfg.n_seqs) return 0;
+    const uint32_t n = h->tok_n[seq] < max ? h->tok_n[seq] : max;
+    if (ids && n) memcpy(ids, h->tok[seq], (size_t)n * sizeof(int32_t));
+    return h->tok_n[seq];
+}
+
+int ct_kv_paged_match_prefix(const ct_kv_paged_t *h, const int32_t *ids, uint32_t n, uint32_t *seq_out,
+                             uint32_t *len_out) {
+    if (!h || (n && !ids) || !seq_out || !len_out) return CT_ERR_ARG;
+    uint32_t best = 0, best_s = 0;
+    for (uint32_t s = 0; s < h->cfg.n_seqs; s++) {
+        if (h->lo[s] != 0 || h->lo[s] == h->hi[s]) continue;      /* nothing mapped from position 0 */
+        const uint32_t lim = h->tok_n[s] < n ? h->tok_n[s] : n;
+        uint32_t m = 0;
+        while (m < lim && h->tok[s][m] == ids[m]) m++;
+        if (m > best) { best = m; best_s = s; }
+    }
+    *seq_out = best_s;
+    *len_out = best;
+    return CT_OK;
 }
 
 /* ---- compaction ----------------------------------------------------------- */
@@ -744,11 +807,12 @@ const int32_t *ct_kv_paged_seq_lens_dev(const ct_kv_paged_t *h) { return h ? h->
  * (u64); the block table (i32, n_seqs x max_pages); the free-order rank of
  * every page (u32); the free set (u32 count, i32 ids); the eviction log (u32
  * count, 5 x u32 each); the live pages (u32 count, then per page its id (i32),
- * page bytes, and page_tokens fp32 scales for int8 / e4m3 pools); last an
- * FNV-1a 64 of everything before it. */
+ * page bytes, and page_tokens fp32 scales for int8 / e4m3 pools); version 2
+ * then the token ids (per sequence a u32 count and that many i32); last an
+ * FNV-1a 64 of everything before it.  Version 1 files (no token ids) load. */
 
 #define CKPT_MAGIC "CTKVPAGE"
-#define CKPT_VERSION 1u
+#define CKPT_VERSION 2u
 
 typedef struct {
     FILE *f;
@@ -835,6 +899,10 @@ int ct_kv_paged_save(ct_kv_paged_t *h, const char *path) {
         free(buf);
     }
     free(seen);
+    for (uint32_t s = 0; s < S && !io.err; s++) {
+        ck_write(&io, &h->tok_n[s], 4);
+        ck_write(&io, h->tok[s], (size_t)h->tok_n[s] * 4);
+    }
     const uint64_t sum = io.fnv;
     if (!io.err && fwrite(&sum, 8, 1, f) != 1) io.err = 1;
     if (fclose(f) != 0) io.err = 1;
@@ -854,9 +922,9 @@ ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
     ck_read(&io, &ver, 4);
     ck_read(&io, &flags, 4);
     ck_read(&io, cfgw, sizeof cfgw);
-    if (io.err || memcmp(magic, CKPT_MAGIC, 8) != 0 || ver != CKPT_VERSION) {
+    if (io.err || memcmp(magic, CKPT_MAGIC, 8) != 0 || ver < 1 || ver > CKPT_VERSION) {
         fclose(f);
-        ct__set_error("ct_kv_paged_load: not a paged KV checkpoint of version 1");
+        ct__set_error("ct_kv_paged_load: not a paged KV checkpoint of version 1 or 2");
         return NULL;
     }
     ct_kv_paged_config_t cfg = {cfgw[0], cfgw[1], cfgw[2], cfgw[3], cfgw[4], cfgw[5], cfgw[6], device};
@@ -940,6 +1008,16 @@ ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
             }
         }
         free(buf);
+    }
+    for (uint32_t s = 0; s < S && !bad && ver >= 2; s++) {
+        uint32_t nt = 0;
+        ck_read(&io, &nt, 4);
+        bad = io.err || nt > h->len[s] || tok_reserve(h, s, nt) != CT_OK;
+        if (!bad) {
+            ck_read(&io, h->tok[s], (size_t)nt * 4);
+            h->tok_n[s] = nt;
+            bad = io.err;
+        }
     }
     if (!bad) {
         const uint64_t want = io.fnv;

@@ -204,6 +204,20 @@ int      ct_kv_paged_fork(ct_kv_paged_t *h, uint32_t src, uint32_t dst, uint32_t
 /* Number of sequences mapping a physical page (0 = free). */
 uint32_t ct_kv_paged_page_refs(const ct_kv_paged_t *h, int32_t page);
 
+/* Token ids of cached positions, for KV reuse across turns (the reference's
+ * engine persists only the ids, engine.c:634-651, and its ct_engine_kv_reuse
+ * is a no-op, engine.c:653-657).  set_tokens records ids for positions
+ * [start, start+n) of seq (start <= the ids recorded so far, start+n <= the
+ * sequence's length); a fork copies the prefix's ids, free_seq drops them,
+ * checkpoints carry them.  match_prefix finds the sequence whose recorded ids
+ * share the longest prefix with ids[0:n] among sequences still mapped from
+ * position 0 (ties: the lowest seq); *len_out = 0 when none matches.  Fork
+ * that many tokens to reuse them. */
+int      ct_kv_paged_set_tokens(ct_kv_paged_t *h, uint32_t seq, uint32_t start, const int32_t *ids, uint32_t n);
+uint32_t ct_kv_paged_tokens(const ct_kv_paged_t *h, uint32_t seq, int32_t *ids_out, uint32_t max);
+int      ct_kv_paged_match_prefix(const ct_kv_paged_t *h, const int32_t *ids, uint32_t n, uint32_t *seq_out,
+                                  uint32_t *len_out);
+
 /* Checkpoint of a paged cache (new; no reference counterpart -- it extends
  * the raw format of kv_cache.c:82-111, which ct_kv_save / ct_kv_load keep
  * unchanged): a versioned header ("CTKVPAGE", version 1), the configuration,

@@ -366,3 +366,58 @@ def test_block_pool_creation_rules():
                        (576, 64, 8)):                # no such dtype
         cfg = ct.PagedConfig(2, 4, 8, P, dim, 0, dt, -1)
         assert not L.ct_kv_paged_create(C.byref(cfg)), (dim, P, dt)
+
+
+def _fnv64(b):
+    h = 0xCBF29CE484222325
+    for x in b:
+        h ^= x
+        h = (h * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def test_token_ids_prefix_match_fork_and_checkpoint(tmp_path):
+    """KV reuse across turns: recorded token ids, longest cached prefix,
+    fork of that prefix (ids come along), free_seq drops them, and the
+    checkpoint carries them (version 2; version 1 files still load)."""
+    S, MP, NP, P = 4, 8, 32, 16
+    h = host_paged(S, MP, NP, P, 0)
+    h.append([0, 1], [40, 20])
+    ids0 = np.arange(100, 140, dtype=np.int32)
+    ids1 = np.concatenate([np.arange(100, 110), np.arange(900, 910)]).astype(np.int32)
+    h.set_tokens(0, 0, ids0[:30])
+    h.set_tokens(0, 30, ids0[30:])
+    h.set_tokens(1, 0, ids1)
+    assert np.array_equal(h.tokens(0), ids0) and np.array_equal(h.tokens(1), ids1)
+    L = ct.lib()
+    # gaps and positions past the cached length are refused
+    assert L.ct_kv_paged_set_tokens(h.h, 1, 25, ids1.ctypes.data, 1) == ct.CT_ERR_ARG
+    assert L.ct_kv_paged_set_tokens(h.h, 1, 15, ids1.ctypes.data, 10) == ct.CT_ERR_ARG
+    prompt = np.concatenate([np.arange(100, 125), [7, 7]]).astype(np.int32)
+    assert h.match_prefix(prompt) == (0, 25)
+    assert h.match_prefix(np.array([900], np.int32))[1] == 0
+    assert h.match_prefix(np.concatenate([np.arange(100, 110), [900]]).astype(np.int32)) == (1, 11)
+    s, n = h.match_prefix(prompt)
+    h.fork(s, 2, n)
+    assert np.array_equal(h.tokens(2), ids0[:25]) and h.seq_lens()[2] == 25
+    h.free_seq(1)
+    assert len(h.tokens(1)) == 0
+    path = tmp_path / "t.ckpt"
+    h.save(path)
+    g = ct.PagedKV.load(path, device=-1)
+    for s in range(S):
+        assert np.array_equal(g.tokens(s), h.tokens(s))
+    assert g.match_prefix(prompt) == (0, 25)
+    g.close()
+    # the same state written as version 1 (no token section): loads, without ids
+    raw = path.read_bytes()
+    body = bytearray(raw[:-8])
+    tok_bytes = sum(4 + 4 * len(h.tokens(s)) for s in range(S))
+    body = body[:-tok_bytes]
+    body[8:12] = (1).to_bytes(4, "little")
+    v1 = tmp_path / "v1.ckpt"
+    v1.write_bytes(bytes(body) + _fnv64(bytes(body)).to_bytes(8, "little"))
+    g1 = ct.PagedKV.load(v1, device=-1)
+    assert np.array_equal(g1.block_table(), h.block_table()) and len(g1.tokens(0)) == 0
+    g1.close()
+    h.close()
