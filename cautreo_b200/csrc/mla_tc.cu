@@ -31,11 +31,11 @@
  * commit of the GEMM2 that read P from it, which arrives on the peer's
  * barrier directly.
  *
- * Roles per CTA (736 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
+ * Roles per CTA (480 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
  * issues the MMAs, warp 2 issues the exchange copies (one elected thread
- * each), warps 3-18 finish scores, softmax and epilogue: four threads per
- * head row (TMEM lane), one per 16-token quarter of a tile; warps 19-22 stage
- * the partial scores (one TMEM lane quadrant each).
+ * each), warps 3-10 finish scores, softmax and epilogue: two threads per head
+ * row (TMEM lane), one per 32-token half of a tile; warps 11-14 stage the
+ * partial scores (one TMEM lane quadrant each).
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
  * 36 KB, an exchange out buffer and two in slots of 32 KB (partial scores,
@@ -59,16 +59,16 @@
 namespace {
 
 constexpr int kH = 128, kE = 576, kDv = 512, kP = 64;
-constexpr int kSoftmaxWarps = 16;
+constexpr int kSoftmaxWarps = 8;             /* two per TMEM lane quadrant: 20 warps keep 128 registers */
 constexpr int kParts = kSoftmaxWarps / 4;               /* threads per head row (one per TMEM lane quadrant warp) */
 constexpr int kTPT = 64 / kParts;                       /* tokens of a page per thread */
 constexpr int kOCols = 256 / kParts;                    /* O columns (value dims) per thread */
 constexpr int kFirstSoftmaxWarp = 3;
 constexpr int kFirstStageWarp = kFirstSoftmaxWarp + kSoftmaxWarps;   /* 4 warps, one per TMEM lane quadrant */
-constexpr int kThreads = 32 * (kFirstStageWarp + 4);   /* 736 */
+constexpr int kThreads = 32 * (kFirstStageWarp + 4);   /* 480 */
 constexpr int kConvWarps = 2;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
 constexpr int kFirstConvWarp = kFirstStageWarp + 4;
-constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 800 */
+constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 544 */
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
 constexpr uint32_t kCodeBytes = 4 * 4096 + 2048 + 256;  /* quantised page half: codes + 64 scales */
@@ -468,7 +468,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     float s[kTPT];
     if (!wait_warp(c, bar(c, B_S_FULL + slot), (t >> 1) & 1, false, 12)) return false;
     tc_fence_after();
-    tmem_ld16(tmem + r.lane_base + kTmemS + slot * 64 + r.part * kTPT, s);
+    if constexpr (kTPT == 16) tmem_ld16(tmem + r.lane_base + kTmemS + slot * 64 + r.part * kTPT, s);
+    else tmem_ld32(tmem + r.lane_base + kTmemS + slot * 64 + r.part * kTPT, s);
     tmem_wait_ld();
     tc_fence_before();
     warp_arrive(bar(c, B_S_EMPTY + slot));            /* with the stagers': GEMM1 of tile t+2 may overwrite */
@@ -553,9 +554,11 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     r.l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
     {
         uint8_t *pr = c.smem + kOffIn + slot * kXBytes + (r.row >> 3) * 2048 + (r.row & 7) * 128;
-        const uint32_t c0 = 2 * r.part, sw = r.row & 7;
-        *reinterpret_cast<uint4 *>(pr + ((c0 ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(pr + (((c0 + 1) ^ sw) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        const uint32_t c0 = (kTPT / 8) * r.part, sw = r.row & 7;      /* 16-byte chunks of 8 tokens */
+        #pragma unroll
+        for (int k = 0; k < kTPT / 8; k++)
+            *reinterpret_cast<uint4 *>(pr + (((c0 + k) ^ sw) << 4)) =
+                make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
     }
     /* a partial page: zero the V rows past its tokens (stale slots may hold
      * anything; the converter already wrote zeros there for quantised pages) */
@@ -574,7 +577,7 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     return true;
 }
 
-/* ---- warps 19-22: staging -------------------------------------------------- */
+/* ---- warps 11-14: staging -------------------------------------------------- */
 
 /* Copies each tile's partial scores (this warp's 32 head rows, all 64
  * tokens) from TMEM to the exchange buffer as soon as GEMM1 has written them,
@@ -724,7 +727,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     }
 }
 
-/* ---- warps 11-12 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
+/* ---- warps 15-16 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
 
 /* 16 codes (one 16-byte chunk) -> 16 bf16 values as two 16-byte chunks.
  * Every int8 and e4m3 value is exactly representable in bf16. */
