@@ -583,14 +583,35 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
  * tokens) from TMEM to the exchange buffer as soon as GEMM1 has written them,
  * independently of the softmax warps, so that the exchange of tile t+1 runs
  * while tile t is being finished. */
-__device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+__device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3, row = quad * 32 + lane, lane_base = (quad * 32) << 16;
-    uint32_t t = 0;
+    uint32_t t = 0, nq = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
         const uint32_t n = count_tiles(ch, p);
+        if (n == 0) continue;
+        /* this CTA's 256 latent dims of the chunk's Q (this thread: head
+         * `row`) into TMEM as soon as the previous chunk's GEMM1s are done,
+         * while the softmax warps may still be finishing that chunk */
+        if (!(ok = wait_warp(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 17))) break;
+        tc_fence_after();
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)ch.seq * kH + row) * kE + rank * 256);
+        #pragma unroll 1
+        for (int q64 = 0; q64 < 4; q64++) {
+            uint32_t u[32];
+            #pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint4 v = __ldg(src + q64 * 8 + k);
+                u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
+            }
+            tmem_st32(tmem + lane_base + kTmemQ + q64 * 32, u);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive(bar(c, B_QT_FULL));
+        nq++;
         for (uint32_t j = 0; j < n && ok; j++, t++) {
             const uint32_t sb = t & 1;
             if (!(ok = wait_warp(c, bar(c, B_S_FULL + sb), (t >> 1) & 1, false, 8))) break;
@@ -651,24 +672,6 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             }
             continue;
         }
-        /* the latent dims of this CTA's half of Q into TMEM, once the
-         * previous chunk's GEMM1s are done: this thread's 256 / kParts dims */
-        if (!wait_warp(c, bar(c, B_Q_EMPTY), (nchunk & 1) ^ 1, false, 17)) { ok = false; break; }
-        tc_fence_after();
-        #pragma unroll 1
-        for (int q64 = 0; q64 < kOCols / 64; q64++) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + oh * kE + rank * 256 + r.part * kOCols + q64 * 64);
-            uint32_t u[32];
-            #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint4 v = __ldg(src + k);
-                u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
-            }
-            tmem_st32(tmem + r.lane_base + kTmemQ + r.part * (kOCols / 2) + q64 * 32, u);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        warp_arrive(bar(c, B_QT_FULL));
         r.m_used = -INFINITY;
         r.l = 0.0f;
         uint32_t j = 0;
@@ -838,7 +841,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
             mbar_init(bar(c, B_KV_FULL + i), 1);
             mbar_init(bar(c, B_KV_EMPTY + i), 1);
         }
-        mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1); mbar_init(bar(c, B_QT_FULL), kSoftmaxWarps);
+        mbar_init(bar(c, B_Q_FULL), 1); mbar_init(bar(c, B_Q_EMPTY), 1); mbar_init(bar(c, B_QT_FULL), 4);
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(c, B_S_FULL + i), 1);
             mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
@@ -877,7 +880,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     } else if (warp < (uint32_t)kFirstStageWarp) {
         softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
     } else if (warp < (uint32_t)kFirstConvWarp) {
-        stager(c, p, tmem, wbeg, wend);
+        stager(c, p, tmem, wbeg, wend, rank);
     } else if (KV != CT_KV_BF16) {
         converter<KV>(c, p, wbeg, wend);
     }
