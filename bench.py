@@ -388,7 +388,8 @@ def run_ours(args, rank, world, local_rank):
                    "page_tokens": PAGE, "kv_dtype": "bf16", "softmax_scale": "1/sqrt(192)",
                    "kv_tokens_per_step": int(tok_total), "sharding": "LPT by length" if world > 1 else "none",
                    "parallelism": f"sequence-sharded x{world}",
-                   "l2": "inputs larger than L2 (per-GPU KV >= 1.9 GB vs 126 MB L2); no flush"},
+                   "l2": f"inputs larger than L2 (KV of rank 0: {tok_rank0 * BYTES_PER_TOKEN / 1e6:.0f} MB vs "
+                         "126 MB L2, read once per step); no flush"},
         "hbm_gbs": tok_total * args.steps * BYTES_PER_TOKEN / (ms_max * 1e-3) / 1e9,
         "gpu_launches": launches_total,
         "e2e": {"value": tok_total * args.steps / (e2e_max * 1e-3), "unit": "KV tokens/s",

@@ -69,10 +69,12 @@ void ct_attn_softmax(float *x, uint32_t n) {
 /* ---- Part 2: MLA plans ---------------------------------------------------- */
 
 /* ct_attn_mla_decode_step_host splits a step into up to this many sequence
- * groups, so that the copies of one group overlap the decode of another;
- * steps that move less than CT_STEP_PIPELINE_MIN_BYTES stay one group. */
+ * groups, so that the copies of one group overlap the decode of another.
+ * Each group costs one more decode launch (~20-30 us of pipeline fill and
+ * drain), worth it while the group's copies (~3 MB, ~60 us over PCIe) are
+ * longer; so a step gets one group per CT_STEP_GROUP_BYTES of copies. */
 #define CT_STEP_GROUPS 8
-#define CT_STEP_PIPELINE_MIN_BYTES (16u << 20)
+#define CT_STEP_GROUP_BYTES (3u << 20)
 
 struct ct_mla_plan {
     ct_mla_dims_t dims;
@@ -276,8 +278,10 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
  * get half the KV tokens of the others: with G groups the cuts fall at
  * (g + 1/2) / (G - 1) of the step's tokens. */
 static int step_host_pipeline(ct_mla_plan_t *p, size_t step_bytes) {
-    uint32_t G = CT_STEP_GROUPS;
-    if (step_bytes < CT_STEP_PIPELINE_MIN_BYTES || p->n_seq < 2 * G) G = 1;
+    uint32_t G = (uint32_t)(step_bytes / CT_STEP_GROUP_BYTES);
+    if (G > CT_STEP_GROUPS) G = CT_STEP_GROUPS;
+    if (G > p->n_seq / 2) G = p->n_seq / 2;             /* at least two sequences a group */
+    if (G < 1) G = 1;
     uint64_t total = 0;
     for (uint32_t s = 0; s < p->n_seq; s++) total += (uint64_t)p->lens_h[s];
     p->group_begin[0] = 0;
