@@ -66,9 +66,9 @@ constexpr int kOCols = 256 / kParts;                    /* O columns (value dims
 constexpr int kFirstSoftmaxWarp = 3;
 constexpr int kFirstStageWarp = kFirstSoftmaxWarp + kSoftmaxWarps;   /* 4 warps, one per TMEM lane quadrant */
 constexpr int kThreads = 32 * (kFirstStageWarp + 4);   /* 480 */
-constexpr int kConvWarps = 2;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
+constexpr int kConvWarps = 4;                           /* int8 / e4m3 pools: codes -> bf16 in shared memory */
 constexpr int kFirstConvWarp = kFirstStageWarp + 4;
-constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 544 */
+constexpr int kThreadsQ = kThreads + 32 * kConvWarps;   /* 608 */
 constexpr int kStages = 3;
 constexpr uint32_t kQBytes = 8192;                      /* the rope dims of the half: SW64 [128 x 32] */
 constexpr uint32_t kCodeBytes = 4 * 4096 + 2048 + 256;  /* quantised page half: codes + 64 scales */
@@ -730,7 +730,7 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
     }
 }
 
-/* ---- warps 15-16 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
+/* ---- warps 15-18 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
 
 /* 16 codes (one 16-byte chunk) -> 16 bf16 values as two 16-byte chunks.
  * Every int8 and e4m3 value is exactly representable in bf16. */
@@ -758,8 +758,8 @@ __device__ __forceinline__ void widen16(const uint4 &c, uint4 &lo, uint4 &hi) {
 
 /* The TMA put each box's codes in the upper half of its bf16 box (latent:
  * 64 rows x 64 codes at +4 KB of an 8 KB SW128 box; rope: 64 x 32 at +2 KB of
- * a 4 KB SW64 box).  A warp owns whole boxes (latent boxes w and w+2, the
- * rope box for warp 0): it loads all of a box's codes into registers, then
+ * a 4 KB SW64 box).  A warp owns whole boxes (latent box w, the rope box
+ * for the last warp): it loads all of a box's codes into registers, then
  * writes the bf16 rows over them, so no other warp's codes are overwritten.
  * Latent rows past the page's tokens become zeros (they are V rows of GEMM2). */
 template <int KV>
@@ -777,8 +777,8 @@ __device__ void converter(const Ctx &c, const Params &p, int wbeg, int wend) {
             if (!wait_warp(c, bar(c, B_KV_FULL + st), (g / kStages) & 1, false, 19)) { ok = false; break; }
             uint8_t *kv = c.smem + kOffKv + st * kKvBytes;
             #pragma unroll 1
-            for (int bi = 0; bi < 2; bi++) {
-                uint8_t *box = kv + (cw + 2 * bi) * 8192;
+            for (int bi = 0; bi < 4 / kConvWarps; bi++) {
+                uint8_t *box = kv + (cw + kConvWarps * bi) * 8192;
                 uint4 code[8];
                 #pragma unroll
                 for (int k = 0; k < 8; k++) code[k] = reinterpret_cast<const uint4 *>(box + 4096)[lane + 32 * k];
@@ -793,7 +793,7 @@ __device__ void converter(const Ctx &c, const Params &p, int wbeg, int wend) {
                 }
                 __syncwarp();
             }
-            if (cw == 0) {
+            if (cw == kConvWarps - 1) {
                 uint8_t *box = kv + 4 * 8192;
                 uint4 code[4];
                 #pragma unroll
