@@ -123,10 +123,15 @@ __global__ void __launch_bounds__(256) k_write_slots(void *pool, float *scales, 
     }
 }
 
+/* Tiles of the gathers below: 64 tokens per CTA, up to 9 (token, 16-value
+ * chunk) pairs per thread (entries of at most 576 values). */
+constexpr int kTileTok = 64, kTileK = 9;
+
 template <bool SrcBf16, int PoolDtype>
 int launch_write(void *pool, float *scales, const void *src, const int32_t *dest, uint32_t n,
                  uint32_t dim, cudaStream_t st) {
     const uint32_t chunks = dim / 16;
+
     const int blocks = (int)((n + kWarps - 1) / kWarps);
     if (chunks <= 32) k_write_slots<SrcBf16, PoolDtype, 1><<<blocks, 256, 0, st>>>(pool, scales, src, dest, n, dim);
     else if (chunks <= 64) k_write_slots<SrcBf16, PoolDtype, 2><<<blocks, 256, 0, st>>>(pool, scales, src, dest, n, dim);
@@ -430,6 +435,89 @@ void launch_gather_blocks(bool ob, const void *pool, const int32_t *bt, uint32_t
     else    k_gather_blocks<Type, false><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, out, tile);
 }
 
+/* K3t: the gathers from bf16 / int8 / e4m3 pools for entries of at most 576
+ * values, as CTA tiles of 64 output rows: (row, 16-value chunk) pairs spread
+ * evenly over the 256 threads (9 each for 576 values, where a warp per token
+ * leaves 28 of 32 lanes idle half the time), all of a thread's loads issued
+ * before any store.  Rows
+ * [64 x, 64 x + 64) of tokens [start, start+n) of one sequence (desc null),
+ * or of desc[y] = (seq, start, count, first output row). */
+template <int PoolDtype, bool OutBf16>
+__global__ void __launch_bounds__(256) k_gather_tiled(const void *pool, const float *scales, const int32_t *bt,
+                                                      uint32_t max_pages, uint32_t page_tokens, uint32_t dim,
+                                                      uint32_t start, uint32_t n, const int4 *desc, void *out) {
+    constexpr int kW = PoolDtype == CT_KV_BF16 ? 8 : 4;      /* words per 16-value chunk */
+    const int32_t *bt_row = bt;
+    size_t row0 = 0;
+    if (desc) {
+        const int4 d = desc[blockIdx.y];
+        bt_row = bt + (size_t)d.x * max_pages;
+        start = (uint32_t)d.y;
+        n = (uint32_t)d.z;
+        row0 = (uint32_t)d.w;
+    }
+    const uint32_t r0 = blockIdx.x * kTileTok;
+    if (r0 >= n) return;
+    const uint32_t C = dim / 16, cnt = min((uint32_t)kTileTok, n - r0), pairs = cnt * C;
+    uint32_t w[kTileK][kW];
+    float sc[kTileK];
+    #pragma unroll
+    for (int k = 0; k < kTileK; k++) {
+        const uint32_t q = threadIdx.x + 256u * k;
+        if (q >= pairs) continue;
+        const uint32_t t = q / C, c = q - t * C, pos = start + r0 + t;
+        const size_t slot = (size_t)bt_row[pos / page_tokens] * page_tokens + pos % page_tokens;
+        const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(pool) +
+                                                         (slot * dim + c * 16) * (PoolDtype == CT_KV_BF16 ? 2 : 1));
+        const uint4 a = __ldcs(p);
+        w[k][0] = a.x; w[k][1] = a.y; w[k][2] = a.z; w[k][3] = a.w;
+        if (kW == 8) {
+            const uint4 b = __ldcs(p + 1);
+            w[k][kW == 8 ? 4 : 0] = b.x; w[k][kW == 8 ? 5 : 1] = b.y; w[k][kW == 8 ? 6 : 2] = b.z; w[k][kW == 8 ? 7 : 3] = b.w;
+        }
+        sc[k] = PoolDtype == CT_KV_BF16 ? 1.0f : scales[slot];
+    }
+    #pragma unroll
+    for (int k = 0; k < kTileK; k++) {
+        const uint32_t q = threadIdx.x + 256u * k;
+        if (q >= pairs) continue;
+        const uint32_t t = q / C, c = q - t * C;
+        uint8_t *orow = static_cast<uint8_t *>(out) + (row0 + r0 + t) * dim * (OutBf16 ? 2 : 4);
+        if constexpr (PoolDtype == CT_KV_BF16 && OutBf16) {
+            uint4 *o = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(orow) + c * 16);
+            __stcs(o, make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]));
+            __stcs(o + 1, make_uint4(w[k][kW - 4], w[k][kW - 3], w[k][kW - 2], w[k][kW - 1]));
+        } else {
+            float v[16];
+            #pragma unroll
+            for (int i = 0; i < 16; i++) {
+                if (PoolDtype == CT_KV_BF16) {
+                    v[i] = __uint_as_float((i & 1) ? (w[k][(i >> 1) % kW] & 0xFFFF0000u) : (w[k][(i >> 1) % kW] << 16));
+                } else if (PoolDtype == CT_KV_INT8) {
+                    v[i] = (float)(int8_t)(uint8_t)(w[k][(i >> 2) % kW] >> (8 * (i & 3))) * sc[k];
+                } else if ((i & 1) == 0) {
+                    const float2 f = ct_e4m3x2_to_f32x2((uint16_t)(w[k][(i >> 2) % kW] >> (8 * (i & 3))));
+                    v[i] = f.x * sc[k];
+                    v[i + 1] = f.y * sc[k];
+                }
+            }
+            if (OutBf16) {
+                uint32_t o[8];
+                #pragma unroll
+                for (int i = 0; i < 8; i++)
+                    o[i] = (uint32_t)ct_f32_to_bf16(v[2 * i]) | ((uint32_t)ct_f32_to_bf16(v[2 * i + 1]) << 16);
+                uint4 *po = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(orow) + c * 16);
+                __stcs(po, make_uint4(o[0], o[1], o[2], o[3]));
+                __stcs(po + 1, make_uint4(o[4], o[5], o[6], o[7]));
+            } else {
+                float4 *po = reinterpret_cast<float4 *>(reinterpret_cast<float *>(orow) + c * 16);
+                #pragma unroll
+                for (int i = 0; i < 4; i++) __stcs(po + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+            }
+        }
+    }
+}
+
 /* K4 (pages): block b copies whole page map[b] -> b; 16-byte vectors with
  * four loads in flight per thread. */
 __global__ void __launch_bounds__(256) k_move_pages(const uint4 *src, const float *src_sc, uint4 *dst,
@@ -548,6 +636,12 @@ template <int D>
 int gather_dispatch(bool ob, uint32_t chunks, const void *pool, const float *scales, const int32_t *bt, uint32_t maxp,
                     uint32_t P, uint32_t dim, uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc,
                     void *out, cudaStream_t st) {
+    if (D != CT_KV_F32 && chunks * kTileTok <= 256u * kTileK) {
+        const dim3 grid((n + kTileTok - 1) / kTileTok, desc ? n_desc : 1);
+        if (ob) k_gather_tiled<D, true><<<grid, 256, 0, st>>>(pool, scales, bt, maxp, P, dim, start, n, desc, out);
+        else    k_gather_tiled<D, false><<<grid, 256, 0, st>>>(pool, scales, bt, maxp, P, dim, start, n, desc, out);
+        return CT_OK;
+    }
     const int mc = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : 0;
     if (!mc) return CT_ERR_UNSUPPORTED;
 #define CT_G(OB, MC) (desc ? gather_many<D, OB, MC>(pool, scales, bt, maxp, P, dim, desc, n_desc, n, out, st) \
