@@ -123,6 +123,104 @@ __global__ void __launch_bounds__(256) k_write_slots(void *pool, float *scales, 
     }
 }
 
+/* Eight lanes per token, four tokens per warp: lane g of a token's group owns
+ * the 8-value units g, g+8, ... (UPL per lane), so every lane does the same
+ * work for entries whose unit count is a multiple of 8 (576 values = 72
+ * units, 9 per lane), a load instruction reads 128 contiguous bytes of bf16
+ * source per token, and the absmax is a 3-step shuffle within the group.
+ * Same codes as k_write_slots: floor(x * id + 0.5) is one round-down
+ * conversion of the rounded sum (NaN -> 0, as the float -> int conversion of
+ * floorf gives), then the clamp. */
+template <bool SrcBf16, int PoolDtype, int UPL>
+__global__ void __launch_bounds__(256) k_write_grouped(void *pool, float *scales, const void *src,
+                                                       const int32_t *dest, uint32_t n, uint32_t dim) {
+    const uint32_t g = threadIdx.x & 7;
+    const uint32_t tok = blockIdx.x * 32 + (threadIdx.x >> 3);
+    const int32_t slot = tok < n ? dest[tok] : -1;
+    const uint32_t n_units = dim / 8;
+    constexpr int kW = SrcBf16 ? 4 : 8;                 /* source words per unit */
+    uint32_t w[UPL][kW];
+    if (slot >= 0) {
+        #pragma unroll
+        for (int i = 0; i < UPL; i++) {
+            const uint32_t u = i * 8 + g;
+            if (u >= n_units) continue;
+            const uint4 *p = SrcBf16 ? reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + (size_t)tok * dim + u * 8)
+                                     : reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + (size_t)tok * dim + u * 8);
+            #pragma unroll
+            for (int k = 0; k < kW / 4; k++) {
+                const uint4 v = __ldg(p + k);
+                w[i][4 * k] = v.x; w[i][4 * k + 1] = v.y; w[i][4 * k + 2] = v.z; w[i][4 * k + 3] = v.w;
+            }
+        }
+    }
+    auto val = [&](int i, int e) -> float {
+        if (SrcBf16) return __uint_as_float((e & 1) ? (w[i][e >> 1] & 0xFFFF0000u) : (w[i][e >> 1] << 16));
+        return __uint_as_float(w[i][e]);
+    };
+    const size_t base = (size_t)(slot < 0 ? 0 : slot) * dim;
+    if (PoolDtype == CT_KV_BF16 || PoolDtype == CT_KV_F32) {
+        if (slot < 0) return;
+        #pragma unroll
+        for (int i = 0; i < UPL; i++) {
+            const uint32_t u = i * 8 + g;
+            if (u >= n_units) continue;
+            if (PoolDtype == CT_KV_BF16) {
+                uint32_t o[4];
+                #pragma unroll
+                for (int k = 0; k < 4; k++)
+                    o[k] = SrcBf16 ? w[i][k]
+                                   : (uint32_t)ct_f32_to_bf16(val(i, 2 * k)) | ((uint32_t)ct_f32_to_bf16(val(i, 2 * k + 1)) << 16);
+                __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(pool) + base + u * 8), make_uint4(o[0], o[1], o[2], o[3]));
+            } else {
+                float4 *p = reinterpret_cast<float4 *>(static_cast<float *>(pool) + base + u * 8);
+                __stcs(p, make_float4(val(i, 0), val(i, 1), val(i, 2), val(i, 3)));
+                __stcs(p + 1, make_float4(val(i, 4), val(i, 5), val(i, 6), val(i, 7)));
+            }
+        }
+        return;
+    }
+    float amax = 0.0f;
+    if (slot >= 0) {
+        #pragma unroll
+        for (int i = 0; i < UPL; i++) {
+            if (i * 8 + g >= n_units) continue;
+            #pragma unroll
+            for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(val(i, e)));
+        }
+    }
+    #pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if (slot < 0) return;
+    const float d = __fdiv_rn(amax, PoolDtype == CT_KV_INT8 ? 127.0f : 448.0f);
+    const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    #pragma unroll
+    for (int i = 0; i < UPL; i++) {
+        const uint32_t u = i * 8 + g;
+        if (u >= n_units) continue;
+        uint32_t c[2];
+        if (PoolDtype == CT_KV_INT8) {
+            int q[8];
+            #pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int r = __float2int_rd(__fadd_rn(__fmul_rn(val(i, e), id), 0.5f));
+                q[e] = max(-127, min(127, r));
+            }
+            #pragma unroll
+            for (int k = 0; k < 2; k++)
+                c[k] = __byte_perm(__byte_perm(q[4 * k], q[4 * k + 1], 0x0040), __byte_perm(q[4 * k + 2], q[4 * k + 3], 0x0040),
+                                   0x5410);
+        } else {
+            #pragma unroll
+            for (int k = 0; k < 2; k++)
+                c[k] = (uint32_t)ct_e4m3x2_code(val(i, 4 * k), val(i, 4 * k + 1), id) |
+                       ((uint32_t)ct_e4m3x2_code(val(i, 4 * k + 2), val(i, 4 * k + 3), id) << 16);
+        }
+        __stcs(reinterpret_cast<uint2 *>(static_cast<uint8_t *>(pool) + base + u * 8), make_uint2(c[0], c[1]));
+    }
+    if (g == 0) scales[slot] = d;
+}
+
 /* Tiles of the gathers below: 64 tokens per CTA, up to 9 (token, 16-value
  * chunk) pairs per thread (entries of at most 576 values). */
 constexpr int kTileTok = 64, kTileK = 9;
@@ -130,8 +228,17 @@ constexpr int kTileTok = 64, kTileK = 9;
 template <bool SrcBf16, int PoolDtype>
 int launch_write(void *pool, float *scales, const void *src, const int32_t *dest, uint32_t n,
                  uint32_t dim, cudaStream_t st) {
-    const uint32_t chunks = dim / 16;
-
+    const uint32_t chunks = dim / 16, units = dim / 8;
+    if (units <= 96) {
+        const int gb = (int)((n + 31) / 32);
+        if (units <= 16) k_write_grouped<SrcBf16, PoolDtype, 2><<<gb, 256, 0, st>>>(pool, scales, src, dest, n, dim);
+        else if (units <= 32) k_write_grouped<SrcBf16, PoolDtype, 4><<<gb, 256, 0, st>>>(pool, scales, src, dest, n, dim);
+        else if (units <= 64) k_write_grouped<SrcBf16, PoolDtype, 8><<<gb, 256, 0, st>>>(pool, scales, src, dest, n, dim);
+        else if (units <= 72) k_write_grouped<SrcBf16, PoolDtype, 9><<<gb, 256, 0, st>>>(pool, scales, src, dest, n, dim);
+        else k_write_grouped<SrcBf16, PoolDtype, 12><<<gb, 256, 0, st>>>(pool, scales, src, dest, n, dim);
+        ct__count_launches(1);
+        return ct__cuda_status(cudaGetLastError(), "write_slots");
+    }
     const int blocks = (int)((n + kWarps - 1) / kWarps);
     if (chunks <= 32) k_write_slots<SrcBf16, PoolDtype, 1><<<blocks, 256, 0, st>>>(pool, scales, src, dest, n, dim);
     else if (chunks <= 64) k_write_slots<SrcBf16, PoolDtype, 2><<<blocks, 256, 0, st>>>(pool, scales, src, dest, n, dim);
