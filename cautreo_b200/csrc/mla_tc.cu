@@ -12,9 +12,10 @@
  *          N=64 tokens, K=288) -> TMEM, double-buffered.  The 256 latent dims
  *          of Q are an A operand in TMEM, the 32 rope dims in shared memory;
  *   the two partial S are exchanged: each CTA stages its partial in shared
- *          memory and a bulk copy moves it into the peer's receive buffer
- *          (the SM-to-SM network moves ~20 B/clk this way, twice what
- *          per-thread remote stores reach).  a + b is the same float in both
+ *          memory and bulk copies, one per TMEM lane quadrant (32 heads,
+ *          8 KB), move it into the peer's receive buffer (the SM-to-SM
+ *          network moves ~20 B/clk this way, twice what per-thread remote
+ *          stores reach).  a + b is the same float in both
  *          CTAs, so both run the identical softmax on identical scores;
  *   softmax in the log2 domain with a lazily updated row maximum (O is
  *          rescaled only when a row's maximum grows by more than 2^8);
@@ -22,9 +23,11 @@
  *          peer's partial scores arrived in;
  *   GEMM2  O_r += P . V[:, own 256 latent dims]  (M=128, N=256, K=64), A = P
  *          from that slot, V read MN-major from the same page tile.
- * Four staging warps copy each tile's partial scores to the exchange buffer
- * as soon as GEMM1 has written them, so the exchange of tile j+1 runs while
- * the softmax warps finish tile j; a score buffer is free once the staging
+ * Four staging warps (one per lane quadrant) copy each tile's partial scores
+ * to the exchange buffer as soon as GEMM1 has written them and issue their
+ * quadrant's copy themselves, so the exchange of tile j+1 runs while the
+ * softmax warps finish tile j, and the softmax warps of a quadrant start
+ * when that quadrant's 8 KB have landed; a score buffer is free once the staging
  * and softmax warps have read it, and the MMA warp issues GEMM1 up to two
  * tiles ahead of GEMM2.  The peer's partial scores
  * land in one of two receive slots; a slot is handed back to the peer by the
@@ -32,10 +35,10 @@
  * barrier directly.
  *
  * Roles per CTA (480 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
- * issues the MMAs, warp 2 issues the exchange copies (one elected thread
- * each), warps 3-10 finish scores, softmax and epilogue: two threads per head
- * row (TMEM lane), one per 32-token half of a tile; warps 11-14 stage the
- * partial scores (one TMEM lane quadrant each).
+ * issues the MMAs (one elected thread each), warp 2 is idle, warps 3-10
+ * finish scores, softmax and epilogue: two threads per head row (TMEM lane),
+ * one per 32-token half of a tile; warps 11-14 stage the partial scores and
+ * copy them to the peer (one TMEM lane quadrant each).
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
  * 36 KB, an exchange out buffer and two in slots of 32 KB (partial scores,
@@ -82,7 +85,7 @@ constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
 constexpr uint32_t kRedBytes = 3 * kParts * kH * 4;     /* row max [2 parities][parts], row sum [parts] */
 constexpr uint32_t kOffScale = kOffRed + kRedBytes;    /* per stage: 64 fp32 token scales (quantised pools) */
 constexpr uint32_t kOffBar = kOffScale + kStages * 256;
-constexpr uint32_t kNumBars = 40;
+constexpr uint32_t kNumBars = 44;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
 constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
@@ -100,10 +103,11 @@ constexpr long long kWaitCycles = 4000000000LL;         /* ~2 s at 2 GHz */
 /* barrier slots */
 enum : uint32_t {
     B_KV_FULL = 0, B_KV_EMPTY = 3, B_Q_FULL = 6, B_Q_EMPTY = 7, B_QT_FULL = 8, B_S_FULL = 9, B_P_FULL = 11,
-    B_O_READY = 13, B_O_FINAL = 14, B_O_FREE = 15, B_SO_FULL = 16, B_SO_EMPTY = 17, B_X_FULL = 18 /* [slot] */,
-    B_X_EMPTY = 20 /* [slot] */, B_DRAIN = 22, B_RED = 23 /* [parity][quad] */, B_RED_L = 31 /* [quad] */,
-    B_CONV_FULL = 35 /* [stage]: page converted to bf16 (quantised pools) */,
-    B_S_EMPTY = 38 /* [score buffer]: the softmax warps have read the scores */
+    B_O_READY = 13, B_O_FINAL = 14, B_O_FREE = 15, B_X_EMPTY = 16 /* [slot] */, B_DRAIN = 18,
+    B_RED = 19 /* [parity][quad] */, B_RED_L = 27 /* [quad] */,
+    B_CONV_FULL = 31 /* [stage]: page converted to bf16 (quantised pools) */,
+    B_S_EMPTY = 34 /* [score buffer]: the softmax warps have read the scores */,
+    B_X_FULL = 36 /* [slot][quad]: the peer's partial scores of a quadrant's rows have landed */
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -382,41 +386,6 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
     while (!mbar_try(bar(c, B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {}
 }
 
-/* ---- warp 2: score exchange (lane 0 issues) ------------------------------- */
-
-__device__ void exchanger(const Ctx &c, const Params &p, int wbeg, int wend) {
-    const bool leader = (threadIdx.x & 31) == 0;
-    const uint32_t in_peer = mapa(c.s + kOffIn, c.peer);
-    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);      /* slot b's barrier is 8 b bytes on */
-    uint32_t t = 0;
-    bool ok = true;
-    for (int ci = wbeg; ci < wend && ok; ci++) {
-        const ct_mla_chunk_t ch = load_chunk(p, ci);
-        const uint32_t n = count_tiles(ch, p);
-        for (uint32_t j = 0; j < n && ok; j++, t++) {
-            if (leader) {
-                /* this tile's partial scores are staged, and the peer has
-                 * consumed tile t-2 from receive slot t & 1 */
-                ok = wait_bar(c, bar(c, B_SO_FULL), t & 1, false, 14) &&
-                     wait_bar(c, bar(c, B_X_EMPTY + (t & 1)), ((t >> 1) & 1) ^ 1, true, 15);
-                if (ok) {
-                    bulk_copy_to_peer(in_peer + (t & 1) * kXBytes, c.s + kOffOut, kXBytes, xf_peer + (t & 1) * 8);
-                    bulk_wait_read();
-                    mbar_arrive(bar(c, B_SO_EMPTY));
-                }
-            }
-            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        }
-    }
-    if (leader) {
-        bulk_wait_all();                            /* every copy has landed in the peer */
-        /* the peer's GEMM2 of the last two tiles releases their slots here
-         * by a remote arrive; wait for it so none lands after exit */
-        for (uint32_t u = t >= 2 ? t - 2 : 0; u < t && ok; u++)
-            ok = wait_bar(c, bar(c, B_X_EMPTY + (u & 1)), (u >> 1) & 1, true, 20);
-    }
-}
-
 /* ---- warps 3-10: scores, softmax, epilogue -------------------------------- */
 
 /* A wait all 32 lanes of a softmax warp leave together (the tcgen05 loads
@@ -473,14 +442,15 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     tmem_wait_ld();
     tc_fence_before();
     warp_arrive(bar(c, B_S_EMPTY + slot));            /* with the stagers': GEMM1 of tile t+2 may overwrite */
-    if (!wait_warp(c, bar(c, B_X_FULL + slot), (t >> 1) & 1, true, 10)) return false;
+    if (!wait_warp(c, bar(c, B_X_FULL + slot * 4 + r.quad), (t >> 1) & 1, true, 10)) return false;
     const float4 *xin = reinterpret_cast<const float4 *>(c.smem + kOffIn + slot * kXBytes);
     #pragma unroll
     for (int q4 = 0; q4 < kTPT / 4; q4++) {
         const float4 w = xin[xoff(r.row, r.part * (kTPT / 4) + q4) >> 4];
         s[4 * q4] += w.x; s[4 * q4 + 1] += w.y; s[4 * q4 + 2] += w.z; s[4 * q4 + 3] += w.w;
     }
-    if (r.tid == 0) mbar_expect_tx(bar(c, B_X_FULL + slot), kXBytes);   /* arm for tile t + 2 */
+    /* arm this quadrant's barrier of the slot for tile t + 2 (8 KB) */
+    if (r.part == 0 && (r.tid & 31) == 0) mbar_expect_tx(bar(c, B_X_FULL + slot * 4 + r.quad), kXBytes / 4);
     /* quantised pages: the scores are code dot products; times the token's scale */
     if (kQuant) {
         #pragma unroll
@@ -581,13 +551,18 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
 
 /* Copies each tile's partial scores (this warp's 32 head rows, all 64
  * tokens) from TMEM to the exchange buffer as soon as GEMM1 has written them,
- * independently of the softmax warps, so that the exchange of tile t+1 runs
- * while tile t is being finished. */
+ * independently of the softmax warps, and sends those 8 KB into the peer's
+ * receive slot (one bulk copy, completing on the peer's barrier of this
+ * quadrant and slot), so that the exchange of tile t+1 runs while tile t is
+ * being finished.  The quadrant's out rows are rewritten only after its
+ * previous copy has read them (the issuing lane's bulk group). */
 __device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3, row = quad * 32 + lane, lane_base = (quad * 32) << 16;
     uint32_t t = 0, nq = 0;
     bool ok = true;
+    const uint32_t in_peer = mapa(c.s + kOffIn, c.peer);
+    const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
         const uint32_t n = count_tiles(ch, p);
@@ -622,14 +597,31 @@ __device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, i
             tmem_wait_ld();
             tc_fence_before();
             warp_arrive(bar(c, B_S_EMPTY + sb));
-            if (!(ok = wait_warp(c, bar(c, B_SO_EMPTY), (t & 1) ^ 1, false, 9))) break;
+            /* this quadrant's rows of the out buffer: its previous copy has read them */
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
             float4 *xout = reinterpret_cast<float4 *>(c.smem + kOffOut);
             #pragma unroll
             for (int q4 = 0; q4 < 16; q4++)
                 xout[xoff(row, q4) >> 4] = make_float4(s[4 * q4], s[4 * q4 + 1], s[4 * q4 + 2], s[4 * q4 + 3]);
             proxy_fence();
-            warp_arrive(bar(c, B_SO_FULL));
+            __syncwarp();
+            if (lane == 0) {
+                /* the peer has consumed tile t-2 from receive slot sb */
+                ok = wait_bar(c, bar(c, B_X_EMPTY + sb), ((t >> 1) & 1) ^ 1, true, 15);
+                if (ok) bulk_copy_to_peer(in_peer + sb * kXBytes + quad * 8192, c.s + kOffOut + quad * 8192, 8192,
+                                          xf_peer + (sb * 4 + quad) * 8);
+            }
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         }
+    }
+    if (lane == 0) {
+        bulk_wait_all();
+        /* the peer's GEMM2 of the last two tiles releases their slots here by
+         * a remote arrive; wait for it so none lands after exit */
+        if (quad == 0)
+            for (uint32_t u = t >= 2 ? t - 2 : 0; u < t && ok; u++)
+                ok = wait_bar(c, bar(c, B_X_EMPTY + (u & 1)), (u >> 1) & 1, true, 20);
     }
 }
 
@@ -845,20 +837,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(c, B_S_FULL + i), 1);
             mbar_init(bar(c, B_P_FULL + i), kSoftmaxWarps);
-            mbar_init(bar(c, B_X_FULL + i), 1);
             mbar_init(bar(c, B_X_EMPTY + i), 1);            /* the peer's GEMM2 commit */
             mbar_init(bar(c, B_S_EMPTY + i), kSoftmaxWarps + 4);   /* softmax and staging warps */
         }
         for (int i = 0; i < 8; i++) mbar_init(bar(c, B_RED + i), kParts);     /* the warps of a quadrant */
+        for (int i = 0; i < 8; i++) mbar_init(bar(c, B_X_FULL + i), 1);       /* 8 KB each */
         for (int i = 0; i < 4; i++) mbar_init(bar(c, B_RED_L + i), kParts);
         mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
-        mbar_init(bar(c, B_SO_FULL), 4); mbar_init(bar(c, B_SO_EMPTY), 1);
         mbar_init(bar(c, B_DRAIN), 1);
         for (int i = 0; i < kStages; i++) mbar_init(bar(c, B_CONV_FULL + i), kConvWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        mbar_expect_tx(bar(c, B_X_FULL + 0), kXBytes);   /* armed for the first two tiles */
-        mbar_expect_tx(bar(c, B_X_FULL + 1), kXBytes);
+        for (int i = 0; i < 8; i++) mbar_expect_tx(bar(c, B_X_FULL + i), kXBytes / 4);   /* the first two tiles */
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -876,7 +866,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     } else if (warp == 1) {
         mma_issuer<KV>(c, p, tmem, wbeg, wend);
     } else if (warp == 2) {
-        exchanger(c, p, wbeg, wend);
+        /* idle: the staging warps issue the exchange copies */
     } else if (warp < (uint32_t)kFirstStageWarp) {
         softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
     } else if (warp < (uint32_t)kFirstConvWarp) {
