@@ -235,6 +235,23 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
         it.init(ch, p);
         int32_t pg, ntok;
         if (!it.next(pg, ntok)) continue;               /* nothing readable in this chunk */
+        /* L2 prefetch three pages ahead of the page being loaded: a load waits
+         * for its stage until GEMM2 frees it, ~2 tiles later, and then reads
+         * from L2 instead of paying the HBM latency in that loop */
+        WarpTiles ah;
+        ah.init(ch, p);
+        int32_t apg, antok;
+        bool ah_ok = ah.next(apg, antok);
+        auto prefetch = [&](int32_t pgx) {
+            if ((threadIdx.x & 31) == 0) {
+                for (int b = 0; b < 4; b++) tma_prefetch_2d(kv_lat, rank * 256 + b * 64, pgx * kP);
+                tma_prefetch_2d(kv_rope, 512 + rank * 32, pgx * kP);
+            }
+        };
+        for (int a = 0; a < 2 && ah_ok; a++) {
+            ah_ok = ah.next(apg, antok);
+            if (ah_ok) prefetch(apg);
+        }
         /* the rope dims of this CTA's half of Q, once the previous chunk's
          * GEMM1s are done (the latent dims go to TMEM) */
         if (leader) {
@@ -271,6 +288,10 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
             }
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             if (!ok) break;
+            if (ah_ok) {
+                ah_ok = ah.next(apg, antok);
+                if (ah_ok) prefetch(apg);
+            }
             g++;
         } while (it.next(pg, ntok));
     }
@@ -290,14 +311,14 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
 
 /* ---- warp 1: MMA issuer (lane 0 issues) ---------------------------------- */
 
-__device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf) {
+__device__ void issue_gemm1(const Ctx &c, uint32_t tmem, uint32_t st, uint32_t sbuf, int i0, int i1) {
     const uint32_t q = c.s + kOffQ, kv = c.s + kOffKv + st * kKvBytes;
     const uint32_t d = tmem + kTmemS + sbuf * 64;
     /* the 256 latent dims of the half: A from TMEM */
-    #pragma unroll
-    for (int i = 0; i < 16; i++)
+    for (int i = i0; i < i1; i++)
         mma_ts(d, tmem + kTmemQ + i * 8, sdesc(kv + (i >> 2) * 8192 + (i & 3) * 32, 1, 64, kSw128), kIdescS,
                i > 0 ? 1u : 0u);
+    if (i1 < 16) return;
     /* rope dims: A from shared memory */
     #pragma unroll
     for (int k = 0; k < 2; k++)
@@ -336,8 +357,7 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
              * have read them, and runs at most two tiles ahead of GEMM2. */
             uint32_t n1 = 0, n2 = 0;
             long long t0 = clock64();
-            while (ok && n2 < n) {
-                bool did = false;
+            auto try_g2 = [&]() -> bool {
                 if (n2 < n1) {
                     const uint32_t gt = g + n2;
                     if (mbar_test(bar(c, B_P_FULL + (gt & 1)), (gt >> 1) & 1) &&
@@ -348,15 +368,24 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
                         mma_commit(bar(c, B_O_READY));
                         mma_commit_to(bar(c, B_X_EMPTY + (gt & 1)), (uint16_t)(1u << c.peer));   /* P read */
                         n2++;
-                        did = true;
+                        return true;
                     }
                 }
+                return false;
+            };
+            while (ok && n2 < n) {
+                bool did = try_g2();
                 if (n1 < n && n1 <= n2 + 2) {
                     const uint32_t gt = g + n1;
                     if (mbar_test(bar(c, kPageReady + gt % kStages), (gt / kStages) & 1) &&
                         mbar_test(bar(c, B_S_EMPTY + (gt & 1)), ((gt >> 1) & 1) ^ 1)) {
                         tc_fence_after();
-                        issue_gemm1(c, tmem, gt % kStages, gt & 1);
+                        /* in two halves: the issuing thread is held at the MMA
+                         * rate, so a P that becomes ready meanwhile gets its
+                         * GEMM2 between them instead of after all 18 MMAs */
+                        issue_gemm1(c, tmem, gt % kStages, gt & 1, 0, 8);
+                        try_g2();
+                        issue_gemm1(c, tmem, gt % kStages, gt & 1, 8, 16);
                         mma_commit(bar(c, B_S_FULL + (gt & 1)));
                         if (n1 == n - 1) mma_commit(bar(c, B_Q_EMPTY));
                         n1++;
