@@ -35,7 +35,8 @@
  * barrier directly.
  *
  * Roles per CTA (480 threads): warp 0 issues TMA loads, warp 1 owns TMEM and
- * issues the MMAs (one elected thread each), warp 2 is idle, warps 3-10
+ * issues the GEMM1s, warp 2 the GEMM2s (one elected thread each; on int8 /
+ * e4m3 pages warp 1 issues both and warp 2 is idle), warps 3-10
  * finish scores, softmax and epilogue: two threads per head row (TMEM lane),
  * one per 32-token half of a tile; warps 11-14 stage the partial scores and
  * copy them to the peer (one TMEM lane quadrant each).
@@ -85,7 +86,7 @@ constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
 constexpr uint32_t kRedBytes = 3 * kParts * kH * 4;     /* row max [2 parities][parts], row sum [parts] */
 constexpr uint32_t kOffScale = kOffRed + kRedBytes;    /* per stage: 64 fp32 token scales (quantised pools) */
 constexpr uint32_t kOffBar = kOffScale + kStages * 256;
-constexpr uint32_t kNumBars = 44;
+constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
 constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
@@ -107,7 +108,8 @@ enum : uint32_t {
     B_RED = 19 /* [parity][quad] */, B_RED_L = 27 /* [quad] */,
     B_CONV_FULL = 31 /* [stage]: page converted to bf16 (quantised pools) */,
     B_S_EMPTY = 34 /* [score buffer]: the softmax warps have read the scores */,
-    B_X_FULL = 36 /* [slot][quad]: the peer's partial scores of a quadrant's rows have landed */
+    B_X_FULL = 36 /* [slot][quad]: the peer's partial scores of a quadrant's rows have landed */,
+    B_DRAIN2 = 44 /* the GEMM2 thread's MMAs (bf16 pages) */
 };
 
 /* instruction descriptors: f32 accumulate, bf16 A and B, M = 128 */
@@ -413,6 +415,81 @@ __device__ void mma_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbe
     mma_commit(bar(c, B_DRAIN));
     long long t0 = clock64();
     while (!mbar_try(bar(c, B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {}
+}
+
+/* GEMM1 of every tile, in order, as soon as its page is in shared memory
+ * and its score buffer has been read (warp 1, one elected thread). */
+template <int KV>
+__device__ void gemm1_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    constexpr uint32_t kPageReady = KV == CT_KV_BF16 ? B_KV_FULL : B_CONV_FULL;
+    const bool leader = (threadIdx.x & 31) == 0;
+    uint32_t g = 0, nchunk = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        const uint32_t n = count_tiles(ch, p);
+        if (n == 0) continue;
+        if (leader) {
+            /* both parts of this chunk's Q: the TMA half and the TMEM half */
+            ok = wait_bar(c, bar(c, B_Q_FULL), nchunk & 1, false, 3) &&
+                 wait_bar(c, bar(c, B_QT_FULL), nchunk & 1, false, 3);
+            for (uint32_t j = 0; j < n && ok; j++) {
+                const uint32_t gt = g + j;
+                ok = wait_bar(c, bar(c, kPageReady + gt % kStages), (gt / kStages) & 1, false, 5) &&
+                     wait_bar(c, bar(c, B_S_EMPTY + (gt & 1)), ((gt >> 1) & 1) ^ 1, false, 5);
+                if (!ok) break;
+                tc_fence_after();
+                issue_gemm1(c, tmem, gt % kStages, gt & 1, 0, 16);
+                mma_commit(bar(c, B_S_FULL + (gt & 1)));
+                if (j == n - 1) mma_commit(bar(c, B_Q_EMPTY));
+            }
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        g += n;
+        nchunk++;
+    }
+    if (!leader) return;
+    /* Drain this thread's MMAs before TMEM is released. */
+    mma_commit(bar(c, B_DRAIN));
+    long long t0 = clock64();
+    while (!mbar_try(bar(c, B_DRAIN), 0) && clock64() - t0 < kWaitCycles) {}
+}
+
+/* GEMM2 of every tile, in order, as soon as its P is written (warp 2, one
+ * elected thread): a thread of its own, so that a ready P never waits
+ * behind the issue of a GEMM1, which the tensor pipe holds back at its
+ * execution rate.  The first GEMM2 of a chunk also waits until the
+ * epilogue has read the previous chunk's O. */
+__device__ void gemm2_issuer(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend) {
+    const bool leader = (threadIdx.x & 31) == 0;
+    uint32_t g = 0, nchunk = 0;
+    bool ok = true;
+    for (int ci = wbeg; ci < wend && ok; ci++) {
+        const ct_mla_chunk_t ch = load_chunk(p, ci);
+        const uint32_t n = count_tiles(ch, p);
+        if (n == 0) continue;
+        if (leader) {
+            for (uint32_t j = 0; j < n && ok; j++) {
+                const uint32_t gt = g + j;
+                ok = wait_bar(c, bar(c, B_P_FULL + (gt & 1)), (gt >> 1) & 1, false, 7) &&
+                     (j > 0 || wait_bar(c, bar(c, B_O_FREE), (nchunk & 1) ^ 1, false, 7));
+                if (!ok) break;
+                tc_fence_after();
+                issue_gemm2(c, tmem, gt % kStages, gt & 1, j == 0);
+                mma_commit(bar(c, B_KV_EMPTY + gt % kStages));
+                mma_commit(bar(c, B_O_READY));
+                mma_commit_to(bar(c, B_X_EMPTY + (gt & 1)), (uint16_t)(1u << c.peer));   /* P read */
+            }
+            if (ok) mma_commit(bar(c, B_O_FINAL));
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        g += n;
+        nchunk++;
+    }
+    if (!leader) return;
+    mma_commit(bar(c, B_DRAIN2));
+    long long t0 = clock64();
+    while (!mbar_try(bar(c, B_DRAIN2), 0) && clock64() - t0 < kWaitCycles) {}
 }
 
 /* ---- warps 3-10: scores, softmax, epilogue -------------------------------- */
@@ -875,6 +952,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
         mbar_init(bar(c, B_O_READY), 1); mbar_init(bar(c, B_O_FINAL), 1);
         mbar_init(bar(c, B_O_FREE), kSoftmaxWarps);
         mbar_init(bar(c, B_DRAIN), 1);
+        mbar_init(bar(c, B_DRAIN2), 1);
         for (int i = 0; i < kStages; i++) mbar_init(bar(c, B_CONV_FULL + i), kConvWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int i = 0; i < 8; i++) mbar_expect_tx(bar(c, B_X_FULL + i), kXBytes / 4);   /* the first two tiles */
@@ -893,9 +971,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     if (warp == 0) {
         producer<KV>(c, p, &kv_lat, &kv_rope, &q_rope, wbeg, wend, rank);
     } else if (warp == 1) {
-        mma_issuer<KV>(c, p, tmem, wbeg, wend);
+        /* bf16 pages: one thread per GEMM; the int8 / e4m3 kernels, whose
+         * converter warps share the SM, measured faster with one thread
+         * issuing both (GEMM2 first when ready) */
+        if constexpr (KV == CT_KV_BF16) gemm1_issuer<KV>(c, p, tmem, wbeg, wend);
+        else mma_issuer<KV>(c, p, tmem, wbeg, wend);
     } else if (warp == 2) {
-        /* idle: the staging warps issue the exchange copies */
+        if constexpr (KV == CT_KV_BF16) gemm2_issuer(c, p, tmem, wbeg, wend);
     } else if (warp < (uint32_t)kFirstStageWarp) {
         softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
     } else if (warp < (uint32_t)kFirstConvWarp) {
