@@ -80,12 +80,6 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, ui
                  ::"r"(dst), "r"(src), "r"(bytes), "r"(bar) : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-/* The same without closing the bulk group: several copies, then bulk_commit(). */
-__device__ __forceinline__ void bulk_copy_to_peer_open(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(dst), "r"(src), "r"(bytes), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 /* Untiled bulk copy global -> this CTA's shared memory (16-B aligned, size
  * a multiple of 16), completing on a local barrier. */
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -93,10 +87,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-/* Every bulk group of this thread but the most recent one has read its source. */
-__device__ __forceinline__ void bulk_wait_read_all_but_last() {
-    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-}
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
