@@ -603,8 +603,9 @@ def _plain_reference(oracle, q, k, v, L_, Hh, D, steps, tokens):
 
 def run_quant(args):
     """64 sequences x 8192 tokens of MLA entries (N(0,1), 1 % x20 outliers) in
-    int8 and fp8-e4m3 pools with one fp32 scale per token: quantise-on-append,
-    dequantise-on-gather and decode over the quantised pages."""
+    int8 and fp8-e4m3 pools with one fp32 scale per token (and, for
+    comparison, a bf16 pool): quantise-on-append, dequantise-on-gather and
+    decode over the quantised pages; then the block-codec pools."""
     import torch
     import cautreo_b200 as ct
     L = ct.lib()
@@ -624,7 +625,9 @@ def run_quant(args):
     gat = torch.empty(n_tok * E, dtype=torch.int16, device="cuda")
     hbm, hbm_kind = measured_hbm()
     res = {}
-    for name, dt in (("int8", ct.CT_KV_INT8), ("e4m3", ct.CT_KV_E4M3)):
+    tensor_peak, _ = measured_tensor()
+    dec_flops = n_tok * H * 2 * (E + DV)                   # q.k over 576 values, p.v over 512, per head
+    for name, dt in (("bf16", ct.CT_KV_BF16), ("int8", ct.CT_KV_INT8), ("e4m3", ct.CT_KV_E4M3)):
         kv = ct.PagedKV(B, pages_per, n_pages, PAGE, E, 0, dt, 0, sp)
         kv.set_free_order(perm)
         kv.append(list(range(B)), [T] * B, None)             # every slot reserved, pages permuted
@@ -663,11 +666,14 @@ def run_quant(args):
             e1.record(stream)
             torch.cuda.synchronize()
             r[what] = e0.elapsed_time(e1) / reps
-        code_bytes = n_tok * (E + 4)
+        code_bytes = n_tok * (E * 2 if dt == ct.CT_KV_BF16 else E + 4)
+        dec_bytes = code_bytes + B * H * (E + DV) * 2          # pages + bf16 q + bf16 out
         res[name] = {
             "append_ms": r["append"], "append_gbs": (n_tok * E * 2 + code_bytes) / (r["append"] * 1e-3) / 1e9,
             "gather_ms": r["gather"], "gather_gbs": (code_bytes + n_tok * E * 2) / (r["gather"] * 1e-3) / 1e9,
             "decode_ms": r["decode"], "decode_tokens_s": n_tok / (r["decode"] * 1e-3),
+            "decode_hbm_frac": dec_bytes / (r["decode"] * 1e-3) / 1e9 / hbm,
+            "decode_tensor_frac": dec_flops / (r["decode"] * 1e-3) / 1e12 / tensor_peak,
             "decode_kernel": "tensor cores" if plan.tensor_cores else "CUDA cores",
         }
         res[name]["append_frac"] = res[name]["append_gbs"] / hbm
