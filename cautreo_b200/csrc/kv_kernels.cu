@@ -24,6 +24,14 @@ namespace {
 
 constexpr int kWarps = 8;          /* tokens per 256-thread block */
 
+/* Two floats -> packed bf16 pair (lo in the low half), round to nearest even
+ * (one cvt; equal to ct_f32_to_bf16 for every non-NaN input). */
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 /* 16 consecutive source values of a token as raw words: bf16 -> 8 words
  * (two per word, low half first), fp32 -> 16 words. */
 template <bool SrcBf16>
@@ -354,23 +362,96 @@ __host__ __device__ inline uint32_t block_tile(uint32_t eb) {
     return t > 64 ? 64 : (t < 1 ? 1 : t);
 }
 
-/* One block between shared memory (2-byte aligned) and registers. */
+/* Blocks in shared memory are 2-byte aligned (34 / 18 / 10 / 6 bytes each):
+ * they are read and written as 16-bit halves, the codes as whole 32-bit
+ * words in registers. */
+template <int Type> struct BlockWords {
+    static constexpr int kCodeWords = (CtBlock<Type>::kBytes - 2) / 4;     /* 8 / 4 / 2 / 1 */
+};
+
+/* The 32 values of one block, exactly ct_block_decode's (code x d in fp32,
+ * exact: at most 8 + 11 significant bits).  A code becomes a float by adding
+ * it to the bits of 1.5 * 2^23 and subtracting that again, which keeps the
+ * work on the integer and fma pipes. */
 template <int Type>
-__device__ __forceinline__ void block_load(const uint8_t *s, uint8_t *b) {
-    constexpr int kB = CtBlock<Type>::kBytes;
+__device__ __forceinline__ void block_decode_smem(const uint8_t *blk, float *x) {
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
+    const float d = ct_ref_fp16_to_f32(h[0]);
+    constexpr int kW = BlockWords<Type>::kCodeWords;
+    uint32_t w[kW];
     #pragma unroll
-    for (int i = 0; i < kB / 2; i++) {
-        const uint16_t h = reinterpret_cast<const uint16_t *>(s)[i];
-        b[2 * i] = (uint8_t)h;
-        b[2 * i + 1] = (uint8_t)(h >> 8);
+    for (int j = 0; j < kW; j++) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
+    #pragma unroll
+    for (int i = 0; i < 32; i++) {
+        float f;
+        if (Type == CT_QUANT_Q8_0) {
+            const int v = (int)(int8_t)(uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+            f = __int_as_float(0x4B400000 + v) - 12582912.0f;
+        } else if (Type == CT_QUANT_Q4_0) {
+            const uint32_t u = ((w[i >> 3] >> (4 * (i & 7))) & 0xFu) ^ 8u;     /* two's complement nibble + 8 */
+            f = __uint_as_float(0x4B400000u | u) - 12582920.0f;
+        } else if (Type == CT_QUANT_Q2_0) {
+            const uint32_t u = (w[i >> 4] >> (2 * (i & 15))) & 3u;           /* code + 1 */
+            f = __uint_as_float(0x4B400000u | u) - 12582913.0f;
+        } else {
+            x[i] = (w[0] >> i) & 1u ? d : -d;
+            continue;
+        }
+        x[i] = __fmul_rn(f, d);
     }
 }
+
+/* One block's fp16 scale and codes, ct_block_encode's, into shared memory. */
 template <int Type>
-__device__ __forceinline__ void block_store(uint8_t *s, const uint8_t *b) {
-    constexpr int kB = CtBlock<Type>::kBytes;
+__device__ __forceinline__ void block_encode_smem(const float *x, uint8_t *blk) {
+    uint16_t *h = reinterpret_cast<uint16_t *>(blk);
+    float amax = 0.0f;
     #pragma unroll
-    for (int i = 0; i < kB / 2; i++)
-        reinterpret_cast<uint16_t *>(s)[i] = (uint16_t)(b[2 * i] | (b[2 * i + 1] << 8));
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(x[i]));
+    constexpr int kW = BlockWords<Type>::kCodeWords;
+    uint32_t w[kW];
+    if (Type == CT_QUANT_Q1_0) {
+        h[0] = ct_ref_f32_to_fp16(amax);
+        uint32_t bits = 0;
+        #pragma unroll
+        for (int i = 0; i < 32; i++) bits |= (x[i] >= 0 ? 1u : 0u) << i;
+        w[0] = bits;
+    } else {
+        constexpr int qm = Type == CT_QUANT_Q8_0 ? 127 : Type == CT_QUANT_Q4_0 ? 7 : 1;
+        const float d = __fdiv_rn(amax, (float)qm);
+        h[0] = ct_ref_f32_to_fp16(d);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int q[32];
+        #pragma unroll
+        for (int i = 0; i < 32; i++) q[i] = max(-qm, min(qm, __float2int_rd(__fadd_rn(__fmul_rn(x[i], id), 0.5f))));
+        if (Type == CT_QUANT_Q8_0) {
+            #pragma unroll
+            for (int j = 0; j < kW; j++)
+                w[j] = __byte_perm(__byte_perm(q[4 * j], q[4 * j + 1], 0x0040), __byte_perm(q[4 * j + 2], q[4 * j + 3], 0x0040),
+                                   0x5410);
+        } else if (Type == CT_QUANT_Q4_0) {
+            #pragma unroll
+            for (int j = 0; j < kW; j++) {
+                uint32_t v = 0;
+                #pragma unroll
+                for (int k = 0; k < 8; k++) v |= ((uint32_t)q[8 * j + k] & 0xFu) << (4 * k);
+                w[j] = v;
+            }
+        } else {
+            #pragma unroll
+            for (int j = 0; j < kW; j++) {
+                uint32_t v = 0;
+                #pragma unroll
+                for (int k = 0; k < 16; k++) v |= ((uint32_t)(q[16 * j + k] + 1) & 3u) << (2 * k);
+                w[j] = v;
+            }
+        }
+    }
+    #pragma unroll
+    for (int j = 0; j < kW; j++) {
+        h[1 + 2 * j] = (uint16_t)w[j];
+        h[2 + 2 * j] = (uint16_t)(w[j] >> 16);
+    }
 }
 
 /* The 32 source values of block b of token tok, as raw 16-byte vectors. */
@@ -416,9 +497,7 @@ __global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void 
         in.load(src, t0 + t, dim, b);
         float x[32];
         in.values(x);
-        uint8_t blk[kB];
-        ct_block_encode<Type>(x, blk);
-        block_store<Type>(stage + t * eb + b * kB, blk);
+        block_encode_smem<Type>(x, stage + t * eb + b * kB);
     }
     __syncthreads();
     if ((eb & 3) == 0) {
@@ -488,10 +567,8 @@ __global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, cons
     row0 += lo - start;
     for (uint32_t p = threadIdx.x; p < cnt * nb; p += 256) {
         const uint32_t t = p / nb, b = p - t * nb;
-        uint8_t blk[kB];
-        block_load<Type>(stage + off + t * eb + b * kB, blk);
         float x[32];
-        ct_block_decode<Type>(blk, x);
+        block_decode_smem<Type>(stage + off + t * eb + b * kB, x);
         uint8_t *orow = static_cast<uint8_t *>(out) + (row0 + t) * dim * (OutBf16 ? 2 : 4);
         if (OutBf16) {
             uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(orow) + b * 32);
@@ -499,8 +576,7 @@ __global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, cons
             for (int i = 0; i < 4; i++) {
                 uint32_t o[4];
                 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    o[j] = (uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j]) | ((uint32_t)ct_f32_to_bf16(x[8 * i + 2 * j + 1]) << 16);
+                for (int j = 0; j < 4; j++) o[j] = bf16x2_rn(x[8 * i + 2 * j], x[8 * i + 2 * j + 1]);
                 __stcs(q + i, make_uint4(o[0], o[1], o[2], o[3]));
             }
         } else {
