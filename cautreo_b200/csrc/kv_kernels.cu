@@ -1,7 +1,10 @@
 /*
  * kv_kernels.cu -- HBM-bound kernels of the paged KV cache:
- *   write_slots   append / quantise-on-append (one warp per token)
- *   gather        block-table gather with dequantise-on-gather
+ *   write_slots   append / quantise-on-append (eight lanes per token up to
+ *                 768 values, one warp per token beyond; block pools: a
+ *                 CTA per 64 tokens staged in shared memory)
+ *   gather        block-table gather with dequantise-on-gather (64-token CTA
+ *                 tiles; block pools: page runs staged in shared memory)
  *   move_pages    page-granular gather used by defragmenting compaction
  *   compress      contiguous every-k-th token compaction (ct_kv_compress)
  *
