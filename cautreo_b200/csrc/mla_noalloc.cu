@@ -38,7 +38,7 @@ constexpr uint32_t kMaxWorkers = 60;                 /* bounds the split sequenc
 constexpr uint32_t kMaxChunks = kMaxSeqs + kMaxWorkers + 8;
 constexpr int kMaxDevices = 64;
 
-__device__ __align__(256) unsigned char g_mla_noalloc_scratch[kScratchBytes];
+static __device__ __align__(256) unsigned char g_mla_noalloc_scratch[kScratchBytes];
 
 void *g_scratch_addr[kMaxDevices];                    /* device address of the array, per device */
 

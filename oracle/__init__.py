@@ -122,6 +122,8 @@ def build() -> None:
     subprocess.run(["make", "-s", "-C", str(HERE), "port"], check=True)
     if Path("/root/reference/src").is_dir():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+        # the reference's own unit-test programs, built from its sources
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref-tests"], check=True)
         # the reference's unit tests linked against this repository's library
         if (HERE.parent / "cautreo_b200" / "libcautreo_b200.so").exists():
             subprocess.run(["make", "-s", "-C", str(HERE), "ours-tests"], check=True)
