@@ -296,9 +296,9 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_graph:
         graphs = (torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph())
         l0 = ct.launch_count()
-        with torch.cuda.graph(graphs[0], stream=stream):
+        with torch.cuda.graph(graphs[0], stream=stream, capture_error_mode="thread_local"):
             append_call()
-        with torch.cuda.graph(graphs[1], stream=stream):
+        with torch.cuda.graph(graphs[1], stream=stream, capture_error_mode="thread_local"):
             decode_call()
         launches_per_step = ct.launch_count() - l0
         with torch.cuda.stream(stream):
