@@ -294,18 +294,26 @@ def run_ours(args, rank, world, local_rank):
     graphs = None
     launches_per_step = 0
     if not args.no_graph:
-        graphs = (torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph())
-        l0 = ct.launch_count()
-        with torch.cuda.graph(graphs[0], stream=stream, capture_error_mode="thread_local"):
-            append_call()
-        with torch.cuda.graph(graphs[1], stream=stream, capture_error_mode="thread_local"):
-            decode_call()
-        launches_per_step = ct.launch_count() - l0
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                graphs[0].replay()
-                graphs[1].replay()
+        try:
+            g = (torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph())
+            l0 = ct.launch_count()
+            with torch.cuda.graph(g[0], stream=stream, capture_error_mode="thread_local"):
+                append_call()
+            with torch.cuda.graph(g[1], stream=stream, capture_error_mode="thread_local"):
+                decode_call()
+            launches_per_step = ct.launch_count() - l0
+            graphs = g
+        except Exception as exc:                        # keep measuring, from the host loop
+            print(f"rank {rank}: CUDA graph capture failed ({exc}); enqueueing from the host", file=sys.stderr)
+            torch.cuda.synchronize()
+        if graphs:
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    graphs[0].replay()
+                    graphs[1].replay()
         barrier()
+    launch_mode = ("each step replays two CUDA graphs (append; decode + combine)" if graphs
+                   else "each step enqueues its launches from the host")
     clocks = ClockSampler(physical_gpu(dev))
     clocks.start()
     launches0 = ct.launch_count()
@@ -415,8 +423,7 @@ def run_ours(args, rank, world, local_rank):
                    "page_tokens": PAGE, "kv_dtype": "bf16", "softmax_scale": "1/sqrt(192)",
                    "kv_tokens_per_step": int(tok_total), "sharding": "LPT by length" if world > 1 else "none",
                    "parallelism": f"sequence-sharded x{world}",
-                   "launch": "each step replays two CUDA graphs (append; decode + combine)" if not args.no_graph
-                             else "each step enqueues its launches from the host",
+                   "launch": launch_mode,
                    "l2": f"inputs larger than L2 (KV of rank 0: {tok_rank0 * BYTES_PER_TOKEN / 1e6:.0f} MB vs "
                          "126 MB L2, read once per step); no flush"},
         "hbm_gbs": tok_total * args.steps * BYTES_PER_TOKEN / (ms_max * 1e-3) / 1e9,
