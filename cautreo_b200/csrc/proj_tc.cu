@@ -12,6 +12,10 @@
  *       by TMA through a 4-stage ring.  The K range is split over CTAs
  *       (ksplit) so that a decode batch of ~1k tokens still fills the GPU;
  *       each CTA writes its fp32 partial tile to scratch [ksplit][n][dim].
+ *       A batch with more 128-token tiles than SMs (a prefill chunk) gives
+ *       each CTA two token tiles, two accumulators over the same W block, so
+ *       the W bytes streamed from L2 per token halve (splitting K instead
+ *       made such batches slower: their tiles' L2 traffic bounds them).
  * finish sums the ksplit partials in split order (the result does not
  *       depend on timing; one thread per 4 values), then, when asked, the
  *       norm (one warp per token), leaving the fp32 entry for the pool writer.
@@ -41,15 +45,18 @@ constexpr long long kWaitP = 4000000000LL;
 
 __device__ int g_proj_error;
 
-template <int NT>
+/* MT token tiles of 128 rows per CTA share each W block (MT = 2 halves the
+ * W traffic per token for batches that fill the GPU without a K split). */
+template <int NT, int MT>
 struct Layout {
-    static constexpr uint32_t kA = kM * kKB * 2;          /* 16 KB */
+    static constexpr uint32_t kA = MT * kM * kKB * 2;     /* 16 KB per token tile */
     static constexpr uint32_t kB = NT * kKB * 2;
     static constexpr uint32_t kStage = kA + kB;
     static constexpr uint32_t kBars = kStagesP * kStage;  /* full[4], empty[4], acc */
     static constexpr uint32_t kTmemSlot = kBars + 9 * 8;
     static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;
-    static constexpr uint32_t kCols = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
+    static constexpr uint32_t kCols1 = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;   /* one accumulator */
+    static constexpr uint32_t kCols = MT * kCols1;
     static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) |
                                        ((uint32_t)(kM >> 4) << 24);
 };
@@ -67,18 +74,19 @@ __device__ bool wait_p(uint32_t bar, uint32_t parity, volatile int *abort, int c
     }
 }
 
-template <int NT>
+template <int NT, int MT>
 __global__ void __launch_bounds__(kThreadsP, 1)
     k_proj_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap, float *scratch,
               uint32_t n, uint32_t dim, uint32_t kblocks, uint32_t per_split) {
-    using Ly = Layout<NT>;
+    using Ly = Layout<NT, MT>;
+    static_assert(Ly::kBytes <= 232448 && Ly::kCols <= 512, "shared memory / TMEM");
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
     const uint32_t raw = smem_addr(smem_raw);
     const uint32_t base = raw + ((1024u - (raw & 1023u)) & 1023u);
     uint8_t *sbase = smem_raw + (base - raw);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t m0 = blockIdx.x * kM, n0 = blockIdx.y * NT, split = blockIdx.z;
+    const uint32_t m0 = blockIdx.x * (kM * MT), n0 = blockIdx.y * NT, split = blockIdx.z;
     const uint32_t kb0 = split * per_split, kb1 = min(kblocks, kb0 + per_split);
     const uint32_t nkb = kb1 > kb0 ? kb1 - kb0 : 0;
     auto full = [&](uint32_t s) { return base + Ly::kBars + 8 * s; };
@@ -129,24 +137,29 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             tc_fence_after();
             const uint32_t a = base + s * Ly::kStage, b = a + Ly::kA;
             #pragma unroll
-            for (int k = 0; k < kKB / 16; k++)
-                mma_ss(tmem, sdesc(a + k * 32, 1, 64, kSw128), sdesc(b + k * 32, 1, 64, kSw128), Ly::kIdesc,
-                       (i > 0 || k > 0) ? 1u : 0u);
+            for (int mt = 0; mt < MT; mt++) {
+                #pragma unroll
+                for (int k = 0; k < kKB / 16; k++)
+                    mma_ss(tmem + mt * Ly::kCols1, sdesc(a + mt * (kM * 128) + k * 32, 1, 64, kSw128),
+                           sdesc(b + k * 32, 1, 64, kSw128), Ly::kIdesc, (i > 0 || k > 0) ? 1u : 0u);
+            }
             mma_commit(empty(s));
         }
         mma_commit(acc);                        /* also when nothing was issued: the epilogue waits on it */
         const long long t0 = clock64();
         while (!mbar_try(acc, 0) && clock64() - t0 < kWaitP) {}    /* drained before TMEM is freed */
     } else if (warp >= 2) {
-        const uint32_t quad = warp & 3, row = quad * 32 + lane, tok = m0 + row;
+        const uint32_t quad = warp & 3, row = quad * 32 + lane;
         if (__all_sync(0xFFFFFFFFu, wait_p(acc, 0, abort, 3))) {    /* warp-uniform: the TMEM loads are collective */
             tc_fence_after();
-            float *dst = scratch + ((size_t)split * n + tok) * dim + n0;
             #pragma unroll 1
-            for (int c = 0; c < NT; c += 32) {
+            for (int mc = 0; mc < MT * NT; mc += 32) {
+                const int mt = mc / NT, c = mc % NT;
+                const uint32_t tok = m0 + mt * kM + row;
+                float *dst = scratch + ((size_t)split * n + tok) * dim + n0;
                 float v[32];
                 if (nkb > 0) {
-                    tmem_ld32(tmem + ((quad * 32) << 16) + c, v);
+                    tmem_ld32(tmem + ((quad * 32) << 16) + mt * Ly::kCols1 + c, v);
                     tmem_wait_ld();
                 } else {
                     #pragma unroll
@@ -227,21 +240,21 @@ bool map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT>
+template <int NT, int MT>
 int launch_proj(const CUtensorMap &xm, const CUtensorMap &wm, float *scratch, uint32_t n, uint32_t dim,
                 uint32_t kblocks, uint32_t ksplit, uint32_t per_split, cudaStream_t st) {
-    using Ly = Layout<NT>;
+    using Ly = Layout<NT, MT>;
     static int attr_set[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(k_proj_tc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::kBytes) !=
+        if (cudaFuncSetAttribute(k_proj_tc<NT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::kBytes) !=
             cudaSuccess)
             return ct__cuda_status(cudaGetLastError(), "proj smem");
         attr_set[dev] = 1;
     }
-    const dim3 grid((n + kM - 1) / kM, dim / NT, ksplit);
-    k_proj_tc<NT><<<grid, kThreadsP, Ly::kBytes, st>>>(xm, wm, scratch, n, dim, kblocks, per_split);
+    const dim3 grid((n + kM * MT - 1) / (kM * MT), dim / NT, ksplit);
+    k_proj_tc<NT, MT><<<grid, kThreadsP, Ly::kBytes, st>>>(xm, wm, scratch, n, dim, kblocks, per_split);
     return ct__cuda_status(cudaGetLastError(), "proj_tc");
 }
 
@@ -286,7 +299,10 @@ extern "C" int ct_kv_project_write_slots(const void *x, const void *w, const flo
     /* K split: about one wave of CTAs, at least 4 K blocks each */
     const int n_sms = sm_count[dev] > 0 ? sm_count[dev] : 148;
     const uint32_t kblocks = n_in / kKB;
-    const uint32_t tiles = ((n + kM - 1) / kM) * (dim / NT);
+    uint32_t tiles = ((n + kM - 1) / kM) * (dim / NT);
+    /* more 128-token tiles than SMs: two per CTA, sharing the W blocks */
+    const uint32_t MT = (tiles > (uint32_t)n_sms && NT <= 192) ? 2 : 1;
+    if (MT == 2) tiles = ((n + 2 * kM - 1) / (2 * kM)) * (dim / NT);
     uint32_t ksplit = (uint32_t)n_sms / (tiles ? tiles : 1);
     if (ksplit < 1) ksplit = 1;
     if (ksplit > kblocks / 4) ksplit = kblocks / 4 ? kblocks / 4 : 1;
@@ -294,7 +310,7 @@ extern "C" int ct_kv_project_write_slots(const void *x, const void *w, const flo
     const uint32_t per_split = (kblocks + ksplit - 1) / ksplit;
     ksplit = (kblocks + per_split - 1) / per_split;
     CUtensorMap xm, wm;
-    if (!map_bf16(&xm, x, n, n_in, kM) || !map_bf16(&wm, w, dim, n_in, NT)) {
+    if (!map_bf16(&xm, x, n, n_in, kM * MT) || !map_bf16(&wm, w, dim, n_in, NT)) {
         ct__set_error("ct_kv_project_write_slots: tensor map encoding failed");
         return CT_ERR_CUDA;
     }
@@ -304,11 +320,14 @@ extern "C" int ct_kv_project_write_slots(const void *x, const void *w, const flo
     float *scratch = nullptr;
     int rc = ct__scratch_alloc((void **)&scratch, part_bytes + (direct ? 0 : entry_bytes), st);
     if (rc) return rc;
-    switch (NT) {
-        case 256: rc = launch_proj<256>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
-        case 192: rc = launch_proj<192>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
-        case 128: rc = launch_proj<128>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
-        default:  rc = launch_proj<64>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+    switch (NT * 4 + MT) {
+        case 256 * 4 + 1: rc = launch_proj<256, 1>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        case 192 * 4 + 1: rc = launch_proj<192, 1>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        case 192 * 4 + 2: rc = launch_proj<192, 2>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        case 128 * 4 + 1: rc = launch_proj<128, 1>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        case 128 * 4 + 2: rc = launch_proj<128, 2>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        case 64 * 4 + 2:  rc = launch_proj<64, 2>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
+        default:          rc = launch_proj<64, 1>(xm, wm, scratch, n, dim, kblocks, ksplit, per_split, st); break;
     }
     float *entry = direct ? scratch : scratch + (size_t)ksplit * n * dim;
     uint32_t launches = 1;
