@@ -61,10 +61,21 @@ def workload(name):
     return lens, desc, seed
 
 
+GOLDEN = 0x9E3779B97F4A7C15
+MASK64 = (1 << 64) - 1
+
+
+def synth_key(seed, stream):
+    """Key of the seeded synthetic stream (seed, stream): the library's
+    ct_synth_key rule (csrc/synth.cu) restated in Python, so that the workload
+    can be derived without loading any native library (the reference arm
+    must not load this repository's)."""
+    return splitmix((seed * GOLDEN + splitmix(stream + 0x632BE59BD9B4E019)) & MASK64)
+
+
 def lengths_loguniform(n, lo, hi, seed):
     """Same rule as the oracle's generator (ct_oracle.c: floor(lo*(hi/lo)^u))."""
-    import cautreo_b200 as ct  # noqa: F401  (key derivation lives in the library)
-    key = ct.synth_key(seed, 0)
+    key = synth_key(seed, 0)
     out = np.empty(n, np.int64)
     for s in range(n):
         z = splitmix(key + (s + 1) * 0x9E3779B97F4A7C15)
@@ -334,6 +345,8 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     launches = ct.launch_count() - launches0 + launches_per_step * args.steps
     graphs = None                                       # released before the process group goes away
+    # a bounded wait that ran out leaves the kernel's outputs invalid: read its error word
+    tc_error = int(L.ct_mla_tc_error(1))
     clk = clocks.stop()
     ms = t_start.elapsed_time(t_end)
     dec_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in ev]))
@@ -372,8 +385,9 @@ def run_ours(args, rank, world, local_rank):
     # this GPU's decode: algorithmic bytes over its own mean launch time
     my_bytes = tokens * BYTES_PER_TOKEN + n * H * E * 2 + n * H * DV * 2
     my_gbs = my_bytes / (dec_ms * 1e-3) / 1e9
-    vals = torch.tensor([ms, e2e_ms, dec_ms, app_ms, tokens, float(launches), float(n), my_gbs], dtype=torch.float64,
-                        device="cuda")
+    tc_error = max(tc_error, int(L.ct_mla_tc_error(1)))
+    vals = torch.tensor([ms, e2e_ms, dec_ms, app_ms, tokens, float(launches), float(n), my_gbs, float(tc_error != 0)],
+                        dtype=torch.float64, device="cuda")
     if world > 1:
         mx = vals.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -440,6 +454,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if gather_ms is not None:
         line["gather_ms"] = gather_ms
+    if float(mx[8]) != 0.0:
+        line["invalid"] = "a bounded wait of the MLA decode kernel expired on some rank (ct_mla_tc_error != 0)"
     return line
 
 
@@ -514,13 +530,19 @@ def run_reference(args):
         if i >= args.warmup:
             rates.append(r)
     value = float(np.mean(rates))
-    sample = (f"stratified sequences of the workload (first <= {CPU_TOKEN_CAP} tokens each), ~{per_step:.0f} s of "
-              f"decode per step through the reference ct_attn_forward (all 128 heads share the gathered fp32 "
-              f"[n][576] entries)")
+    total = int((lens + 1).sum())
+    sample = (f"each step: up to 64 sequences stratified over the workload's lengths, each decoded over its first "
+              f"<= {CPU_TOKEN_CAP} tokens through the reference ct_attn_forward (all 128 heads share the gathered "
+              f"fp32 [n][576] entries), ~{per_step:.0f} s of decode on {threads} threads; value = sampled KV tokens "
+              f"over the busiest thread's decode time.  Extrapolation to the full step ({total} KV tokens): "
+              f"{total / value:.0f} s at this rate, taking the reference's cost per KV token as independent of the "
+              f"sequence length (each head's pass over n x 576 fp32 entries leaves the host caches beyond ~1k "
+              f"tokens, so longer sequences cost the same per token)")
     return {"metric": METRIC, "value": value, "unit": "KV tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f64 accumulate (f32 in/out)", "data": "synthetic",
             "config": {"workload": desc}, "impl": "reference",
+            "full_step_s_extrapolated": total / value,
             "cpu_baseline": {"value": value, "unit": "KV tokens/s", "cores": threads, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": value, "unit": "KV tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -714,6 +736,8 @@ def run_quant(args):
         }
         res[name]["append_frac"] = res[name]["append_gbs"] / hbm
         res[name]["gather_frac"] = res[name]["gather_gbs"] / hbm
+        if L.ct_mla_tc_error(1) != 0:
+            res[name]["invalid"] = "a bounded wait of the MLA decode kernel expired (ct_mla_tc_error != 0)"
         plan.close()
         kv.close()
     # cold-tier block codecs (quant.h Q8_0 / Q4_0 / Q2_0 / Q1_0): append and gather only

@@ -953,7 +953,8 @@ ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
     uint32_t free_n = 0, log_n = 0, n_live = 0;
     ck_read(&io, &free_n, 4);
     int bad = io.err || free_n > NP;
-    for (uint32_t i = 0; i < S && !bad; i++) bad = h->len[i] > MP * P || h->lo[i] > h->hi[i] || h->hi[i] > MP;
+    for (uint32_t i = 0; i < S && !bad; i++)
+        bad = (uint64_t)h->len[i] > (uint64_t)MP * P || h->lo[i] > h->hi[i] || h->hi[i] > MP;
     for (uint32_t p = 0; p < NP && !bad; p++) bad = h->rank[p] >= NP;
     for (size_t i = 0; i < (size_t)S * MP && !bad; i++) bad = h->bt[i] < -1 || h->bt[i] >= (int32_t)NP;
     if (!bad) {                                        /* reference counts follow from the table */
@@ -961,6 +962,19 @@ ct_kv_paged_t *ct_kv_paged_load(const char *path, int device) {
         for (size_t i = 0; i < (size_t)S * MP; i++) if (h->bt[i] >= 0) h->refc[h->bt[i]]++;
         ck_read(&io, h->heap, (size_t)free_n * 4);
         for (uint32_t i = 0; i < free_n && !bad; i++) bad = h->heap[i] < 0 || h->heap[i] >= (int32_t)NP;
+        /* every page is either free (once) or mapped, never both: a free id
+         * that is also in the table, or listed twice, would let the
+         * allocator hand a live page to another sequence */
+        uint32_t distinct_live = 0;
+        for (uint32_t p = 0; p < NP && !bad; p++) distinct_live += h->refc[p] > 0;
+        for (uint32_t i = 0; i < free_n && !bad; i++) {
+            const int32_t id = h->heap[i];
+            bad = h->refc[id] != 0;
+            h->refc[id] = UINT32_MAX;                  /* marks a free id seen */
+        }
+        for (uint32_t i = 0; i < free_n; i++)          /* undo the marks */
+            if (h->heap[i] >= 0 && h->heap[i] < (int32_t)NP && h->refc[h->heap[i]] == UINT32_MAX) h->refc[h->heap[i]] = 0;
+        bad = bad || (uint64_t)free_n + distinct_live != NP;
     }
     if (!bad) {                                        /* the free set back into rank order */
         int32_t *ids = (int32_t *)malloc((size_t)(free_n ? free_n : 1) * 4);

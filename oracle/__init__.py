@@ -120,7 +120,9 @@ def build() -> None:
     """Build the restatement, and the reference objects when the reference
     sources are present (they are not on every machine that runs tests)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "port"], check=True)
-    if Path("/root/reference/src").is_dir():
+    # where the reference sources lie is the Makefile's REF (overridable from
+    # the environment); `have-ref` succeeds when they are there
+    if subprocess.run(["make", "-s", "-C", str(HERE), "have-ref"], capture_output=True).returncode == 0:
         subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
         # the reference's own unit-test programs, built from its sources
         subprocess.run(["make", "-s", "-C", str(HERE), "ref-tests"], check=True)

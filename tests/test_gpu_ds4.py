@@ -1,7 +1,7 @@
 """GPU: the MLA-lite cache of ds4_forward.c (store at :1565-1570, attention at
 :1572-1627) through ct_ds4_attend, against the oracle's MLA decode on the same
 fp32 latents and the bf16-rounded query (scale 1/sqrt(kv_dim), one head, V =
-the latent).  Tolerance: max-abs <= 2e-2 and norm-relative <= 1e-2 (bf16
+the latent).  Tolerance, elementwise: |got - ref| <= 2e-2 + 1e-2 |ref| (bf16
 query and output)."""
 import ctypes as C
 

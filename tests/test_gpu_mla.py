@@ -1,7 +1,7 @@
 """GPU: paged absorbed-MLA decode (ct_attn_mla_decode_paged) against the
 oracle, whose MLA numerics are pinned bit-exactly to the reference's own
 ct_attn_forward (tests/test_oracle.py).  Tolerance (bf16 inputs, fp32
-accumulation): max-abs <= 2e-2 and norm-relative <= 1e-2."""
+accumulation), elementwise: |got - ref| <= 2e-2 + 1e-2 |ref| (helpers.close)."""
 from pathlib import Path
 
 import numpy as np

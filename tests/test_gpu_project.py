@@ -68,7 +68,10 @@ def project(x, w, n, n_in, dim, pool_dtype, norm_w=None, eps=1e-6, norm_dim=0, n
 
 
 @pytest.mark.parametrize("n,n_in,dim", [(1, 512, 576), (37, 4096, 576), (300, 4096, 576), (130, 1024, 512),
-                                        (1024, 4096, 576), (8192, 512, 576), (6500, 512, 576)])
+                                        (1024, 4096, 576), (8192, 512, 576), (6500, 512, 576),
+                                        # two token tiles per CTA with 128- and 64-wide output tiles
+                                        # (640 = 10 x 64, 320 = 5 x 64), the second with a ragged tail
+                                        (8192, 512, 640), (6500, 512, 320)])
 def test_projection_matches_fp64(n, n_in, dim):
     x, w = inputs(n, n_in, dim, 1)
     codes, _ = project(x, w, n, n_in, dim, ct.CT_KV_F32)

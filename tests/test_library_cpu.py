@@ -265,6 +265,46 @@ def test_paged_checkpoint_rejects_damage(tmp_path):
     h.close()
 
 
+def _fnv1a64(data):
+    h = 0xCBF29CE484222325
+    for b in data:
+        h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def test_paged_checkpoint_rejects_inconsistent_free_set(tmp_path):
+    """A checkpoint whose checksum is right but whose free set names a page
+    the block table maps (or names a page twice) is rejected: loading it
+    would let the allocator hand a live page to another sequence."""
+    S, MP, NP, P = 4, 8, 10, 4
+    h = host_paged(S, MP, NP, P, 0)
+    h.append([0, 1, 2], [5, 9, 1])                # 2 + 3 + 1 = 6 live pages, 4 free
+    path = tmp_path / "kv.ckpt"
+    h.save(path)
+    raw = bytes(path.read_bytes())
+    # header 104 B, then len / lo / hi (4 B each per seq), last_access (8 B),
+    # the block table, the free order (4 B per page), then free_n and the ids
+    off_free = 104 + S * (4 + 4 + 4 + 8) + S * MP * 4 + NP * 4
+    free_n = int(np.frombuffer(raw[off_free:off_free + 4], np.uint32)[0])
+    assert free_n == NP - 6
+    ids = np.frombuffer(raw[off_free + 4:off_free + 4 + 4 * free_n], np.int32).copy()
+    live = int(h.block_table()[0, 0])
+    L = ct.lib()
+    for bad_ids in (np.array([live] + ids[1:].tolist(), np.int32),        # a mapped page marked free
+                    np.array([ids[1]] + ids[1:].tolist(), np.int32)):     # a free page listed twice
+        body = bytearray(raw[:-8])
+        body[off_free + 4:off_free + 4 + 4 * free_n] = bad_ids.tobytes()
+        (tmp_path / "bad.ckpt").write_bytes(bytes(body) + _fnv1a64(body).to_bytes(8, "little"))
+        assert not L.ct_kv_paged_load(str(tmp_path / "bad.ckpt").encode(), -1)
+    # the untouched bytes re-signed the same way still load (the layout above is right)
+    body = bytearray(raw[:-8])
+    (tmp_path / "ok.ckpt").write_bytes(bytes(body) + _fnv1a64(body).to_bytes(8, "little"))
+    g = ct.PagedKV.load(tmp_path / "ok.ckpt", device=-1)
+    assert _state(g) == _state(h)
+    g.close()
+    h.close()
+
+
 # ---- prefix sharing (tables only) ---------------------------------------------
 
 def test_fork_shares_full_pages_copies_the_partial_one():

@@ -2,8 +2,9 @@
 not allocate device memory on their decode path (an engine that reserved
 almost all of HBM for its KV pool, or a serving loop that bans allocator
 calls once running).  It must give the same results as the planned entry
-point (ct_mla_plan_create + ct_attn_mla_decode_paged) within the attention
-tolerance, call after call, without changing the device's free memory.
+point (ct_mla_plan_create + ct_attn_mla_decode_paged) and as the oracle,
+within the attention tolerance, call after call, without changing the
+device's free memory.
 
 This file sorts last so that a run stopping at the first failure has run every
 other test first; it also passes on its own in a fresh process."""
@@ -40,6 +41,7 @@ def test_noalloc_matches_planned_decode_twice():
                 ref_lse.data_ptr(), stream())
     want = oracle.bf16_to_f32(host(ref_out, np.uint16)).reshape(len(lens), MLA_H, MLA_DV)
     want_lse = host(ref_lse, np.float32)
+    oracle_want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
 
     out = empty((len(lens), MLA_H, MLA_DV), np.uint16)
     lse = empty((len(lens), MLA_H), np.float32)
@@ -55,6 +57,9 @@ def test_noalloc_matches_planned_decode_twice():
         got = oracle.bf16_to_f32(host(out, np.uint16)).reshape(len(lens), MLA_H, MLA_DV)
         ok, mx, excess = close(got, want)
         assert ok, (call, mx, excess)
+        if call == 0:                             # and against the oracle directly
+            ok, mx, excess = close(got, oracle_want)
+            assert ok, ("oracle", mx, excess)
         assert np.all(got[lens == 0] == 0)
         got_lse = host(lse, np.float32)
         fin = np.isfinite(want_lse)
