@@ -220,6 +220,24 @@ def test_mla_variable_lengths_sharded_shape():
     assert ok, (mx, rel)
 
 
+@pytest.mark.parametrize("zero_q", [False, True])
+def test_mla_many_short_sequences(zero_q):
+    """Many short sequences: every worker runs several chunks of one to three
+    pages back to back, so chunk boundaries (query reloads, epilogues, the
+    split-KV combine) come every few tiles.  A zero query makes every
+    softmax uniform (output = mean of the latents)."""
+    k = oracle.key(31, 600)
+    lens = oracle.lengths_loguniform(k, 600, 1, 200).astype(np.int32)
+    pool, bt, q = mla_case(lens, seed=31)
+    if zero_q:
+        q = np.zeros_like(q)
+    got, plan = run_decode(pool, bt, lens, q)
+    assert plan.tensor_cores
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(got, want)
+    assert ok, (mx, rel)
+
+
 def test_mla_through_paged_handle():
     """Append through ct_kv_paged_append, then decode the handle's pool."""
     S, E = 3, MLA_E
