@@ -401,16 +401,44 @@ def run_ours(args, rank, world, local_rank):
     gbs_mean = float(sm[7]) / world                     # per-GPU achieved GB/s, mean over ranks
     tok_rank0 = tokens
 
-    # ---- the one exchange: gather outputs to rank 0 (timed separately) ----
+    # ---- the one exchange: outputs and statistics gathered to rank 0 by the
+    # library's NCCL backend (ct_dist_gather_rows / ct_dist_gather_stats),
+    # timed separately with events on the stream the gather runs after ----
     gather_ms = None
+    per_rank = None
     if world > 1:
-        from cautreo_b200.shard import gather_rows
-        gather_rows(out.view(n, H * DV), rank_of, rank, world)    # first collective sets up the communicator
-        torch.cuda.synchronize()
-        g0 = time.perf_counter()
-        full = gather_rows(out.view(n, H * DV), rank_of, rank, world)
-        torch.cuda.synchronize()
-        gather_ms = (time.perf_counter() - g0) * 1e3
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(ct.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)                         # the launcher's process group carries the id
+        nctx = ct.NcclContext(rank, world, bytes(uid.cpu().numpy()), dev)
+        full = torch.empty((n_all, H * DV), dtype=torch.int16, device="cuda") if rank == 0 else None
+        ids = mine.astype(np.uint32)
+        row_bytes = H * DV * 2
+
+        def gather():
+            nctx.gather_rows(out.data_ptr(), n, row_bytes, ids, n_all, full.data_ptr() if full is not None else None,
+                             sp)
+
+        gather()                                       # first call sizes the staging buffers
+        gms = []
+        for _ in range(3):
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            gather()
+            g1.record(stream)
+            torch.cuda.synchronize()
+            gms.append(g0.elapsed_time(g1))
+        gt = torch.tensor([float(np.median(gms))], dtype=torch.float64, device="cuda")
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gather_ms = float(gt[0])
+        mine_stats = ct.DistStats(int(tokens), int(my_bytes), float(dec_ms * 1e3), int(tc_error), int(n))
+        allst = nctx.gather_stats(mine_stats)
+        if rank == 0:
+            per_rank = [{"kv_tokens": int(x.kv_tokens), "bytes": int(x.bytes), "decode_us": float(x.decode_us),
+                         "error": int(x.error), "n_seqs": int(x.n_seqs)} for x in allst]
+        nctx.close()
 
     if rank != 0:
         return None
@@ -453,7 +481,9 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
     }
     if gather_ms is not None:
-        line["gather_ms"] = gather_ms
+        line["gather_ms"] = gather_ms                 # outputs of every rank to rank 0 (C-ABI NCCL gather)
+        line["value_with_gather"] = tok_total / ((ms_max / args.steps + gather_ms) * 1e-3)
+        line["per_rank"] = per_rank
     if float(mx[8]) != 0.0:
         line["invalid"] = "a bounded wait of the MLA decode kernel expired on some rank (ct_mla_tc_error != 0)"
     return line
@@ -863,6 +893,87 @@ def run_produce(args):
             "paths": res}
 
 
+def run_serve(args):
+    """A serving loop whose sequences grow: the sequence-sharded workload's
+    1024 sequences (512..65536 tokens, seed 4) take one new token each per
+    step through the paged allocator (ct_kv_paged_append: host bookkeeping,
+    pages opened as lengths cross page boundaries, block-table and length
+    updates scattered to the device, the token written), then one decode
+    over all their tokens with a plan created once (the work split is
+    recomputed on the device from the current lengths at every decode).
+    Timed per step on the device (events around the step on the launching
+    stream) and on the host (wall clock, which includes the allocator)."""
+    import torch
+    import cautreo_b200 as ct
+    L = ct.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    lens0 = lengths_loguniform(1024, 512, 65536, seed=4)
+    n = len(lens0)
+    grow = args.warmup + args.steps + 1
+    cap = lens0 + grow
+    pages_cap = (cap + PAGE - 1) // PAGE
+    n_pages, max_pages = int(pages_cap.sum()), int(pages_cap.max())
+    kv = ct.PagedKV(n, max_pages, n_pages, PAGE, E, 0, ct.CT_KV_BF16, 0, sp)
+    kv.set_free_order(np.random.default_rng(4000).permutation(n_pages).astype(np.int32))
+    kv.append(list(range(n)), lens0.tolist(), None)              # the cached context, slots reserved
+    rows = torch.arange(n, dtype=torch.int32, device="cuda")
+    ct.check(L.ct_synth_fill_paged(kv.pool, None, ct.CT_KV_BF16, kv.block_table_dev, max_pages, rows.data_ptr(),
+                                   kv.seq_lens_dev, n, int(lens0.max()), PAGE, E, ct.synth_key(4, 10), 0, 1.0, sp), "fill")
+    q = torch.empty(n * H * E, dtype=torch.int16, device="cuda")
+    new_tok = torch.empty(n * E, dtype=torch.int16, device="cuda")
+    ct.check(L.ct_synth_fill(q.data_ptr(), 0, ct.synth_key(4, 11), 0, n * H * E, 0, 1.0, sp))
+    ct.check(L.ct_synth_fill(new_tok.data_ptr(), 0, ct.synth_key(4, 13), 0, n * E, 0, 1.0, sp))
+    out = torch.empty(n * H * DV, dtype=torch.int16, device="cuda")
+    plan = ct.MlaPlan(lens0.astype(np.int32), n_pages, max_pages_per_seq=max_pages)
+    seqs = np.arange(n, dtype=np.uint32)
+    ones = np.ones(n, np.uint32)
+    torch.cuda.synchronize()
+
+    def step():
+        ct.check(L.ct_kv_paged_append(kv.h, seqs.ctypes.data, ones.ctypes.data, n, new_tok.data_ptr(),
+                                      ct.CT_KV_BF16), "append")
+        ct.check(L.ct_attn_mla_decode_paged(plan.h, q.data_ptr(), kv.pool, None, kv.block_table_dev, kv.seq_lens_dev,
+                                            out.data_ptr(), None, sp), "decode")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    opened0 = kv.stats().n_pages_live
+    tok0 = int(kv.seq_lens().astype(np.int64).sum())
+    e0, e1 = _events(torch, 2)
+    launches0 = ct.launch_count()
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / args.steps
+    launches = ct.launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    assert L.ct_mla_tc_error(1) == 0
+    st = kv.stats()
+    attended = tok0 + n * (args.steps + 1) / 2.0      # mean KV tokens a timed step attends (each adds n)
+    hbm, hbm_kind = measured_hbm()
+    gbs = (attended * BYTES_PER_TOKEN + n * H * (E + DV) * 2) / (ms * 1e-3) / 1e9
+    line = {"metric": "serving loop with growing sequences: KV tokens/s per decode step including the allocator",
+            "value": attended / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "host_ms_per_step": wall, "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic (seed 4)",
+            "config": {"workload": "1024 seqs, 512..65536 tokens (seed 4), +1 token per sequence per step through "
+                                   "ct_kv_paged_append, decode with one plan (device-side work split)",
+                       "l2": "inputs larger than L2; no flush"},
+            "pages_opened_in_timed_steps": int(st.n_pages_live - opened0),
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_kind": hbm_kind, "kernel": "whole step (append + plan + decode + combine)"}}
+    plan.close()
+    kv.close()
+    return line
+
+
 def run_evict(args):
     """256 sequences, lengths log-uniform 512..32768 (seed 3), 64-token bf16
     MLA pages in a pool of 60 % of the demand, 4096-token sliding window with
@@ -940,7 +1051,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sharded", choices=["sharded", "mla32", "plain", "quant", "evict", "produce"])
+    ap.add_argument("--workload", default="sharded",
+                    choices=["sharded", "mla32", "plain", "quant", "evict", "produce", "serve"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="enqueue each step's launches from the host")
@@ -948,10 +1060,11 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
 
-    if args.workload in ("plain", "quant", "evict", "produce"):
+    if args.workload in ("plain", "quant", "evict", "produce", "serve"):
         if int(os.environ.get("RANK", "0")) != 0 or args.impl == "reference":
             return 0          # one-GPU measurements of the other configurations
-        line = {"plain": run_plain, "quant": run_quant, "evict": run_evict, "produce": run_produce}[args.workload](args)
+        line = {"plain": run_plain, "quant": run_quant, "evict": run_evict, "produce": run_produce,
+                "serve": run_serve}[args.workload](args)
         print(json.dumps(line), flush=True)
         return 0
 

@@ -217,6 +217,10 @@ SIGNATURES = {
     "ct_dist_available_memory": (U64, [P, U32]),
     "ct_dist_shard_lpt": (I, [P, U32, U32, P]),
     "ct_dist_rank_sequences": (U32, [P, U32, U32, P]),
+    "ct_dist_nccl_unique_id": (I, [P]),
+    "ct_dist_init_nccl": (P, [P, P, I]),
+    "ct_dist_gather_rows": (I, [P, P, U32, SZ, P, U32, P, P]),
+    "ct_dist_gather_stats": (I, [P, P, P]),
     # synth.h
     "ct_synth_key": (U64, [U64, U64]),
     "ct_synth_fill": (I, [P, U32, U64, U64, U64, U32, F, P]),
@@ -492,6 +496,50 @@ class MlaPlan:
                                                 ptr(scales), ptr(block_table), ptr(seq_lens), ptr(out_host),
                                                 stream)
         check(rc, "ct_attn_mla_decode_step_host")
+
+
+class DistConfig(C.Structure):
+    _fields_ = [("mode", C.c_int), ("n_devices", C.c_uint32), ("device_id", C.c_uint32), ("device_names", C.c_void_p)]
+
+
+class DistStats(C.Structure):
+    _fields_ = [("kv_tokens", C.c_uint64), ("bytes", C.c_uint64), ("decode_us", C.c_double), ("error", C.c_int32),
+                ("n_seqs", C.c_uint32)]
+
+
+class NcclContext:
+    """ct_dist_init_nccl: an NCCL communicator over world processes, one GPU
+    each; `uid` is the 128-byte id rank 0 made with nccl_unique_id()."""
+
+    def __init__(self, rank, world, uid, device):
+        self.cfg = DistConfig(0, world, rank, None)
+        buf = (C.c_uint8 * 128).from_buffer_copy(bytes(uid))
+        self.h = lib().ct_dist_init_nccl(C.byref(self.cfg), buf, device)
+        if not self.h:
+            raise RuntimeError("ct_dist_init_nccl failed: " + lib().ct_hal_cuda_last_error().decode())
+        self.rank, self.world = rank, world
+
+    def gather_rows(self, rows, n_rows, row_bytes, global_ids, n_global, out, stream=None):
+        ids = np.ascontiguousarray(global_ids, np.uint32)
+        check(lib().ct_dist_gather_rows(self.h, ptr(rows), n_rows, row_bytes, ptr(ids), n_global, ptr(out), stream),
+              "ct_dist_gather_rows")
+
+    def gather_stats(self, mine):
+        out = (DistStats * self.world)()
+        check(lib().ct_dist_gather_stats(self.h, C.byref(mine), C.cast(out, C.c_void_p) if self.rank == 0 else None),
+              "ct_dist_gather_stats")
+        return list(out) if self.rank == 0 else None
+
+    def close(self):
+        if self.h:
+            lib().ct_dist_destroy(self.h)
+            self.h = None
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_uint8 * 128)()
+    check(lib().ct_dist_nccl_unique_id(buf), "ct_dist_nccl_unique_id")
+    return bytes(buf)
 
 
 def lpt_shard(lengths, n_ranks):

@@ -80,11 +80,23 @@ int ct__launch_attn_shared(const float *q, const float *k, const float *v, uint3
                            uint32_t n_heads, uint32_t head_dim, float scale, float *out,
                            float *scratch_scores, void *stream);
 int ct__launch_softmax(float *x, uint32_t n, void *stream);
+/* dst[ids[i]] = src[i] for n rows of row_bytes (a multiple of 4). */
+int ct__launch_scatter_rows(void *dst, const void *src, const uint32_t *ids, uint32_t n, size_t row_bytes,
+                            void *stream);
 
+/* Work list of n_seq sequences from the device lengths (mla_plan.cu):
+ * chunks [n_seq + n_workers], worker_begin [n_workers + 1], combines,
+ * counts[2] = (chunks, combines) written. */
+int ct__launch_mla_plan(const uint32_t *rows, const int32_t *seq_lens, uint32_t n_seq, uint32_t page_tokens,
+                        uint32_t max_pages, uint32_t n_workers, ct_mla_chunk_t *chunks, int32_t *worker_begin,
+                        ct_mla_combine_t *combines, int32_t *counts, void *stream);
+/* counts (device, may be NULL): how many of the n_chunks / n_combines
+ * entries are in use (the CUDA-core and combine launches cover n_chunks /
+ * n_combines blocks and skip the rest). */
 int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks,
                           uint32_t n_chunks, const int32_t *worker_begin, uint32_t n_workers,
                           const ct_mla_combine_t *combines,
-                          uint32_t n_combines, const void *q, const void *pool,
+                          uint32_t n_combines, const int32_t *counts, const void *q, const void *pool,
                           const float *scales, const int32_t *block_table,
                           const int32_t *seq_lens, void *out, float *lse, float *part_o,
                           float *part_ml, void *stream, uint32_t *n_launches);

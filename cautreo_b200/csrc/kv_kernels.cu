@@ -922,3 +922,31 @@ extern "C" int ct__launch_scatter_i32(int32_t *dst, const int32_t *pairs, uint32
     ct__count_launches(1);
     return ct__cuda_status(cudaGetLastError(), "scatter_i32");
 }
+
+/* Gathered rows to their places: dst[ids[i]] = src[i] for n rows of
+ * row_bytes (a multiple of 4), a warp per row. */
+__global__ void k_scatter_rows(uint8_t *dst, const uint8_t *src, const uint32_t *ids, uint32_t n, size_t row_bytes) {
+    const uint32_t lane = threadIdx.x & 31;
+    const size_t warps = (size_t)gridDim.x * (blockDim.x / 32);
+    for (size_t r = blockIdx.x * (size_t)(blockDim.x / 32) + (threadIdx.x >> 5); r < n; r += warps) {
+        const uint8_t *s = src + r * row_bytes;
+        uint8_t *d = dst + (size_t)ids[r] * row_bytes;
+        if (row_bytes % 16 == 0 && ((uintptr_t)s & 15) == 0 && ((uintptr_t)d & 15) == 0) {
+            for (size_t i = lane; i < row_bytes / 16; i += 32)
+                reinterpret_cast<uint4 *>(d)[i] = reinterpret_cast<const uint4 *>(s)[i];
+        } else {
+            for (size_t i = lane; i < row_bytes / 4; i += 32)
+                reinterpret_cast<uint32_t *>(d)[i] = reinterpret_cast<const uint32_t *>(s)[i];
+        }
+    }
+}
+
+extern "C" int ct__launch_scatter_rows(void *dst, const void *src, const uint32_t *ids, uint32_t n, size_t row_bytes,
+                                       void *stream) {
+    if (n == 0) return CT_OK;
+    if (!dst || !src || !ids || row_bytes % 4 != 0) return CT_ERR_ARG;
+    k_scatter_rows<<<ct__grid_for((size_t)n * 32, 256, 148 * 8), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), ids, n, row_bytes);
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "scatter_rows");
+}

@@ -168,7 +168,7 @@ extern "C" int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, con
     const size_t off_wb = align256((size_t)nc * sizeof(ct_mla_chunk_t));
     const size_t off_cb = off_wb + align256((size_t)(W + 1) * sizeof(int32_t));
     const size_t off_ml = off_cb + align256((size_t)(ncb ? ncb : 1) * sizeof(ct_mla_combine_t));
-    const size_t off_o = off_ml + align256((size_t)(parts ? parts : 1) * shape->n_heads * 2 * sizeof(float));
+    const size_t off_o = off_ml + align256((size_t)(parts ? parts : 1) * shape->n_heads * 4 * sizeof(float));
     const size_t need = off_o + (size_t)(parts ? parts : 1) * shape->n_heads * shape->v_dim * sizeof(float);
     if (need > kScratchBytes) {
         ct__set_error("ct_attn_mla_decode_paged_noalloc: this batch needs more than CT_MLA_NOALLOC_SCRATCH_BYTES "
@@ -190,7 +190,7 @@ extern "C" int ct_attn_mla_decode_paged_noalloc(const ct_mla_shape_t *shape, con
     uint32_t launches = 0;
     return ct__launch_mla_decode(&dims, reinterpret_cast<const ct_mla_chunk_t *>(base), nc,
                                  reinterpret_cast<const int32_t *>(base + off_wb), W,
-                                 reinterpret_cast<const ct_mla_combine_t *>(base + off_cb), ncb, q, pool, scales,
+                                 reinterpret_cast<const ct_mla_combine_t *>(base + off_cb), ncb, nullptr, q, pool, scales,
                                  block_table, seq_lens, out, lse, reinterpret_cast<float *>(base + off_o),
                                  reinterpret_cast<float *>(base + off_ml), stream, &launches);
 }

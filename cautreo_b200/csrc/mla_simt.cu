@@ -76,9 +76,11 @@ __device__ __forceinline__ void load_tile(float *kv_s, const void *pool, const f
 
 template <int Dtype>
 __global__ void __launch_bounds__(256) k_mla_simt(ct_mla_dims_t dims, const ct_mla_chunk_t *chunks,
-                                                  const uint16_t *q, const void *pool, const float *scales,
-                                                  const int32_t *block_table, const int32_t *seq_lens,
-                                                  uint16_t *out, float *lse, float *part_o, float *part_ml) {
+                                                  const int32_t *counts, const uint16_t *q, const void *pool,
+                                                  const float *scales, const int32_t *block_table,
+                                                  const int32_t *seq_lens, uint16_t *out, float *lse, float *part_o,
+                                                  float *part_ml) {
+    if (counts && (int32_t)blockIdx.x >= counts[0]) return;       /* beyond the planned chunks */
     extern __shared__ float smem[];
     float *q_s = smem;                            /* [HG][QSTR] */
     float *kv_s = q_s + HG * QSTR;                /* [TT][KSTR] */
@@ -173,43 +175,49 @@ __global__ void __launch_bounds__(256) k_mla_simt(ct_mla_dims_t dims, const ct_m
                 part_o[ph * Dv + d0] = acc[h][0];
                 if (d0 + 1 < Dv) part_o[ph * Dv + d0 + 1] = acc[h][1];
             }
-            if (threadIdx.x == 0) { part_ml[2 * ph] = mh; part_ml[2 * ph + 1] = lh; }
+            if (threadIdx.x == 0) { part_ml[4 * ph] = mh; part_ml[4 * ph + 1] = lh; part_ml[4 * ph + 2] = lh; }
         }
     }
 }
 
 }  // namespace
 
-/* Split-KV combine: partials (o_i unnormalised, m_i in log2 units, l_i)
- * merge as o = sum_i 2^(m_i - M) o_i / sum_i 2^(m_i - M) l_i. */
-__global__ void __launch_bounds__(128) k_mla_combine(const ct_mla_combine_t *items, uint32_t H, uint32_t Dv,
-                                                     const float *part_o, const float *part_ml, uint16_t *out,
-                                                     float *lse) {
+/* Split-KV combine: partials (o_i unnormalised, m_i in log2 units, and the
+ * row sums l_i of the value dims below and above v_dim / 2 -- the two SMs of
+ * a tensor-core worker each normalise their half of the dims by their own
+ * sum) merge as o = sum_i 2^(m_i - M) o_i / sum_i 2^(m_i - M) l_i.  Entries
+ * of part_ml are (m, l_lo, l_hi, unused). */
+__global__ void __launch_bounds__(128) k_mla_combine(const ct_mla_combine_t *items, const int32_t *counts, uint32_t H,
+                                                     uint32_t Dv, const float *part_o, const float *part_ml,
+                                                     uint16_t *out, float *lse) {
+    if (counts && (int32_t)blockIdx.x >= counts[1]) return;       /* beyond the planned combines */
     const ct_mla_combine_t it = items[blockIdx.x];
     const uint32_t h = blockIdx.y;
     float M = -INFINITY;
     for (int i = 0; i < it.n_parts; i++) {
         const size_t ph = (size_t)(it.first_part + i) * H + h;
-        if (part_ml[2 * ph + 1] > 0.0f) M = fmaxf(M, part_ml[2 * ph]);
+        if (part_ml[4 * ph + 1] > 0.0f) M = fmaxf(M, part_ml[4 * ph]);
     }
-    float L = 0.0f;
+    float L[2] = {0.0f, 0.0f};
     for (int i = 0; i < it.n_parts; i++) {
         const size_t ph = (size_t)(it.first_part + i) * H + h;
-        const float li = part_ml[2 * ph + 1];
-        if (li > 0.0f) L += exp2f(part_ml[2 * ph] - M) * li;
+        if (part_ml[4 * ph + 1] > 0.0f) {
+            const float w = exp2f(part_ml[4 * ph] - M);
+            L[0] += w * part_ml[4 * ph + 1];
+            L[1] += w * part_ml[4 * ph + 2];
+        }
     }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    const float inv[2] = {L[0] > 0.0f ? 1.0f / L[0] : 0.0f, L[1] > 0.0f ? 1.0f / L[1] : 0.0f};
     const size_t oh = (size_t)it.seq * H + h;
     for (uint32_t d = threadIdx.x; d < Dv; d += blockDim.x) {
         float o = 0.0f;
         for (int i = 0; i < it.n_parts; i++) {
             const size_t ph = (size_t)(it.first_part + i) * H + h;
-            const float li = part_ml[2 * ph + 1];
-            if (li > 0.0f) o = fmaf(exp2f(part_ml[2 * ph] - M), part_o[ph * Dv + d], o);
+            if (part_ml[4 * ph + 1] > 0.0f) o = fmaf(exp2f(part_ml[4 * ph] - M), part_o[ph * Dv + d], o);
         }
-        out[oh * Dv + d] = ct_f32_to_bf16(o * inv);
+        out[oh * Dv + d] = ct_f32_to_bf16(o * inv[d >= Dv / 2]);
     }
-    if (lse && threadIdx.x == 0) lse[oh] = L > 0.0f ? M * kLn2 + logf(L) : -INFINITY;
+    if (lse && threadIdx.x == 0) lse[oh] = L[0] > 0.0f ? M * kLn2 + logf(L[0]) : -INFINITY;
 }
 
 /* Declared in mla_tc.cu: the tcgen05 kernel for H=128, E=576, Dv=512, P=64,
@@ -223,7 +231,7 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
 extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chunk_t *chunks,
                                      uint32_t n_chunks, const int32_t *worker_begin, uint32_t n_workers,
                                      const ct_mla_combine_t *combines,
-                                     uint32_t n_combines, const void *q, const void *pool,
+                                     uint32_t n_combines, const int32_t *counts, const void *q, const void *pool,
                                      const float *scales, const int32_t *block_table,
                                      const int32_t *seq_lens, void *out, float *lse, float *part_o,
                                      float *part_ml, void *stream, uint32_t *n_launches) {
@@ -239,7 +247,7 @@ extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chu
             switch (dims->kv_dtype) {
 #define CT_SIMT(D)                                                                                        \
     cudaFuncSetAttribute(k_mla_simt<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes); \
-    k_mla_simt<D><<<grid, 256, kSmemBytes, st>>>(*dims, chunks, static_cast<const uint16_t *>(q), pool,  \
+    k_mla_simt<D><<<grid, 256, kSmemBytes, st>>>(*dims, chunks, counts, static_cast<const uint16_t *>(q), pool, \
                                                   scales, block_table, seq_lens,                         \
                                                   static_cast<uint16_t *>(out), lse, part_o, part_ml);   \
     break;
@@ -259,7 +267,7 @@ extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chu
     }
     if (n_combines > 0) {
         k_mla_combine<<<dim3(n_combines, dims->n_heads), 128, 0, st>>>(
-            combines, dims->n_heads, dims->v_dim, part_o, part_ml, static_cast<uint16_t *>(out), lse);
+            combines, counts, dims->n_heads, dims->v_dim, part_o, part_ml, static_cast<uint16_t *>(out), lse);
         int rc = ct__cuda_status(cudaGetLastError(), "mla_combine");
         if (rc != CT_OK) return rc;
         launches++;

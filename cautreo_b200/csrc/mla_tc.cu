@@ -764,8 +764,9 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
                 if (ch.part < 0) {
                     if (p.lse) p.lse[oh] = -INFINITY;
                 } else {
-                    p.part_ml[2 * ((size_t)ch.part * kH + r.row)] = -INFINITY;
-                    p.part_ml[2 * ((size_t)ch.part * kH + r.row) + 1] = 0.0f;
+                    float *ml = p.part_ml + 4 * ((size_t)ch.part * kH + r.row);     /* (m, l_lo, l_hi, -) */
+                    ml[0] = -INFINITY;
+                    ml[1] = ml[2] = 0.0f;
                 }
             }
             continue;
@@ -820,8 +821,10 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             if (ch.part < 0) {
                 if (p.lse) p.lse[oh] = l_tot > 0.0f ? r.m_used * kLn2 + logf(l_tot) : -INFINITY;
             } else {
-                p.part_ml[2 * ((size_t)ch.part * kH + r.row)] = r.m_used;
-                p.part_ml[2 * ((size_t)ch.part * kH + r.row) + 1] = l_tot;
+                /* both CTAs use the same probabilities: one sum for both halves of the dims */
+                float *ml = p.part_ml + 4 * ((size_t)ch.part * kH + r.row);     /* (m, l_lo, l_hi, -) */
+                ml[0] = r.m_used;
+                ml[1] = ml[2] = l_tot;
             }
         }
         nchunk++;

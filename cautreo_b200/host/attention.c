@@ -6,13 +6,15 @@
  * arguments, defaults and return values; inputs are copied to the device, the
  * kernels of attn_plain.cu run, the result is copied back.
  *
- * Part 2: MLA decode plans.  A plan splits every sequence's pages into
- * chunks so that each worker (a pair of SMs for the tensor-core kernel, one
- * block per chunk and head group for the CUDA-core kernel) gets the same
- * number of KV tokens: the sequences are laid end to end, cut into n_workers
- * equal token ranges at page boundaries, and every range becomes the chunks
- * of the sequences it covers.  Chunks of a split sequence write partial
- * (o, m, l) to the plan's scratch; one combine launch merges them.
+ * Part 2: MLA decode plans.  A plan holds the device buffers of the work
+ * split for a fixed number of sequences: every decode first runs the
+ * planning kernel (csrc/mla_plan.cu), which lays the sequences' pages end to
+ * end from the CURRENT device lengths and gives each worker (a pair of SMs
+ * for the tensor-core kernel, one block per chunk and head group for the
+ * CUDA-core kernel) the same number of pages; chunks of a split sequence
+ * write partial (o, m, l) to the plan's scratch and one combine launch
+ * merges them.  So a plan stays valid while the sequences grow, and a
+ * serving step needs no host planning and no allocation.
  */
 #include "../../include/attention.h"
 #include "../../include/hal.h"
@@ -78,13 +80,16 @@ void ct_attn_softmax(float *x, uint32_t n) {
 
 struct ct_mla_plan {
     ct_mla_dims_t dims;
-    uint32_t n_seq, n_workers, n_chunks, n_combines, n_parts;
+    uint32_t n_seq, n_workers, n_chunks, n_combines, n_parts;   /* the split of the creation lengths */
+    uint32_t cap_chunks, cap_combines, cap_parts;
     int device;
     int tensor_cores;
-    ct_mla_chunk_t *chunks;      /* device [n_chunks], worker-major */
+    ct_mla_chunk_t *chunks;      /* device [cap_chunks], worker-major, written by the planning kernel */
     int32_t *worker_begin;       /* device [n_workers + 1] */
-    ct_mla_combine_t *combines;  /* device [n_combines] */
-    float *part_o, *part_ml;     /* device scratch */
+    ct_mla_combine_t *combines;  /* device [cap_combines] */
+    int32_t *counts;             /* device: chunks and combines of the last decode */
+    uint32_t *rows_dev;          /* device [n_seq] block-table rows, or NULL for 0..n_seq-1 */
+    float *part_o, *part_ml;     /* device scratch: [cap_parts][n_heads][v_dim], [cap_parts][n_heads][4] */
     size_t scratch_bytes;
     void *stage_q, *stage_e, *stage_o;   /* device staging of ct_attn_mla_decode_step_host */
     uint32_t last_launches;
@@ -109,7 +114,7 @@ int ct__mla_tc_workers(const ct_mla_dims_t *dims, int device);
 
 void ct_mla_plan_destroy(ct_mla_plan_t *p) {
     if (!p) return;
-    cudaFree(p->chunks); cudaFree(p->worker_begin); cudaFree(p->combines);
+    cudaFree(p->chunks); cudaFree(p->worker_begin); cudaFree(p->combines); cudaFree(p->counts); cudaFree(p->rows_dev);
     cudaFree(p->part_o); cudaFree(p->part_ml);
     cudaFree(p->stage_q); cudaFree(p->stage_e); cudaFree(p->stage_o);
     for (uint32_t g = 0; g < CT_STEP_GROUPS; g++) {
@@ -155,15 +160,12 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
     p->n_workers = tc_workers > 0 ? (uint32_t)tc_workers : (uint32_t)n_sms;
     p->tensor_cores = tc_workers > 0;
 
-    /* Token quota per worker; cuts fall on page boundaries. */
-    uint64_t total = 0;
     for (uint32_t s = 0; s < n_seq; s++) {
         if (seq_lens[s] < 0 || (uint64_t)(seq_lens[s] + P - 1) / P > shape->max_pages_per_seq) {
             ct__set_error("ct_mla_plan_create: sequence longer than its block-table row");
             free(p);
             return NULL;
         }
-        total += (uint64_t)seq_lens[s];
     }
     p->rows_h = (uint32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(uint32_t));
     p->lens_h = (int32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(int32_t));
@@ -177,79 +179,42 @@ ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *s
         p->lens_h[s] = seq_lens[s];
     }
     const uint32_t W = p->n_workers;
-    const uint64_t quota = total / W + 1;
-    const size_t cap = (size_t)n_seq + 2 * (size_t)W + 8;
-    ct_mla_chunk_t *ch = (ct_mla_chunk_t *)calloc(cap, sizeof *ch);
-    int32_t *wb = (int32_t *)calloc((size_t)W + 1, sizeof(int32_t));
-    int32_t *first_chunk = (int32_t *)malloc((size_t)(n_seq ? n_seq : 1) * sizeof(int32_t));
-    int32_t *n_of = (int32_t *)calloc((size_t)(n_seq ? n_seq : 1), sizeof(int32_t));
-    if (!ch || !wb || !first_chunk || !n_of) goto fail;
-
-    uint32_t nc = 0, w = 0;
-    uint64_t filled = 0;                 /* tokens given to worker w */
-    wb[0] = 0;
+    /* The split the planning kernel makes for the creation lengths (the same
+     * rule, for ct_mla_plan_chunks): pages end to end, W equal page ranges. */
+    uint64_t total = 0;
+    for (uint32_t s = 0; s < n_seq; s++) total += ((uint32_t)seq_lens[s] + P - 1) / P;
+    const uint64_t Q = total ? (total + W - 1) / W : 1;
+    uint64_t cp = 0;
     for (uint32_t s = 0; s < n_seq; s++) {
-        const int32_t row = seq_rows ? (int32_t)seq_rows[s] : (int32_t)s;
-        const uint32_t pages = ((uint32_t)seq_lens[s] + P - 1) / P;
-        first_chunk[s] = (int32_t)nc;
-        if (pages == 0) {                /* empty sequence: one chunk that writes zeros */
-            ch[nc++] = (ct_mla_chunk_t){ (int32_t)s, row, 0, 0, -1, {0, 0, 0} };
-            n_of[s] = 1;
-            continue;
-        }
-        uint32_t pg = 0;
-        while (pg < pages) {
-            uint64_t room = quota > filled ? quota - filled : 0;
-            uint32_t take = (uint32_t)((room + P / 2) / P);          /* nearest page count */
-            if (take == 0) take = 1;
-            if (w + 1 >= W || take > pages - pg) take = pages - pg;   /* last worker takes the rest */
-            ch[nc++] = (ct_mla_chunk_t){ (int32_t)s, row, (int32_t)pg, (int32_t)(pg + take), 0, {0, 0, 0} };
-            n_of[s]++;
-            uint64_t tok = (uint64_t)take * P;
-            if (pg + take == pages) tok = (uint64_t)seq_lens[s] - (uint64_t)pg * P;
-            pg += take;
-            filled += tok;
-            if (filled + P / 2 >= quota && w + 1 < W) { wb[++w] = (int32_t)nc; filled = 0; }
-            if (nc + 2 >= cap) goto fail;
-        }
+        const uint64_t np = ((uint32_t)seq_lens[s] + P - 1) / P;
+        const uint32_t n = np ? (uint32_t)((cp + np - 1) / Q - cp / Q + 1) : 1;
+        p->n_chunks += n;
+        if (n > 1) { p->n_parts += n; p->n_combines++; }
+        cp += np;
     }
-    while (w < W) wb[++w] = (int32_t)nc;
-    p->n_chunks = nc;
-
-    /* Partial slots for split sequences, and their combine items. */
-    ct_mla_combine_t *cb = (ct_mla_combine_t *)calloc((size_t)(n_seq ? n_seq : 1), sizeof *cb);
-    if (!cb) goto fail;
-    uint32_t parts = 0, ncb = 0;
-    for (uint32_t s = 0; s < n_seq; s++) {
-        if (n_of[s] <= 1) { ch[first_chunk[s]].part = -1; continue; }
-        cb[ncb++] = (ct_mla_combine_t){ (int32_t)s, (int32_t)parts, n_of[s], 0 };
-        for (int32_t i = 0; i < n_of[s]; i++) ch[first_chunk[s] + i].part = (int32_t)(parts++);
-    }
-    p->n_combines = ncb;
-    p->n_parts = parts;
-
+    /* Capacities for any lengths: every interior cut adds one chunk, and
+     * split sequences hold at most 2 (W - 1) parts and W - 1 combines. */
+    p->cap_chunks = n_seq + W;
+    p->cap_combines = W < n_seq ? W : (n_seq ? n_seq : 1);
+    p->cap_parts = 2 * W < n_seq + W ? 2 * W : n_seq + W;
     int rc = ct__cuda_status(cudaSetDevice(device), "ct_mla_plan_create");
-    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->chunks, (size_t)(nc ? nc : 1) * sizeof *ch), "plan chunks");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->chunks, (size_t)p->cap_chunks * sizeof(ct_mla_chunk_t)), "plan chunks");
     if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->worker_begin, ((size_t)W + 1) * sizeof(int32_t)), "plan workers");
-    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->combines, (size_t)(ncb ? ncb : 1) * sizeof *cb), "plan combines");
-    const size_t po = (size_t)(parts ? parts : 1) * shape->n_heads * shape->v_dim * sizeof(float);
-    const size_t pm = (size_t)(parts ? parts : 1) * shape->n_heads * 2 * sizeof(float);
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->combines, (size_t)p->cap_combines * sizeof(ct_mla_combine_t)), "plan combines");
+    if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->counts, 2 * sizeof(int32_t)), "plan counts");
+    if (!rc && seq_rows) {
+        rc = ct__cuda_status(cudaMalloc((void **)&p->rows_dev, (size_t)(n_seq ? n_seq : 1) * sizeof(uint32_t)), "plan rows");
+        if (!rc && n_seq)
+            rc = ct__cuda_status(cudaMemcpy(p->rows_dev, seq_rows, (size_t)n_seq * sizeof(uint32_t), cudaMemcpyHostToDevice),
+                                 "plan rows");
+    }
+    const size_t po = (size_t)p->cap_parts * shape->n_heads * shape->v_dim * sizeof(float);
+    const size_t pm = (size_t)p->cap_parts * shape->n_heads * 4 * sizeof(float);   /* (m, l_lo, l_hi, -) */
     if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->part_o, po), "plan scratch");
     if (!rc) rc = ct__cuda_status(cudaMalloc((void **)&p->part_ml, pm), "plan scratch");
     p->scratch_bytes = po + pm;
-    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->chunks, ch, (size_t)(nc ? nc : 1) * sizeof *ch, cudaMemcpyHostToDevice), "plan upload");
-    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->worker_begin, wb, ((size_t)W + 1) * sizeof(int32_t), cudaMemcpyHostToDevice), "plan upload");
-    if (!rc) rc = ct__cuda_status(cudaMemcpy(p->combines, cb, (size_t)(ncb ? ncb : 1) * sizeof *cb, cudaMemcpyHostToDevice), "plan upload");
-    free(cb);
-    free(ch); free(wb); free(first_chunk); free(n_of);
     if (rc) { ct_mla_plan_destroy(p); return NULL; }
     return p;
-fail:
-    ct__set_error("ct_mla_plan_create: out of memory");
-    free(ch); free(wb); free(first_chunk); free(n_of);
-    free(p->rows_h); free(p->lens_h);
-    free(p);
-    return NULL;
 }
 
 uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p) { return p ? p->n_chunks : 0; }
@@ -265,9 +230,12 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
     if ((plan->dims.kv_dtype == CT_KV_INT8 || plan->dims.kv_dtype == CT_KV_E4M3) && !scales) return CT_ERR_ARG;
     ct_mla_plan_t *p = (ct_mla_plan_t *)plan;
     uint32_t launches = 0;
-    int rc = ct__launch_mla_decode(&p->dims, p->chunks, p->n_chunks, p->worker_begin, p->n_workers, p->combines,
-                                   p->n_combines, q, pool, scales, block_table, seq_lens, out, lse, p->part_o,
-                                   p->part_ml, stream, &launches);
+    int rc = ct__launch_mla_plan(p->rows_dev, seq_lens, p->n_seq, p->dims.page_tokens, p->dims.max_pages_per_seq,
+                                 p->n_workers, p->chunks, p->worker_begin, p->combines, p->counts, stream);
+    if (!rc) rc = ct__launch_mla_decode(&p->dims, p->chunks, p->cap_chunks, p->worker_begin, p->n_workers, p->combines,
+                                        p->cap_combines, p->counts, q, pool, scales, block_table, seq_lens, out, lse,
+                                        p->part_o, p->part_ml, stream, &launches);
+    if (!rc) { launches++; ct__count_launches(1); }
     p->last_launches = launches;
     return rc;
 }

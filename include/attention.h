@@ -79,18 +79,24 @@ typedef struct {
     uint32_t n_pages;        /* pages in the pool; block-table entries >= n_pages are skipped */
 } ct_mla_shape_t;
 
-/* A work plan: the split of every sequence's pages into chunks, the chunk
- * order across SMs, and the device scratch for partial results.  Built on
- * the host from the sequence lengths; stays valid while no sequence's page
- * count changes (a token appended inside the last page keeps it valid). */
+/* A work plan: device buffers for the split of every sequence's pages into
+ * chunks across the SMs, and the scratch for partial results of sequences
+ * that are split.  Each ct_attn_mla_decode_paged first recomputes the split
+ * on the device from the CURRENT device lengths (pages laid end to end, the
+ * same number of pages per worker), so one plan serves any lengths up to
+ * max_pages_per_seq pages: a serving loop whose sequences grow reuses it,
+ * without host planning or allocation, and a whole step can be replayed as
+ * one CUDA graph. */
 typedef struct ct_mla_plan ct_mla_plan_t;
 
 /* seq_rows (host, may be NULL = 0..n_seq-1): block-table row of each output
- * sequence.  seq_lens_host: tokens each sequence attends. */
+ * sequence.  seq_lens_host: the sequences' lengths now (checked against
+ * max_pages_per_seq; ct_mla_plan_chunks reports their split). */
 ct_mla_plan_t *ct_mla_plan_create(const ct_mla_shape_t *shape, const uint32_t *seq_rows,
                                   const int32_t *seq_lens_host, uint32_t n_seq, int device);
 void   ct_mla_plan_destroy(ct_mla_plan_t *p);
-/* Number of work chunks and the split-KV scratch bytes the plan holds. */
+/* Number of work chunks the creation lengths split into, and the split-KV
+ * scratch bytes the plan holds (sized for any lengths). */
 uint32_t ct_mla_plan_chunks(const ct_mla_plan_t *p);
 /* Workers the plan balances over, and whether it runs the tensor-core kernel
  * (1: 128 heads x 576 bf16 entries x 64-token pages on sm_100; 0: the
@@ -109,7 +115,8 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
                              const float *scales, const int32_t *block_table,
                              const int32_t *seq_lens, void *out, float *lse, void *stream);
 
-/* Number of kernel launches the last ct_attn_mla_decode_paged issued. */
+/* Number of kernel launches the last ct_attn_mla_decode_paged issued
+ * (planning, decode, and the combine when a sequence was split). */
 uint32_t ct_mla_plan_launches(const ct_mla_plan_t *p);
 
 /* Error word of the tensor-core MLA kernel on the current device: 0 when no

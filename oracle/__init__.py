@@ -129,6 +129,8 @@ def build() -> None:
         # the reference's unit tests linked against this repository's library
         if (HERE.parent / "cautreo_b200" / "libcautreo_b200.so").exists():
             subprocess.run(["make", "-s", "-C", str(HERE), "ours-tests"], check=True)
+            # the reference engine's transformer forward, against either KV cache
+            subprocess.run(["make", "-s", "-C", str(HERE), "engine"], check=True)
 
 
 def _load(path, sigs):

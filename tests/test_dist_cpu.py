@@ -74,3 +74,29 @@ def test_rank_with_no_sequences():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert np.array_equal(got[:, 0], np.array([3, 10], np.int16))
+
+
+# ---- the C-ABI NCCL backend: what runs without a GPU -------------------------
+
+def test_nccl_unique_id_and_reference_contexts():
+    """ct_dist_nccl_unique_id makes a fresh 128-byte id (NCCL's bootstrap
+    needs no GPU); contexts from ct_dist_init keep the reference's
+    single-process behaviour and refuse the NCCL gathers."""
+    import ctypes as C
+    import cautreo_b200 as ct
+    a, b = ct.nccl_unique_id(), ct.nccl_unique_id()
+    assert len(a) == 128 and a != b
+    L = ct.lib()
+    cfg = ct.DistConfig(0, 2, 1, None)
+    h = L.ct_dist_init(C.byref(cfg))
+    try:
+        assert L.ct_dist_n_devices(h) == 2 and L.ct_dist_device_id(h) == 1 and not L.ct_dist_is_leader(h)
+        x = (C.c_float * 4)(1, 2, 3, 4)
+        assert L.ct_dist_allreduce(h, x, 4) and list(x) == [1, 2, 3, 4]     # identity, as the reference
+        assert L.ct_dist_gather_rows(h, None, 0, 16, None, 0, None, None) == ct.CT_ERR_ARG
+        st = ct.DistStats()
+        assert L.ct_dist_gather_stats(h, C.byref(st), None) == ct.CT_ERR_ARG
+    finally:
+        L.ct_dist_destroy(h)
+    bad = ct.DistConfig(0, 2, 2, None)                                    # rank beyond the world
+    assert not L.ct_dist_init_nccl(C.byref(bad), (C.c_uint8 * 128)(), 0)

@@ -37,30 +37,17 @@ def no_expired_waits():
 
 def split_sequences(lens, workers, page=PAGE):
     """Sequences the work plan cuts across workers: the sequences' pages laid
-    end to end, worker w takes about total/W tokens, cuts on page
-    boundaries (the planner's balancing rule)."""
-    lens = [int(n) for n in lens]
-    total = sum(lens)
-    quota = total // workers + 1
-    parts = [0] * len(lens)
-    w, filled = 0, 0
-    for s, n in enumerate(lens):
-        pages = (n + page - 1) // page
-        pg = 0
-        if pages == 0:
-            parts[s] = 1
-        while pg < pages:
-            room = max(quota - filled, 0)
-            take = max((room + page // 2) // page, 1)
-            if w + 1 >= workers or take > pages - pg:
-                take = pages - pg
-            parts[s] += 1
-            tok = take * page if pg + take < pages else n - pg * page
-            pg += take
-            filled += tok
-            if filled + page // 2 >= quota and w + 1 < workers:
-                w, filled = w + 1, 0
-    return [s for s, p in enumerate(parts) if p > 1]
+    end to end, worker w takes the pages [w*Q, (w+1)*Q) with
+    Q = ceil(total / workers) (the planning kernel's rule)."""
+    pages = [(int(n) + page - 1) // page for n in lens]
+    total = sum(pages)
+    q = max(1, -(-total // workers))
+    out, cp = [], 0
+    for s, n in enumerate(pages):
+        if n and (cp + n - 1) // q != cp // q:
+            out.append(s)
+        cp += n
+    return out
 
 
 def gather_subset(pool_dev, bt, lens, subset, page=PAGE, E=MLA_E):

@@ -238,6 +238,26 @@ def test_mla_many_short_sequences(zero_q):
     assert ok, (mx, rel)
 
 
+def test_mla_plan_follows_device_lengths():
+    """A plan splits the work on the device from the lengths it is given at
+    each decode: the same plan decodes sequences that grew (new pages), that
+    shrank, and that became empty, as a serving loop reuses one plan."""
+    cap = [3000, 700, 64, 5000, 1]
+    pool, bt, q = mla_case(cap, seed=41)
+    plan = ct.MlaPlan(np.array([10, 10, 10, 10, 10], np.int32), pool.shape[0], max_pages_per_seq=bt.shape[1])
+    pd, qd, btd = dev(pool), dev(q), dev(bt)
+    for lens in ([10, 10, 10, 10, 1], [2999, 65, 64, 4097, 0], [3000, 700, 64, 5000, 1], [1, 0, 63, 129, 1]):
+        lens = np.array(lens, np.int32)
+        ld = dev(lens)
+        out = empty((len(lens), MLA_H, MLA_DV), np.uint16)
+        plan.decode(qd.data_ptr(), pd.data_ptr(), None, btd.data_ptr(), ld.data_ptr(), out.data_ptr(), None, stream())
+        got = oracle.bf16_to_f32(host(out, np.uint16)).reshape(len(lens), MLA_H, MLA_DV)
+        want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+        ok, mx, rel = close(got, want)
+        assert ok, (lens.tolist(), mx, rel)
+        assert np.all(got[lens == 0] == 0)
+
+
 def test_mla_through_paged_handle():
     """Append through ct_kv_paged_append, then decode the handle's pool."""
     S, E = 3, MLA_E

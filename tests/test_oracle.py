@@ -321,3 +321,24 @@ def test_lpt_balances():
         load = np.bincount(r, weights=lens, minlength=R_)
         assert load.max() - load.min() <= lens.max()
         assert load.max() / load.mean() < 1.01
+
+
+def test_reference_engine_runs_on_the_tiny_gguf(tmp_path):
+    """The reference engine's transformer forward (compiled from the
+    reference sources with oracle/engine_drive.c) loads the synthetic GGUF
+    and decodes; its logits are finite and repeat run to run."""
+    import subprocess
+    from engine_gguf import write_tiny_llama
+    exe = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "engine_ref"
+    if not exe.exists():
+        pytest.skip("engine_ref not built (needs the reference sources at build time)")
+    cfg = write_tiny_llama(tmp_path / "tiny.gguf")
+    runs = []
+    for i in range(2):
+        out = tmp_path / f"l{i}.bin"
+        r = subprocess.run([str(exe), str(tmp_path / "tiny.gguf"), "12", str(out)], capture_output=True, text=True,
+                           timeout=120)
+        assert r.returncode == 0, r.stderr
+        runs.append(np.fromfile(out, np.float32).reshape(12, cfg["n_vocab"]))
+    assert np.isfinite(runs[0]).all() and runs[0].std() > 0.1
+    assert np.array_equal(runs[0], runs[1])
