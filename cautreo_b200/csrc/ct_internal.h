@@ -173,8 +173,15 @@ template <int Type> struct CtBlock {
     static constexpr int kBytes = Type == 1 ? 34 : Type == 2 ? 18 : Type == 3 ? 10 : 6;
 };
 
+/* The reference converts floorf(v) with a C (int) cast, which on x86-64
+ * (cvttss2si) gives INT_MIN for NaN and for values outside the int range;
+ * the clamp then turns INT_MIN into -lim.  So v NaN or >= 2^31 codes -lim
+ * here too (a CUDA cast would give 0 for NaN and saturate at INT_MAX), and
+ * v < -2^31 saturates to INT_MIN, also -lim. */
 CT_DEV int ct_block_code(float x, float id, int lim) {
-    int q = (int)floorf(__fadd_rn(__fmul_rn(x, id), 0.5f));
+    const float v = __fadd_rn(__fmul_rn(x, id), 0.5f);
+    if (!(v < 2147483648.0f)) return -lim;
+    const int q = (int)floorf(v);
     return q > lim ? lim : (q < -lim ? -lim : q);
 }
 

@@ -351,101 +351,109 @@ __global__ void __launch_bounds__(256) k_gather_batch(const void *pool, const fl
     gather_token<PoolDtype, OutBf16, MaxChunks>(pool, scales, slot, dim, static_cast<uint8_t *>(out) + out_elt);
 }
 
-/* K1b / K3c: block-quantised pools.  A CTA takes a tile of `tile` tokens
- * and spreads its (token, block) pairs over all 256 threads; the tile's
- * entries are staged in shared memory ([tile][entry bytes]) so that they
- * move to or from HBM as consecutive 4-byte words (2-byte words when an
- * entry is an odd number of them), and every thread reads or writes whole
- * 64-byte (bf16) / 128-byte (fp32) runs of values. */
+/* K1b / K3c: block-quantised pools (Q8_0 / Q4_0 / Q2_0 / Q1_0).
+ * Append: a CTA takes a tile of up to 64 consecutive source tokens; a thread
+ * encodes a whole block (32 values, so the per-block scale arithmetic is
+ * paid once per 32 values) and loads its next block while it encodes this
+ * one, and several CTAs per SM keep the loads in flight.  The tile's entries
+ * are built in shared memory and go out as 16-byte vectors when its slots
+ * are consecutive.
+ * Gather: persistent CTAs (four per SM) stride over runs of one page's
+ * entries, double-buffered in shared memory with cp.async, so the copy of
+ * the next run is in flight while one is decoded; a block is decoded by kL
+ * adjacent lanes (4 for bf16 output, 8 for fp32), each storing its values as
+ * one 16-byte vector, so a warp writes 512 consecutive bytes per
+ * instruction. */
 constexpr int kMaxBlocks = 128;                 /* dim <= 4096 */
-constexpr uint32_t kBlkSmem = 48 * 1024;        /* stage bytes per CTA */
+constexpr uint32_t kBlkOut = 48 * 1024;         /* append: entry bytes of a tile */
+constexpr uint32_t kBlkStage = 18 * 1024;       /* gather: code bytes per buffer */
+constexpr int kBlkCtasPerSm = 4;                /* gather */
 
-__host__ __device__ inline uint32_t block_tile(uint32_t eb) {
-    const uint32_t t = kBlkSmem / eb;
-    return t > 64 ? 64 : (t < 1 ? 1 : t);
+/* Tokens per tile or item: the largest power of two whose bytes fit the
+ * budget (1..64), so that a tile of a 64-token page never straddles two
+ * pages. */
+__host__ __device__ inline uint32_t blk_tile(uint32_t bytes_per_token, uint32_t budget) {
+    uint32_t t = budget / bytes_per_token;
+    t = t > 64 ? 64 : (t < 1 ? 1 : t);
+    while (t & (t - 1)) t &= t - 1;
+    return t;
 }
 
-/* Blocks in shared memory are 2-byte aligned (34 / 18 / 10 / 6 bytes each):
- * they are read and written as 16-bit halves, the codes as whole 32-bit
- * words in registers. */
-template <int Type> struct BlockWords {
-    static constexpr int kCodeWords = (CtBlock<Type>::kBytes - 2) / 4;     /* 8 / 4 / 2 / 1 */
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+/* every group of this thread except the newest has landed */
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+/* max that propagates NaN (IEEE maximum, not maxNum) */
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
+template <int Type> struct BlockCode {
+    static constexpr int kBits = Type == CT_QUANT_Q8_0 ? 8 : Type == CT_QUANT_Q4_0 ? 4 : Type == CT_QUANT_Q2_0 ? 2 : 1;
+    static constexpr int kMax = Type == CT_QUANT_Q8_0 ? 127 : Type == CT_QUANT_Q4_0 ? 7 : 1;
 };
 
-/* The 32 values of one block, exactly ct_block_decode's (code x d in fp32,
- * exact: at most 8 + 11 significant bits).  A code becomes a float by adding
- * it to the bits of 1.5 * 2^23 and subtracting that again, which keeps the
- * work on the integer and fma pipes. */
+/* One block's fp16 scale and packed codes, ct_block_encode's bit for bit,
+ * into blk (2-byte aligned, shared memory).  Fast path: the block's |x|
+ * maximum, taken NaN-propagating, is finite, and d = amax / qmax is 0 or a
+ * normal float.  Then |x id| <= qmax (1 + 2^-22), so floor(x id + 0.5) lies
+ * in [-qmax, qmax] without a clamp, and the floor is taken by adding
+ * 1.5 * 2^23 (plus 1 for Q2_0's code + 1) rounding down: the low bits of that
+ * sum are the two's-complement code.  Otherwise (a NaN, an Inf, a subnormal
+ * scale) every value goes through ct_block_code, and the maximum skips NaNs
+ * as the reference's does. */
 template <int Type>
-__device__ __forceinline__ void block_decode_smem(const uint8_t *blk, float *x) {
-    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
-    const float d = ct_ref_fp16_to_f32(h[0]);
-    constexpr int kW = BlockWords<Type>::kCodeWords;
-    uint32_t w[kW];
-    #pragma unroll
-    for (int j = 0; j < kW; j++) w[j] = (uint32_t)h[1 + 2 * j] | ((uint32_t)h[2 + 2 * j] << 16);
-    #pragma unroll
-    for (int i = 0; i < 32; i++) {
-        float f;
-        if (Type == CT_QUANT_Q8_0) {
-            const int v = (int)(int8_t)(uint8_t)(w[i >> 2] >> (8 * (i & 3)));
-            f = __int_as_float(0x4B400000 + v) - 12582912.0f;
-        } else if (Type == CT_QUANT_Q4_0) {
-            const uint32_t u = ((w[i >> 3] >> (4 * (i & 7))) & 0xFu) ^ 8u;     /* two's complement nibble + 8 */
-            f = __uint_as_float(0x4B400000u | u) - 12582920.0f;
-        } else if (Type == CT_QUANT_Q2_0) {
-            const uint32_t u = (w[i >> 4] >> (2 * (i & 15))) & 3u;           /* code + 1 */
-            f = __uint_as_float(0x4B400000u | u) - 12582913.0f;
-        } else {
-            x[i] = (w[0] >> i) & 1u ? d : -d;
-            continue;
-        }
-        x[i] = __fmul_rn(f, d);
-    }
-}
-
-/* One block's fp16 scale and codes, ct_block_encode's, into shared memory. */
-template <int Type>
-__device__ __forceinline__ void block_encode_smem(const float *x, uint8_t *blk) {
+__device__ __forceinline__ void block_encode_thread(const float *x, uint8_t *blk) {
+    constexpr int kW = (CtBlock<Type>::kBytes - 2) / 4;
     uint16_t *h = reinterpret_cast<uint16_t *>(blk);
     float amax = 0.0f;
     #pragma unroll
-    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(x[i]));
-    constexpr int kW = BlockWords<Type>::kCodeWords;
+    for (int i = 0; i < 32; i++) amax = fmax_nan(amax, fabsf(x[i]));
+    const bool finite = amax <= 3.40282347e38f;                /* false for NaN and Inf */
+    if (amax != amax) {
+        amax = 0.0f;
+        #pragma unroll
+        for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(x[i]));
+    }
     uint32_t w[kW];
     if (Type == CT_QUANT_Q1_0) {
         h[0] = ct_ref_f32_to_fp16(amax);
         uint32_t bits = 0;
         #pragma unroll
-        for (int i = 0; i < 32; i++) bits |= (x[i] >= 0 ? 1u : 0u) << i;
+        for (int i = 0; i < 32; i++) bits |= (x[i] >= 0.0f ? 1u : 0u) << i;
         w[0] = bits;
     } else {
-        constexpr int qm = Type == CT_QUANT_Q8_0 ? 127 : Type == CT_QUANT_Q4_0 ? 7 : 1;
+        constexpr int qm = BlockCode<Type>::kMax;
+        constexpr float magic = Type == CT_QUANT_Q2_0 ? 12582913.0f : 12582912.0f;
         const float d = __fdiv_rn(amax, (float)qm);
         h[0] = ct_ref_f32_to_fp16(d);
         const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        int q[32];
-        #pragma unroll
-        for (int i = 0; i < 32; i++) q[i] = max(-qm, min(qm, __float2int_rd(__fadd_rn(__fmul_rn(x[i], id), 0.5f))));
+        uint32_t r[32];
+        if (finite && (d == 0.0f || d >= 1.17549435e-38f)) {
+            #pragma unroll
+            for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__fadd_rd(__fadd_rn(__fmul_rn(x[i], id), 0.5f), magic));
+        } else {
+            #pragma unroll
+            for (int i = 0; i < 32; i++) r[i] = (uint32_t)(ct_block_code(x[i], id, qm) + (Type == CT_QUANT_Q2_0 ? 1 : 0));
+        }
         if (Type == CT_QUANT_Q8_0) {
             #pragma unroll
             for (int j = 0; j < kW; j++)
-                w[j] = __byte_perm(__byte_perm(q[4 * j], q[4 * j + 1], 0x0040), __byte_perm(q[4 * j + 2], q[4 * j + 3], 0x0040),
+                w[j] = __byte_perm(__byte_perm(r[4 * j], r[4 * j + 1], 0x0040), __byte_perm(r[4 * j + 2], r[4 * j + 3], 0x0040),
                                    0x5410);
-        } else if (Type == CT_QUANT_Q4_0) {
-            #pragma unroll
-            for (int j = 0; j < kW; j++) {
-                uint32_t v = 0;
-                #pragma unroll
-                for (int k = 0; k < 8; k++) v |= ((uint32_t)q[8 * j + k] & 0xFu) << (4 * k);
-                w[j] = v;
-            }
         } else {
+            constexpr int cb = BlockCode<Type>::kBits, per = 32 / cb;
             #pragma unroll
             for (int j = 0; j < kW; j++) {
                 uint32_t v = 0;
                 #pragma unroll
-                for (int k = 0; k < 16; k++) v |= ((uint32_t)(q[16 * j + k] + 1) & 3u) << (2 * k);
+                for (int k = 0; k < per; k++) v |= (r[per * j + k] & ((1u << cb) - 1u)) << (cb * k);
                 w[j] = v;
             }
         }
@@ -457,19 +465,80 @@ __device__ __forceinline__ void block_encode_smem(const float *x, uint8_t *blk) 
     }
 }
 
-/* The 32 source values of block b of token tok, as raw 16-byte vectors. */
+/* Lane q's kV values of a block in shared memory, ct_block_decode's exactly
+ * (code x d in fp32, exact: at most 8 + 11 significant bits).  A code becomes
+ * a float by placing it, offset to be non-negative, in the low bits of
+ * 1.5 * 2^23 (one byte permute for Q8_0) and subtracting that float's base;
+ * Q1_0 sets d's sign from the bit.  No conversion instructions. */
+template <int Type, int kV>
+__device__ __forceinline__ void block_decode_lane(const uint8_t *blk, uint32_t q, float *x) {
+    constexpr int cb = BlockCode<Type>::kBits, LB = kV * cb;    /* this lane's code bits */
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
+    const float d = ct_ref_fp16_to_f32(h[0]);
+    uint32_t w0, w1 = 0;
+    if (LB == 64) {
+        const uint16_t *c = h + 1 + 4 * q;
+        w0 = (uint32_t)c[0] | ((uint32_t)c[1] << 16);
+        w1 = (uint32_t)c[2] | ((uint32_t)c[3] << 16);
+    } else if (LB == 32) {
+        const uint16_t *c = h + 1 + 2 * q;
+        w0 = (uint32_t)c[0] | ((uint32_t)c[1] << 16);
+    } else if (LB == 16) {
+        w0 = h[1 + q];
+    } else {
+        constexpr uint32_t S = LB < 16 ? 16 / LB : 1;
+        w0 = (uint32_t)h[1 + q / S] >> ((q % S) * LB);
+    }
+    #pragma unroll
+    for (int i = 0; i < kV; i++) {
+        if (Type == CT_QUANT_Q1_0) {
+            x[i] = __uint_as_float(__float_as_uint(d) ^ ((((w0 >> i) & 1u) ^ 1u) << 31));
+            continue;
+        }
+        float f;
+        if (Type == CT_QUANT_Q8_0)
+            f = __uint_as_float(__byte_perm((i < 4 ? w0 : w1) ^ 0x80808080u, 0x4B400000u, 0x7650u + (i & 3))) - 12583040.0f;
+        else if (Type == CT_QUANT_Q4_0)
+            f = __uint_as_float((((w0 >> (4 * i)) & 0xFu) ^ 8u) | 0x4B400000u) - 12582920.0f;
+        else
+            f = __uint_as_float(((w0 >> (2 * i)) & 3u) | 0x4B400000u) - 12582913.0f;
+        x[i] = __fmul_rn(f, d);
+    }
+}
+
+int blk_sm_count() {
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] <= 0) {
+        int c = 0;
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+        cached[dev] = c;
+    }
+    return cached[dev];
+}
+
+/* The 32 source values of one block as raw 16-byte vectors (bf16: 4, fp32:
+ * 8), from a 16-byte aligned source, or with 2-byte loads from one that is
+ * not. */
 template <bool SrcBf16>
 struct BlockSrc {
-    uint4 v[SrcBf16 ? 4 : 8];
-    __device__ __forceinline__ void load(const void *src, size_t tok, uint32_t dim, uint32_t b) {
-        const uint4 *q = SrcBf16 ? reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + tok * dim + b * 32)
-                                 : reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + tok * dim + b * 32);
-        #pragma unroll
-        for (int i = 0; i < (SrcBf16 ? 4 : 8); i++) v[i] = __ldcs(q + i);
+    static constexpr int kVec = SrcBf16 ? 4 : 8;
+    uint4 v[kVec];
+    template <bool Aligned>
+    __device__ __forceinline__ void load(const uint8_t *q) {
+        if (Aligned) {
+            #pragma unroll
+            for (int i = 0; i < kVec; i++) v[i] = __ldcs(reinterpret_cast<const uint4 *>(q) + i);
+        } else {
+            uint16_t *h = reinterpret_cast<uint16_t *>(v);
+            #pragma unroll
+            for (int i = 0; i < 8 * kVec; i++) h[i] = __ldcs(reinterpret_cast<const unsigned short *>(q) + i);
+        }
     }
     __device__ __forceinline__ void values(float *x) const {
         #pragma unroll
-        for (int i = 0; i < (SrcBf16 ? 4 : 8); i++) {
+        for (int i = 0; i < kVec; i++) {
             const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
             #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -484,32 +553,58 @@ struct BlockSrc {
     }
 };
 
-/* A CTA takes `tile` consecutive source tokens; threads take (token, block)
- * pairs (many CTAs per SM keep the loads in flight). */
-template <bool SrcBf16, int Type>
-__global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void *src, const int32_t *dest,
-                                                      uint32_t n, uint32_t dim, uint32_t tile) {
+/* Append: tokens [tile x, tile x + tile) of the source, whose blocks are
+ * back to back (64 or 128 bytes each).  When the tile's slots are
+ * consecutive (a run of one page, the usual bulk append) its entries are one
+ * byte run of the pool: they are encoded into shared memory at the run's
+ * offset modulo 16 and stored as 16-byte vectors (2-byte pieces at the two
+ * ragged ends); otherwise each token's entry is stored as 4- or 2-byte
+ * words.  Tokens with a negative slot are skipped. */
+template <bool SrcBf16, int Type, bool Aligned>
+__global__ void __launch_bounds__(256, 4) k_write_blocks(uint8_t *pool, const void *src, const int32_t *dest, uint32_t n,
+                                                      uint32_t dim, uint32_t tile) {
     constexpr int kB = CtBlock<Type>::kBytes;
-    extern __shared__ __align__(16) uint8_t stage[];
+    constexpr uint32_t kBlkBytes = SrcBf16 ? 64 : 128;
+    extern __shared__ __align__(16) uint8_t outs[];            /* tile * eb + 16 bytes */
     const uint32_t nb = dim / 32, eb = nb * kB;
-    const uint32_t t0 = blockIdx.x * tile, cnt = min(tile, n - t0);
-    for (uint32_t p = threadIdx.x; p < cnt * nb; p += 256) {
-        const uint32_t t = p / nb, b = p - t * nb;
-        if (dest[t0 + t] < 0) continue;
-        BlockSrc<SrcBf16> in;
-        in.load(src, t0 + t, dim, b);
+    const uint32_t t0 = blockIdx.x * tile, cnt = min(tile, n - t0), nblk = cnt * nb;
+    const uint8_t *s8 = static_cast<const uint8_t *>(src) + (size_t)t0 * nb * kBlkBytes;
+    BlockSrc<SrcBf16> cur;
+    if (threadIdx.x < nblk) cur.template load<Aligned>(s8 + (size_t)threadIdx.x * kBlkBytes);
+    const uint32_t d0 = (uint32_t)dest[t0];
+    const bool mine = threadIdx.x >= cnt || (uint32_t)dest[t0 + threadIdx.x] == d0 + threadIdx.x;
+    const bool contig = __syncthreads_and(mine) && (int32_t)d0 >= 0 && ((uintptr_t)pool & 15) == 0;
+    const size_t g0 = contig ? (size_t)d0 * eb : 0;
+    const uint32_t mis = (uint32_t)(g0 & 15);                   /* even: eb is */
+    for (uint32_t p = threadIdx.x; p < nblk; p += 256) {
         float x[32];
-        in.values(x);
-        block_encode_smem<Type>(x, stage + t * eb + b * kB);
+        if (!SrcBf16 && p != threadIdx.x) cur.template load<Aligned>(s8 + (size_t)p * kBlkBytes);
+        cur.values(x);
+        /* bf16: the next block's 64 bytes are in flight during this encode
+         * (fp32 sources, 128 bytes a block, would not fit the registers) */
+        if (SrcBf16 && p + 256 < nblk) cur.template load<Aligned>(s8 + (size_t)(p + 256) * kBlkBytes);
+        block_encode_thread<Type>(x, outs + mis + p * kB);
     }
     __syncthreads();
-    if ((eb & 3) == 0) {
+    if (contig) {
+        const uint32_t end = mis + cnt * eb, nv = (end + 15) / 16;
+        uint8_t *g = pool + (g0 - mis);
+        for (uint32_t v = threadIdx.x; v < nv; v += 256) {
+            const uint32_t a = 16 * v;
+            if (a >= mis && a + 16 <= end) {
+                *reinterpret_cast<uint4 *>(g + a) = *reinterpret_cast<const uint4 *>(outs + a);
+            } else {
+                for (uint32_t c = max(a, mis); c < min(a + 16, end); c += 2)
+                    *reinterpret_cast<uint16_t *>(g + c) = *reinterpret_cast<const uint16_t *>(outs + c);
+            }
+        }
+    } else if ((eb & 3) == 0) {
         const uint32_t W = eb / 4;
         for (uint32_t p = threadIdx.x; p < cnt * W; p += 256) {
             const uint32_t t = p / W, w = p - t * W;
             const int32_t slot = dest[t0 + t];
             if (slot >= 0)
-                reinterpret_cast<uint32_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint32_t *>(stage + t * eb)[w];
+                reinterpret_cast<uint32_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint32_t *>(outs + t * eb)[w];
         }
     } else {
         const uint32_t W = eb / 2;
@@ -517,92 +612,123 @@ __global__ void __launch_bounds__(256) k_write_blocks(uint8_t *pool, const void 
             const uint32_t t = p / W, w = p - t * W;
             const int32_t slot = dest[t0 + t];
             if (slot >= 0)
-                reinterpret_cast<uint16_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint16_t *>(stage + t * eb)[w];
+                reinterpret_cast<uint16_t *>(pool + (size_t)slot * eb)[w] = reinterpret_cast<const uint16_t *>(outs + t * eb)[w];
         }
     }
 }
 
-/* Tokens [start, start+n) of one sequence (desc == nullptr), or of desc[y]
- * = (seq, start, count, first output row) for blockIdx.y.  A CTA takes
- * `tile` consecutive tokens of one page: x = page index within the range x
- * tiles per page + tile within the page.  Those entries are one contiguous
- * run of the page, copied to shared memory as 16-byte vectors (rounded out
- * to 16-byte boundaries inside the page), four in flight per thread. */
+/* One gather item: tokens [lo, hi) of one page, at most `tile` of them. */
+struct BlkItem {
+    const uint8_t *page;
+    uint32_t lo, hi, a, nvec, off;
+    size_t row0;
+};
+
+/* Gather: tokens [start, start+n) of one sequence (desc == nullptr), or of
+ * desc[y] = (seq, start, count, first output row) for each y.  Item i =
+ * (y, x): x = page index within the range x tiles per page + tile within the
+ * page, items_x of them per y.  An item's entries are one contiguous run of
+ * its page, copied as 16-byte vectors (rounded out to 16-byte boundaries
+ * inside the page); each lane then decodes its kV values and stores them as
+ * one 16-byte vector of the output row. */
 template <int Type, bool OutBf16>
-__global__ void __launch_bounds__(256) k_gather_blocks(const uint8_t *pool, const int32_t *bt, uint32_t max_pages,
-                                                       uint32_t page_tokens, uint32_t dim, uint32_t start, uint32_t n,
-                                                       const int4 *desc, void *out, uint32_t tile) {
-    constexpr int kB = CtBlock<Type>::kBytes;
-    extern __shared__ __align__(16) uint8_t stage[];
-    const uint32_t nb = dim / 32, eb = nb * kB, P = page_tokens;
-    const int32_t *bt_row = bt;
-    size_t row0 = 0;
-    if (desc) {
-        const int4 d = desc[blockIdx.y];
-        bt_row = bt + (size_t)d.x * max_pages;
-        start = (uint32_t)d.y;
-        n = (uint32_t)d.z;
-        row0 = (uint32_t)d.w;
-    }
-    if (n == 0) return;
-    const uint32_t per_page = (P + tile - 1) / tile;
-    const uint32_t lp = start / P + blockIdx.x / per_page;
-    const uint32_t sub = blockIdx.x % per_page;
-    const uint32_t lo = max(start, lp * P + sub * tile);
-    const uint32_t hi = min(min(start + n, lp * P + P), lp * P + sub * tile + tile);
-    if (lo >= hi) return;
-    const uint8_t *page = pool + (size_t)bt_row[lp] * P * eb;
-    const uint32_t b_lo = (lo - lp * P) * eb, b_hi = (hi - lp * P) * eb;
-    const uint32_t a = b_lo & ~15u, nvec = (((b_hi + 15u) & ~15u) - a) / 16;
-    const uint4 *src = reinterpret_cast<const uint4 *>(page + a);
-    uint4 *dst = reinterpret_cast<uint4 *>(stage);
-    for (uint32_t v0 = threadIdx.x; v0 < nvec; v0 += 4 * 256) {
-        uint4 r[4];
-        #pragma unroll
-        for (int k = 0; k < 4; k++)
-            if (v0 + 256 * k < nvec) r[k] = __ldcs(src + v0 + 256 * k);
-        #pragma unroll
-        for (int k = 0; k < 4; k++)
-            if (v0 + 256 * k < nvec) dst[v0 + 256 * k] = r[k];
-    }
-    __syncthreads();
-    const uint32_t cnt = hi - lo, off = b_lo - a;
-    row0 += lo - start;
-    for (uint32_t p = threadIdx.x; p < cnt * nb; p += 256) {
-        const uint32_t t = p / nb, b = p - t * nb;
-        float x[32];
-        block_decode_smem<Type>(stage + off + t * eb + b * kB, x);
-        uint8_t *orow = static_cast<uint8_t *>(out) + (row0 + t) * dim * (OutBf16 ? 2 : 4);
-        if (OutBf16) {
-            uint4 *q = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(orow) + b * 32);
-            #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                uint32_t o[4];
-                #pragma unroll
-                for (int j = 0; j < 4; j++) o[j] = bf16x2_rn(x[8 * i + 2 * j], x[8 * i + 2 * j + 1]);
-                __stcs(q + i, make_uint4(o[0], o[1], o[2], o[3]));
+__global__ void __launch_bounds__(256, kBlkCtasPerSm) k_gather_blocks(const uint8_t *pool, const int32_t *bt,
+                                                                      uint32_t max_pages, uint32_t page_tokens,
+                                                                      uint32_t dim, uint32_t start, uint32_t n,
+                                                                      const int4 *desc, uint64_t items_x,
+                                                                      uint64_t n_items, void *out, uint32_t tile) {
+    constexpr int kB = CtBlock<Type>::kBytes, kL = OutBf16 ? 4 : 8, kV = 32 / kL;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const uint32_t nb = dim / 32, eb = nb * kB, P = page_tokens, per_page = (P + tile - 1) / tile;
+    const uint32_t stage = (tile * eb + 32 + 15) & ~15u;
+    auto find = [&](uint64_t i, BlkItem &w) -> uint64_t {
+        for (; i < n_items; i += gridDim.x) {
+            const uint64_t y = i / items_x;
+            const uint32_t x = (uint32_t)(i - y * items_x);
+            const int32_t *bt_row = bt;
+            uint32_t s0 = start, cn = n;
+            size_t r0 = 0;
+            if (desc) {
+                const int4 d = desc[y];
+                bt_row = bt + (size_t)d.x * max_pages;
+                s0 = (uint32_t)d.y;
+                cn = (uint32_t)d.z;
+                r0 = (uint32_t)d.w;
             }
-        } else {
-            float4 *q = reinterpret_cast<float4 *>(reinterpret_cast<float *>(orow) + b * 32);
-            #pragma unroll
-            for (int i = 0; i < 8; i++) __stcs(q + i, make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
+            if (cn == 0) continue;
+            const uint32_t lp = s0 / P + x / per_page, sub = x % per_page;
+            const uint32_t lo = max(s0, lp * P + sub * tile);
+            const uint32_t hi = min(min(s0 + cn, lp * P + P), lp * P + sub * tile + tile);
+            if (lo >= hi) continue;
+            const uint32_t b_lo = (lo - lp * P) * eb, b_hi = (hi - lp * P) * eb;
+            w.page = pool + (size_t)bt_row[lp] * P * eb;
+            w.a = b_lo & ~15u;
+            w.nvec = (((b_hi + 15u) & ~15u) - w.a) / 16;
+            w.off = b_lo - w.a;
+            w.lo = lo;
+            w.hi = hi;
+            w.row0 = r0 + (lo - s0);
+            return i;
         }
+        return n_items;
+    };
+    auto issue = [&](const BlkItem &w, uint8_t *buf) {
+        const uint8_t *s = w.page + w.a;
+        for (uint32_t v = threadIdx.x; v < w.nvec; v += 256) cp_async16(buf + 16 * v, s + 16 * v);
+    };
+    BlkItem cur, nxt;
+    uint64_t i = find(blockIdx.x, cur);
+    if (i < n_items) issue(cur, smem);
+    cp_async_commit();
+    for (uint32_t k = 0; i < n_items; k++) {
+        const uint64_t j = find(i + gridDim.x, nxt);
+        if (j < n_items) issue(nxt, smem + ((k + 1) & 1) * stage);
+        cp_async_commit();
+        cp_async_wait_prev();
+        __syncthreads();
+        const uint8_t *buf = smem + (k & 1) * stage + cur.off;
+        const uint32_t units = (cur.hi - cur.lo) * nb * kL;
+        const size_t e0 = cur.row0 * dim;
+        for (uint32_t u = threadIdx.x; u < units; u += 256) {
+            const uint32_t blk = u / kL, q = u % kL;
+            float x[kV];
+            block_decode_lane<Type, kV>(buf + blk * kB, q, x);
+            const size_t e = e0 + (size_t)blk * 32 + q * kV;    /* token t, block b: t dim + 32 b = 32 blk */
+            if (OutBf16) {
+                __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + e),
+                       make_uint4(bf16x2_rn(x[0], x[1]), bf16x2_rn(x[2], x[3]), bf16x2_rn(x[4], x[5]),
+                                  bf16x2_rn(x[6], x[7])));
+            } else {
+                __stcs(reinterpret_cast<float4 *>(static_cast<float *>(out) + e), make_float4(x[0], x[1], x[2], x[3]));
+            }
+        }
+        __syncthreads();                          /* this buffer is refilled next */
+        cur = nxt;
+        i = j;
     }
+}
+
+template <bool SrcBf16, int Type>
+void launch_write_blocks_t(uint8_t *pool, const void *src, const int32_t *dest, uint32_t n, uint32_t dim,
+                           cudaStream_t st) {
+    const uint32_t eb = dim / 32 * CtBlock<Type>::kBytes, tile = blk_tile(eb, kBlkOut);
+    const int grid = (int)((n + tile - 1) / tile);
+    const size_t sm = (size_t)tile * eb + 16;
+    if (((uintptr_t)src & 15) == 0)
+        k_write_blocks<SrcBf16, Type, true><<<grid, 256, sm, st>>>(pool, src, dest, n, dim, tile);
+    else
+        k_write_blocks<SrcBf16, Type, false><<<grid, 256, sm, st>>>(pool, src, dest, n, dim, tile);
 }
 
 template <bool SrcBf16>
 int launch_write_blocks(uint32_t type, void *pool, const void *src, const int32_t *dest, uint32_t n, uint32_t dim,
                         cudaStream_t st) {
-    static const uint32_t kB[4] = {34, 18, 10, 6};
-    const uint32_t eb = dim / 32 * kB[type - CT_KV_Q8_0], tile = block_tile(eb);
-    const int blocks = (int)((n + tile - 1) / tile);
-    const size_t sm = (size_t)tile * eb;
     uint8_t *p = static_cast<uint8_t *>(pool);
     switch (type) {
-        case CT_KV_Q8_0: k_write_blocks<SrcBf16, CT_QUANT_Q8_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
-        case CT_KV_Q4_0: k_write_blocks<SrcBf16, CT_QUANT_Q4_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
-        case CT_KV_Q2_0: k_write_blocks<SrcBf16, CT_QUANT_Q2_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
-        default:         k_write_blocks<SrcBf16, CT_QUANT_Q1_0><<<blocks, 256, sm, st>>>(p, src, dest, n, dim, tile); break;
+        case CT_KV_Q8_0: launch_write_blocks_t<SrcBf16, CT_QUANT_Q8_0>(p, src, dest, n, dim, st); break;
+        case CT_KV_Q4_0: launch_write_blocks_t<SrcBf16, CT_QUANT_Q4_0>(p, src, dest, n, dim, st); break;
+        case CT_KV_Q2_0: launch_write_blocks_t<SrcBf16, CT_QUANT_Q2_0>(p, src, dest, n, dim, st); break;
+        default:         launch_write_blocks_t<SrcBf16, CT_QUANT_Q1_0>(p, src, dest, n, dim, st); break;
     }
     ct__count_launches(1);
     return ct__cuda_status(cudaGetLastError(), "write_slots");
@@ -611,14 +737,16 @@ int launch_write_blocks(uint32_t type, void *pool, const void *src, const int32_
 template <int Type>
 void launch_gather_blocks(bool ob, const void *pool, const int32_t *bt, uint32_t maxp, uint32_t P, uint32_t dim,
                           uint32_t start, uint32_t n, const int4 *desc, uint32_t n_desc, void *out, cudaStream_t st) {
-    const uint32_t eb = dim / 32 * CtBlock<Type>::kBytes, tile = block_tile(eb + 32);
+    const uint32_t eb = dim / 32 * CtBlock<Type>::kBytes, tile = blk_tile(eb, kBlkStage);
     const uint32_t per_page = (P + tile - 1) / tile;
     /* n tokens starting anywhere in a page span at most n / P + 2 pages */
-    const dim3 grid((n / P + 2) * per_page, desc ? n_desc : 1);
-    const size_t sm = (size_t)tile * eb + 32;
+    const uint64_t items_x = (uint64_t)(n / P + 2) * per_page, n_items = items_x * (desc ? n_desc : 1);
+    const uint64_t cap = (uint64_t)blk_sm_count() * kBlkCtasPerSm;
+    const int grid = (int)(n_items < cap ? n_items : cap);
+    const size_t sm = 2 * (size_t)((tile * eb + 32 + 15) & ~15u);
     const uint8_t *p = static_cast<const uint8_t *>(pool);
-    if (ob) k_gather_blocks<Type, true><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, out, tile);
-    else    k_gather_blocks<Type, false><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, out, tile);
+    if (ob) k_gather_blocks<Type, true><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, items_x, n_items, out, tile);
+    else    k_gather_blocks<Type, false><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, items_x, n_items, out, tile);
 }
 
 /* K3t: the gathers from bf16 / int8 / e4m3 pools for entries of at most 576

@@ -186,38 +186,86 @@ __global__ void __launch_bounds__(256) k_mla_simt(ct_mla_dims_t dims, const ct_m
  * row sums l_i of the value dims below and above v_dim / 2 -- the two SMs of
  * a tensor-core worker each normalise their half of the dims by their own
  * sum) merge as o = sum_i 2^(m_i - M) o_i / sum_i 2^(m_i - M) l_i.  Entries
- * of part_ml are (m, l_lo, l_hi, unused). */
-__global__ void __launch_bounds__(128) k_mla_combine(const ct_mla_combine_t *items, const int32_t *counts, uint32_t H,
-                                                     uint32_t Dv, const float *part_o, const float *part_ml,
-                                                     uint16_t *out, float *lse) {
+ * of part_ml are (m, l_lo, l_hi, unused).  Block = one combine item x 4
+ * heads, a warp per head: the lanes reduce M and L over the parts, then each
+ * lane accumulates its value dims over the parts in part order (v_dim a
+ * multiple of 128: four consecutive dims per 128, as 16-byte loads, all of a
+ * part's loads issued before its FMAs). */
+constexpr int kCombineHeads = 4;
+
+__global__ void __launch_bounds__(32 * kCombineHeads) k_mla_combine(const ct_mla_combine_t *items,
+                                                                   const int32_t *counts, uint32_t H, uint32_t Dv,
+                                                                   const float *part_o, const float *part_ml,
+                                                                   uint16_t *out, float *lse) {
     if (counts && (int32_t)blockIdx.x >= counts[1]) return;       /* beyond the planned combines */
     const ct_mla_combine_t it = items[blockIdx.x];
-    const uint32_t h = blockIdx.y;
+    const uint32_t lane = threadIdx.x & 31, h = blockIdx.y * kCombineHeads + (threadIdx.x >> 5);
+    if (h >= H) return;
     float M = -INFINITY;
-    for (int i = 0; i < it.n_parts; i++) {
+    for (int i = (int)lane; i < it.n_parts; i += 32) {
         const size_t ph = (size_t)(it.first_part + i) * H + h;
         if (part_ml[4 * ph + 1] > 0.0f) M = fmaxf(M, part_ml[4 * ph]);
     }
+    #pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    /* the row sums in part order, as one thread would add them */
     float L[2] = {0.0f, 0.0f};
     for (int i = 0; i < it.n_parts; i++) {
         const size_t ph = (size_t)(it.first_part + i) * H + h;
-        if (part_ml[4 * ph + 1] > 0.0f) {
-            const float w = exp2f(part_ml[4 * ph] - M);
-            L[0] += w * part_ml[4 * ph + 1];
-            L[1] += w * part_ml[4 * ph + 2];
+        const float4 ml = *reinterpret_cast<const float4 *>(part_ml + 4 * ph);
+        if (ml.y > 0.0f) {
+            const float w = exp2f(ml.x - M);
+            L[0] += w * ml.y;
+            L[1] += w * ml.z;
         }
     }
     const float inv[2] = {L[0] > 0.0f ? 1.0f / L[0] : 0.0f, L[1] > 0.0f ? 1.0f / L[1] : 0.0f};
     const size_t oh = (size_t)it.seq * H + h;
-    for (uint32_t d = threadIdx.x; d < Dv; d += blockDim.x) {
-        float o = 0.0f;
+    if ((Dv & 127) == 0 && Dv <= 512) {
+        const uint32_t slabs = Dv / 128;
+        float4 acc[4];
+        #pragma unroll
+        for (int k = 0; k < 4; k++) acc[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int i = 0; i < it.n_parts; i++) {
             const size_t ph = (size_t)(it.first_part + i) * H + h;
-            if (part_ml[4 * ph + 1] > 0.0f) o = fmaf(exp2f(part_ml[4 * ph] - M), part_o[ph * Dv + d], o);
+            const float4 ml = *reinterpret_cast<const float4 *>(part_ml + 4 * ph);
+            if (!(ml.y > 0.0f)) continue;
+            const float w = exp2f(ml.x - M);
+            const float4 *po = reinterpret_cast<const float4 *>(part_o + ph * Dv) + lane;
+            float4 v[4];
+            #pragma unroll
+            for (int k = 0; k < 4; k++)
+                if ((uint32_t)k < slabs) v[k] = __ldcs(po + 32 * k);
+            #pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if ((uint32_t)k >= slabs) continue;
+                acc[k].x = fmaf(w, v[k].x, acc[k].x);
+                acc[k].y = fmaf(w, v[k].y, acc[k].y);
+                acc[k].z = fmaf(w, v[k].z, acc[k].z);
+                acc[k].w = fmaf(w, v[k].w, acc[k].w);
+            }
         }
-        out[oh * Dv + d] = ct_f32_to_bf16(o * inv[d >= Dv / 2]);
+        #pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if ((uint32_t)k >= slabs) continue;
+            const uint32_t d = 128 * k + 4 * lane;
+            const float s = d >= Dv / 2 ? inv[1] : inv[0];          /* Dv / 2 is a multiple of 4 */
+            uint2 pk;
+            pk.x = (uint32_t)ct_f32_to_bf16(acc[k].x * s) | ((uint32_t)ct_f32_to_bf16(acc[k].y * s) << 16);
+            pk.y = (uint32_t)ct_f32_to_bf16(acc[k].z * s) | ((uint32_t)ct_f32_to_bf16(acc[k].w * s) << 16);
+            *reinterpret_cast<uint2 *>(out + oh * Dv + d) = pk;
+        }
+    } else {
+        for (uint32_t d = lane; d < Dv; d += 32) {
+            float o = 0.0f;
+            for (int i = 0; i < it.n_parts; i++) {
+                const size_t ph = (size_t)(it.first_part + i) * H + h;
+                if (part_ml[4 * ph + 1] > 0.0f) o = fmaf(exp2f(part_ml[4 * ph] - M), part_o[ph * Dv + d], o);
+            }
+            out[oh * Dv + d] = ct_f32_to_bf16(o * (d >= Dv / 2 ? inv[1] : inv[0]));
+        }
     }
-    if (lse && threadIdx.x == 0) lse[oh] = L[0] > 0.0f ? M * kLn2 + logf(L[0]) : -INFINITY;
+    if (lse && lane == 0) lse[oh] = L[0] > 0.0f ? M * kLn2 + logf(L[0]) : -INFINITY;
 }
 
 /* Declared in mla_tc.cu: the tcgen05 kernel for H=128, E=576, Dv=512, P=64,
@@ -266,7 +314,8 @@ extern "C" int ct__launch_mla_decode(const ct_mla_dims_t *dims, const ct_mla_chu
         launches++;
     }
     if (n_combines > 0) {
-        k_mla_combine<<<dim3(n_combines, dims->n_heads), 128, 0, st>>>(
+        k_mla_combine<<<dim3(n_combines, (dims->n_heads + kCombineHeads - 1) / kCombineHeads), 32 * kCombineHeads, 0,
+                        st>>>(
             combines, counts, dims->n_heads, dims->v_dim, part_o, part_ml, static_cast<uint16_t *>(out), lse);
         int rc = ct__cuda_status(cudaGetLastError(), "mla_combine");
         if (rc != CT_OK) return rc;

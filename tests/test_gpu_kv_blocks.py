@@ -139,6 +139,67 @@ def test_block_pool_gather_batch_and_odd_word_entries(pool_dtype):
         h.close()
 
 
+def edge_entries(n, E, seed):
+    """N(0,1) tokens with NaN, +-Inf, subnormal, zero, -0 and near-FLT_MAX
+    values planted in some of them."""
+    x = oracle.normal_f32(oracle.key(seed, 40), 0, n * E, 100, 20.0).reshape(n, E)
+    x[1] *= 1e-39                       # subnormal block maxima: 1 / d overflows to Inf
+    x[2, 5] = np.nan
+    x[2, 32 + 3] = np.inf
+    x[2, 64 + 7] = -np.inf
+    x[2, 96:128] = 3.0e38               # d = amax / qmax overflows the fp16 scale
+    x[3] = 0.0
+    x[4] = -0.0
+    x[5, :16] = np.nan
+    x[6, :32] = np.nan                  # an all-NaN block
+    return x
+
+
+@pytest.mark.parametrize("pool_dtype", BLOCKS)
+@pytest.mark.parametrize("src", ["bf16", "f32"])
+def test_block_write_slots_edge_values_and_layouts(pool_dtype, src):
+    """ct_kv_paged_write_slots into a block pool: slots in reverse order with a
+    stride, from a source that is not 16-byte aligned (per-token stores, 2-byte
+    staging), then one contiguous run from an odd slot (16-byte stores from an
+    offset that is not a multiple of 16).  The tokens hold NaN, +-Inf,
+    subnormal, zero and -0 values: the reference's (int)floorf(...) of a NaN or
+    out-of-range value is INT_MIN on x86-64, which its clamp turns into -qmax,
+    and every stored byte must equal the reference's.  Then an append and the
+    gathers of those tokens equal the reference's decode (NaN positions
+    excepted, as in same_f32 / same_bf16)."""
+    P, E, NP, n = 64, 576, 4, 40
+    L = ct.lib()
+    x = edge_entries(n, E, 45)
+    if src == "bf16":
+        raw = oracle.f32_to_bf16(x).reshape(n, E)
+        xf, elt, sdt = oracle.bf16_to_f32(raw).reshape(n, E), 2, ct.CT_KV_BF16
+    else:
+        raw, xf, elt, sdt = x, x, 4, ct.CT_KV_F32
+    eb = ct.entry_bytes(pool_dtype, E)
+    want = ref_encode(pool_dtype, xf)
+    pad = np.zeros(16 // elt, raw.dtype)
+    shifted = dev(np.concatenate([pad[:1], raw.reshape(-1), pad]))
+    aligned = dev(raw)
+    h = ct.PagedKV(1, NP, NP, P, E, 0, pool_dtype, 0, stream())
+    for dest, src_ptr in ((5 + 3 * np.arange(n)[::-1], shifted.data_ptr() + elt),
+                          (131 + np.arange(n), aligned.data_ptr())):
+        d = dev(np.ascontiguousarray(dest, np.int32))
+        ct.check(L.ct_kv_paged_write_slots(h.pool, None, pool_dtype, src_ptr, sdt, d.data_ptr(), n, E, stream()))
+        stored = pool_bytes(h, NP, P, eb)
+        assert np.array_equal(stored[dest], want), (dest[0], "stored blocks")
+    h.close()
+    g = ct.PagedKV(1, NP, NP, P, E, 0, pool_dtype, 0, stream())
+    g.append([0], [n], aligned.data_ptr(), sdt)
+    want_f32 = ref_decode(pool_dtype, want, E)
+    o32 = empty((n, E), np.float32)
+    ct.check(L.ct_kv_paged_gather(g.h, 0, 0, n, o32.data_ptr(), ct.CT_KV_F32))
+    assert same_f32(host(o32, np.float32), want_f32)
+    o16 = empty((n, E), np.uint16)
+    ct.check(L.ct_kv_paged_gather(g.h, 0, 0, n, o16.data_ptr(), ct.CT_KV_BF16))
+    assert same_bf16(host(o16, np.uint16), want_f32)
+    g.close()
+
+
 def test_block_pool_checkpoint_fork_compaction(tmp_path):
     """Q2_0 pool: a checkpoint restores the bytes, a fork shares the full
     pages and copies the partial one, compaction keeps every gather."""
