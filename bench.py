@@ -893,6 +893,141 @@ def run_produce(args):
             "paths": res}
 
 
+def run_aux(args):
+    """The library's secondary kernels, each on inputs larger than L2 (one
+    launch per step, CUDA events on the launching stream), for the launch
+    list and DRAM bytes of every kernel that the other workloads do not
+    reach: entries longer than 768 values appended (k_write_slots), gathers
+    from an fp32 pool (k_gather, k_gather_batch), the CUDA-core MLA decode of
+    a 16-head shape (k_mla_simt), the reference block and per-token codecs
+    on device buffers (k_quant_blocks, k_dequant_blocks, k_quant_tokens,
+    k_dequant_tokens), the reference attention and softmax contracts
+    (k_attn_shared, k_softmax), ct_kv_compress (k_compress_*) and the row
+    scatter of the multi-GPU gather (k_scatter_rows, through a one-rank NCCL
+    context)."""
+    import torch
+    import cautreo_b200 as ct
+    L = ct.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    res = {}
+
+    def timed(name, fn, nbytes, reps=None):
+        reps = reps or args.steps
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch, 2)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
+
+    # entries of 1024 values, bf16 -> int8 + scale (one warp per token), 131,072 tokens
+    n, D = 131072, 1024
+    src = torch.zeros(n * D, dtype=torch.int16, device="cuda")
+    codes = torch.empty(n * D, dtype=torch.int8, device="cuda")
+    scl = torch.empty(n, dtype=torch.float32, device="cuda")
+    dest = torch.arange(n, dtype=torch.int32, device="cuda")
+    timed("k_write_slots bf16 -> int8, 1024 values x 131072", lambda: ct.check(L.ct_kv_paged_write_slots(
+        codes.data_ptr(), scl.data_ptr(), ct.CT_KV_INT8, src.data_ptr(), ct.CT_KV_BF16, dest.data_ptr(), n, D, sp)),
+        n * (2 * D + D + 4))
+    del src, codes, scl, dest
+    # fp32 pool gathers: 65,536 tokens of 576 values
+    n = 65536
+    kv = ct.PagedKV(2, n // PAGE, n // PAGE, PAGE, E, 0, ct.CT_KV_F32, 0, sp)
+    kv.append([0, 1], [n // 2, n // 2], None)
+    out = torch.empty(n * E, dtype=torch.float32, device="cuda")
+    timed("k_gather f32 pool -> f32, 32768 tokens", lambda: ct.check(L.ct_kv_paged_gather(
+        kv.h, 0, 0, n // 2, out.data_ptr(), ct.CT_KV_F32)), (n // 2) * E * 8)
+    g_seqs, g_starts, g_counts = np.array([0, 1], np.uint32), np.zeros(2, np.uint32), np.full(2, n // 2, np.uint32)
+    timed("k_gather_batch f32 pool -> f32, 2 x 32768 tokens", lambda: ct.check(L.ct_kv_paged_gather_batch(
+        kv.h, g_seqs.ctypes.data, g_starts.ctypes.data, g_counts.ctypes.data, 2, out.data_ptr(), ct.CT_KV_F32)),
+        n * E * 8)
+    kv.close()
+    del out
+    # CUDA-core MLA decode, 16 heads (a shape the tensor-core kernel does not take): 32 x 4096 tokens
+    S, T, Hs = 32, 4096, 16
+    pages = S * T // PAGE
+    pool = torch.zeros(pages * PAGE * E, dtype=torch.int16, device="cuda")
+    bt = torch.arange(pages, dtype=torch.int32, device="cuda")
+    lens = torch.full((S,), T, dtype=torch.int32, device="cuda")
+    q = torch.zeros(S * Hs * E, dtype=torch.int16, device="cuda")
+    o = torch.empty(S * Hs * DV, dtype=torch.int16, device="cuda")
+    plan = ct.MlaPlan(np.full(S, T, np.int32), pages, n_heads=Hs, max_pages_per_seq=T // PAGE)
+    timed("k_mla_simt 16 heads, 32 x 4096 tokens", lambda: plan.decode(
+        q.data_ptr(), pool.data_ptr(), None, bt.data_ptr(), lens.data_ptr(), o.data_ptr(), None, sp),
+        S * T * E * 2 + S * Hs * (E + DV) * 2, reps=max(1, args.steps // 4))
+    plan.close()
+    del pool, bt, lens, q, o
+    # reference block codec Q8_0 and per-token int8 codec on device buffers, 32 M values
+    nv = 32 * 1024 * 1024
+    x = torch.zeros(nv, dtype=torch.float32, device="cuda")
+    blk = torch.empty(nv // 32 * 34, dtype=torch.uint8, device="cuda")
+    timed("k_quant_blocks Q8_0, 32 M values", lambda: ct.check(L.ct_quant_q8_0_dev(x.data_ptr(), blk.data_ptr(), nv, sp)),
+          nv * 4 + nv // 32 * 34)
+    timed("k_dequant_blocks Q8_0, 32 M values", lambda: ct.check(L.ct_dequant_q8_0_dev(blk.data_ptr(), x.data_ptr(), nv,
+                                                                                         sp)), nv * 4 + nv // 32 * 34)
+    del blk
+    n_tok = nv // E
+    c8 = torch.empty(n_tok * E, dtype=torch.int8, device="cuda")
+    sc = torch.empty(n_tok, dtype=torch.float32, device="cuda")
+    timed("k_quant_tokens int8 from fp32, 58254 x 576", lambda: ct.check(L.ct_quant_kv_int8(
+        x.data_ptr(), 0, n_tok, E, c8.data_ptr(), sc.data_ptr(), sp)), n_tok * (E * 4 + E + 4))
+    timed("k_dequant_tokens int8 to fp32, 58254 x 576", lambda: ct.check(L.ct_dequant_kv_int8(
+        c8.data_ptr(), sc.data_ptr(), n_tok, E, x.data_ptr(), sp)), n_tok * (E * 4 + E + 4))
+    del x, c8, sc
+    # the reference attention contract (host buffers in and out; the kernel reads K and V once)
+    nt, hh, hd = 262144, 8, 128
+    qh = np.zeros(hh * hd, np.float32)
+    kh = np.zeros(nt * hd, np.float32)
+    vh = np.zeros(nt * hd, np.float32)
+    oh = np.zeros(hh * hd, np.float32)
+    for _ in range(2):
+        if not L.ct_attn_forward(qh.ctypes.data, kh.ctypes.data, vh.ctypes.data, nt, hh, hd, 0.0, oh.ctypes.data):
+            raise RuntimeError("ct_attn_forward")
+    sm = np.zeros(16 * 1024 * 1024, np.float32)
+    for _ in range(2):
+        L.ct_attn_softmax(sm.ctypes.data, sm.size)
+    res["k_attn_shared, k_softmax"] = {"note": "host-buffer reference contracts (ct_attn_forward 262144 tokens x 8 "
+                                                "heads x 128, ct_attn_softmax 16 M values); see the launch list"}
+    del kh, vh, sm
+    # ct_kv_compress: 4 layers x 4096 tokens x 1024 values, every second token kept
+    cache = ct.KvCache(4, 8, 128, 4096)
+    row = np.zeros(1024, np.float32)
+    for layer in range(4):
+        for pos in range(4096):
+            cache.append(layer, pos, row, row)
+    if not L.ct_kv_compress(cache.h, 2.0):
+        raise RuntimeError("ct_kv_compress")
+    res["k_compress_*"] = {"note": "ct_kv_compress, 4 layers x 4096 tokens x 1024 fp32 values (K and V), step 2; "
+                                   "see the launch list"}
+    cache.close()
+    # row scatter of the multi-GPU gather, one rank: 1024 rows of 128 KB
+    ctx = ct.NcclContext(0, 1, ct.nccl_unique_id(), 0)
+    nr, rb = 1024, H * DV * 2
+    rows = torch.zeros(nr * rb // 2, dtype=torch.int16, device="cuda")
+    dst = torch.empty(nr * rb // 2, dtype=torch.int16, device="cuda")
+    ids = np.arange(nr, dtype=np.uint32)[::-1].copy()
+    timed("k_scatter_rows 1024 x 128 KB (one-rank gather)", lambda: ctx.gather_rows(
+        rows.data_ptr(), nr, rb, ids, nr, dst.data_ptr(), sp), 2 * nr * rb)
+    ctx.close()
+    hbm, hbm_kind = measured_hbm()
+    for v in res.values():
+        if "gbs" in v:
+            v["frac"] = v["gbs"] / hbm
+    return {"metric": "secondary kernels: GB/s each", "value": None, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "mixed",
+            "data": "zeros (timing and traffic only; parity is in tests/)",
+            "config": {"workload": "one launch per step of each secondary kernel, inputs larger than L2",
+                       "peak": hbm, "peak_kind": hbm_kind},
+            "kernels": res}
+
+
 def run_serve(args):
     """A serving loop whose sequences grow: the sequence-sharded workload's
     1024 sequences (512..65536 tokens, seed 4) take one new token each per
@@ -1052,7 +1187,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="sharded",
-                    choices=["sharded", "mla32", "plain", "quant", "evict", "produce", "serve"])
+                    choices=["sharded", "mla32", "plain", "quant", "evict", "produce", "serve", "aux"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="enqueue each step's launches from the host")
@@ -1060,11 +1195,11 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
 
-    if args.workload in ("plain", "quant", "evict", "produce", "serve"):
+    if args.workload in ("plain", "quant", "evict", "produce", "serve", "aux"):
         if int(os.environ.get("RANK", "0")) != 0 or args.impl == "reference":
             return 0          # one-GPU measurements of the other configurations
         line = {"plain": run_plain, "quant": run_quant, "evict": run_evict, "produce": run_produce,
-                "serve": run_serve}[args.workload](args)
+                "serve": run_serve, "aux": run_aux}[args.workload](args)
         print(json.dumps(line), flush=True)
         return 0
 

@@ -75,11 +75,21 @@ int ct__launch_kv_compress(float *k, float *v, float *scratch, uint32_t n_layers
 
 int ct__launch_q_blocks(int type, const float *x, void *blocks, int64_t n, void *stream);
 int ct__launch_deq_blocks(int type, const void *blocks, float *x, int64_t n, void *stream);
+/* The same on the paged cache's kernels (kv_kernels.cu); CT_ERR_UNSUPPORTED
+ * when the shape or alignment does not suit them. */
+int ct__launch_encode_blocks(int type, const float *x, void *blocks, int64_t n, void *stream);
+int ct__launch_decode_blocks(int type, const void *blocks, float *x, int64_t n, void *stream);
+int ct__launch_quant_tokens(int int8, const void *x, int src_is_bf16, uint32_t n_tok, uint32_t dim, void *codes,
+                            float *scales, void *stream);
 
+/* ct_attn_forward / ct_attn_softmax on device buffers; scratch of the size
+ * the _scratch_bytes functions give (long inputs run split over CTAs). */
+size_t ct__attn_scratch_bytes(uint32_t n_tokens, uint32_t n_heads, uint32_t head_dim);
 int ct__launch_attn_shared(const float *q, const float *k, const float *v, uint32_t n_tokens,
                            uint32_t n_heads, uint32_t head_dim, float scale, float *out,
-                           float *scratch_scores, void *stream);
-int ct__launch_softmax(float *x, uint32_t n, void *stream);
+                           float *scratch, void *stream);
+size_t ct__softmax_scratch_bytes(uint32_t n);
+int ct__launch_softmax(float *x, uint32_t n, void *scratch, void *stream);
 /* dst[ids[i]] = src[i] for n rows of row_bytes (a multiple of 4). */
 int ct__launch_scatter_rows(void *dst, const void *src, const uint32_t *ids, uint32_t n, size_t row_bytes,
                             void *stream);

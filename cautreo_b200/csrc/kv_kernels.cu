@@ -23,6 +23,8 @@
 #include "../../include/quant.h"
 #include "ct_internal.h"
 
+#include <algorithm>
+
 namespace {
 
 constexpr int kWarps = 8;          /* tokens per 256-thread block */
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(256) k_write_slots(void *pool, float *scales, 
     const uint32_t warp = blockIdx.x * kWarps + (threadIdx.x >> 5);
     const uint32_t lane = threadIdx.x & 31;
     if (warp >= n) return;
-    const int32_t slot = dest[warp];
+    const int32_t slot = dest ? dest[warp] : (int32_t)warp;      /* no dest: slot = token */
     if (slot < 0) return;
     const uint32_t n_chunks = dim / 16;
     Chunk<SrcBf16> v[MaxChunks];
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(256) k_write_grouped(void *pool, float *scales
                                                        const int32_t *dest, uint32_t n, uint32_t dim) {
     const uint32_t g = threadIdx.x & 7;
     const uint32_t tok = blockIdx.x * 32 + (threadIdx.x >> 3);
-    const int32_t slot = tok < n ? dest[tok] : -1;
+    const int32_t slot = tok < n ? (dest ? dest[tok] : (int32_t)tok) : -1;   /* no dest: slot = token */
     const uint32_t n_units = dim / 8;
     constexpr int kW = SrcBf16 ? 4 : 8;                 /* source words per unit */
     uint32_t w[UPL][kW];
@@ -365,7 +367,7 @@ __global__ void __launch_bounds__(256) k_gather_batch(const void *pool, const fl
  * one 16-byte vector, so a warp writes 512 consecutive bytes per
  * instruction. */
 constexpr int kMaxBlocks = 128;                 /* dim <= 4096 */
-constexpr uint32_t kBlkOut = 48 * 1024;         /* append: entry bytes of a tile */
+constexpr uint32_t kBlkOut = 47 * 1024;         /* append: entry bytes of a tile (+16 within 48 KB) */
 constexpr uint32_t kBlkStage = 18 * 1024;       /* gather: code bytes per buffer */
 constexpr int kBlkCtasPerSm = 4;                /* gather */
 
@@ -571,8 +573,9 @@ __global__ void __launch_bounds__(256, 4) k_write_blocks(uint8_t *pool, const vo
     const uint8_t *s8 = static_cast<const uint8_t *>(src) + (size_t)t0 * nb * kBlkBytes;
     BlockSrc<SrcBf16> cur;
     if (threadIdx.x < nblk) cur.template load<Aligned>(s8 + (size_t)threadIdx.x * kBlkBytes);
-    const uint32_t d0 = (uint32_t)dest[t0];
-    const bool mine = threadIdx.x >= cnt || (uint32_t)dest[t0 + threadIdx.x] == d0 + threadIdx.x;
+    /* no dest: the entries go to slots 0, 1, 2, ... */
+    const uint32_t d0 = dest ? (uint32_t)dest[t0] : t0;
+    const bool mine = !dest || threadIdx.x >= cnt || (uint32_t)dest[t0 + threadIdx.x] == d0 + threadIdx.x;
     const bool contig = __syncthreads_and(mine) && (int32_t)d0 >= 0 && ((uintptr_t)pool & 15) == 0;
     const size_t g0 = contig ? (size_t)d0 * eb : 0;
     const uint32_t mis = (uint32_t)(g0 & 15);                   /* even: eb is */
@@ -749,6 +752,23 @@ void launch_gather_blocks(bool ob, const void *pool, const int32_t *bt, uint32_t
     else    k_gather_blocks<Type, false><<<grid, 256, sm, st>>>(p, bt, maxp, P, dim, start, n, desc, items_x, n_items, out, tile);
 }
 
+/* The reference block codecs on flat device arrays (ct_quant_q*_0 /
+ * ct_quant_deq*_0 on the device): decode with eight lanes per block, each
+ * storing its four fp32 values as one 16-byte vector (a warp writes 512
+ * consecutive bytes); the block bytes are read straight from global memory. */
+template <int Type>
+__global__ void __launch_bounds__(256) k_decode_blocks_flat(const uint8_t *src, float *dst, int64_t nb) {
+    constexpr int kB = CtBlock<Type>::kBytes;
+    const int64_t units = nb * 8;
+    for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = u >> 3;
+        const uint32_t q = (uint32_t)(u & 7);
+        float x[4];
+        block_decode_lane<Type, 4>(src + blk * kB, q, x);
+        __stcs(reinterpret_cast<float4 *>(dst + blk * 32 + q * 4), make_float4(x[0], x[1], x[2], x[3]));
+    }
+}
+
 /* K3t: the gathers from bf16 / int8 / e4m3 pools for entries of at most 576
  * values, as CTA tiles of 64 output rows: (row, 16-value chunk) pairs spread
  * evenly over the 256 threads (9 each for 576 values, where a warp per token
@@ -891,6 +911,56 @@ __global__ void k_compress_scalar(float *k, float *v, float *scratch, uint32_t m
 }
 
 }  // namespace
+
+/* Flat block codecs: n fp32 values (a multiple of 32) <-> n / 32 blocks.
+ * The encode runs the append kernel with the blocks as consecutive slots of
+ * "tokens" of up to 128 blocks.  Returns CT_ERR_UNSUPPORTED for arrays of
+ * 2^32 tokens or more (the callers then use their per-block kernels). */
+extern "C" int ct__launch_encode_blocks(int type, const float *x, void *blocks, int64_t n, void *stream) {
+    const int64_t nb = n / 32;
+    if (((uintptr_t)blocks & 15) != 0) return CT_ERR_UNSUPPORTED;      /* the kernel stores 4- and 16-byte words */
+    uint32_t f = 128;
+    while (f > 1 && nb % f) f >>= 1;
+    if (nb / f >= (int64_t)0xFFFFFFFF) return CT_ERR_UNSUPPORTED;
+    const uint32_t dim = 32 * f, n_tok = (uint32_t)(nb / f);
+    if (n_tok == 0) return CT_OK;
+    static const uint32_t kPool[5] = {0, CT_KV_Q8_0, CT_KV_Q4_0, CT_KV_Q2_0, CT_KV_Q1_0};
+    if (type < 1 || type > 4) return CT_ERR_ARG;
+    return launch_write_blocks<false>(kPool[type], blocks, x, nullptr, n_tok, dim, (cudaStream_t)stream);
+}
+
+extern "C" int ct__launch_decode_blocks(int type, const void *blocks, float *x, int64_t n, void *stream) {
+    const int64_t nb = n / 32;
+    if (nb == 0) return CT_OK;
+    if (((uintptr_t)x & 15) != 0 || ((uintptr_t)blocks & 1) != 0) return CT_ERR_UNSUPPORTED;
+    const int grid = (int)std::min<int64_t>((nb * 8 + 255) / 256, (int64_t)148 * 16);
+    const uint8_t *src = static_cast<const uint8_t *>(blocks);
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (type) {
+        case CT_QUANT_Q8_0: k_decode_blocks_flat<CT_QUANT_Q8_0><<<grid, 256, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q4_0: k_decode_blocks_flat<CT_QUANT_Q4_0><<<grid, 256, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q2_0: k_decode_blocks_flat<CT_QUANT_Q2_0><<<grid, 256, 0, st>>>(src, x, nb); break;
+        case CT_QUANT_Q1_0: k_decode_blocks_flat<CT_QUANT_Q1_0><<<grid, 256, 0, st>>>(src, x, nb); break;
+        default: return CT_ERR_ARG;
+    }
+    ct__count_launches(1);
+    return ct__cuda_status(cudaGetLastError(), "decode_blocks");
+}
+
+/* Per-token int8 / e4m3 codes of n_tok consecutive entries (dim a multiple
+ * of 16, at most 2048) into consecutive rows: the append kernels with the
+ * rows as slots. */
+extern "C" int ct__launch_quant_tokens(int int8, const void *x, int src_is_bf16, uint32_t n_tok, uint32_t dim,
+                                       void *codes, float *scales, void *stream) {
+    if (dim % 16 != 0 || dim > 2048) return CT_ERR_UNSUPPORTED;
+    if (n_tok == 0) return CT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (int8)
+        return src_is_bf16 ? launch_write<true, CT_KV_INT8>(codes, scales, x, nullptr, n_tok, dim, st)
+                           : launch_write<false, CT_KV_INT8>(codes, scales, x, nullptr, n_tok, dim, st);
+    return src_is_bf16 ? launch_write<true, CT_KV_E4M3>(codes, scales, x, nullptr, n_tok, dim, st)
+                       : launch_write<false, CT_KV_E4M3>(codes, scales, x, nullptr, n_tok, dim, st);
+}
 
 extern "C" int ct_kv_paged_write_slots(void *pool, float *scales, uint32_t pool_dtype, const void *entries,
                                        uint32_t src_dtype, const int32_t *dest_slot, uint32_t n,
@@ -1052,18 +1122,32 @@ extern "C" int ct__launch_scatter_i32(int32_t *dst, const int32_t *pairs, uint32
 }
 
 /* Gathered rows to their places: dst[ids[i]] = src[i] for n rows of
- * row_bytes (a multiple of 4), a warp per row. */
+ * row_bytes (a multiple of 4).  A warp takes a 4 KB segment of a row (long
+ * rows spread over many warps), its lanes' eight 16-byte loads in flight
+ * before their stores; 4-byte words where the row or a pointer is not
+ * 16-byte aligned. */
 __global__ void k_scatter_rows(uint8_t *dst, const uint8_t *src, const uint32_t *ids, uint32_t n, size_t row_bytes) {
     const uint32_t lane = threadIdx.x & 31;
+    const size_t seg_per_row = (row_bytes + 4095) / 4096, n_seg = (size_t)n * seg_per_row;
     const size_t warps = (size_t)gridDim.x * (blockDim.x / 32);
-    for (size_t r = blockIdx.x * (size_t)(blockDim.x / 32) + (threadIdx.x >> 5); r < n; r += warps) {
-        const uint8_t *s = src + r * row_bytes;
-        uint8_t *d = dst + (size_t)ids[r] * row_bytes;
-        if (row_bytes % 16 == 0 && ((uintptr_t)s & 15) == 0 && ((uintptr_t)d & 15) == 0) {
-            for (size_t i = lane; i < row_bytes / 16; i += 32)
-                reinterpret_cast<uint4 *>(d)[i] = reinterpret_cast<const uint4 *>(s)[i];
+    for (size_t w = blockIdx.x * (size_t)(blockDim.x / 32) + (threadIdx.x >> 5); w < n_seg; w += warps) {
+        const size_t r = w / seg_per_row, off = (w - r * seg_per_row) * 4096;
+        const size_t len = row_bytes - off < 4096 ? row_bytes - off : 4096;
+        const uint8_t *s = src + r * row_bytes + off;
+        uint8_t *d = dst + (size_t)ids[r] * row_bytes + off;
+        if (len % 16 == 0 && ((uintptr_t)s & 15) == 0 && ((uintptr_t)d & 15) == 0) {
+            const uint4 *s4 = reinterpret_cast<const uint4 *>(s);
+            uint4 *d4 = reinterpret_cast<uint4 *>(d);
+            const uint32_t nv = (uint32_t)(len / 16);
+            uint4 v[8];
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (lane + 32u * j < nv) v[j] = __ldcs(s4 + lane + 32 * j);
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (lane + 32u * j < nv) d4[lane + 32 * j] = v[j];
         } else {
-            for (size_t i = lane; i < row_bytes / 4; i += 32)
+            for (size_t i = lane; i < len / 4; i += 32)
                 reinterpret_cast<uint32_t *>(d)[i] = reinterpret_cast<const uint32_t *>(s)[i];
         }
     }
@@ -1073,7 +1157,8 @@ extern "C" int ct__launch_scatter_rows(void *dst, const void *src, const uint32_
                                        void *stream) {
     if (n == 0) return CT_OK;
     if (!dst || !src || !ids || row_bytes % 4 != 0) return CT_ERR_ARG;
-    k_scatter_rows<<<ct__grid_for((size_t)n * 32, 256, 148 * 8), 256, 0, (cudaStream_t)stream>>>(
+    const size_t segs = (size_t)n * ((row_bytes + 4095) / 4096);
+    k_scatter_rows<<<ct__grid_for(segs * 32, 256, 148 * 16), 256, 0, (cudaStream_t)stream>>>(
         static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), ids, n, row_bytes);
     ct__count_launches(1);
     return ct__cuda_status(cudaGetLastError(), "scatter_rows");

@@ -229,7 +229,7 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
                          const CUtensorMap *q_rope, int wbeg, int wend, uint32_t rank) {
     constexpr bool kQuant = KV != CT_KV_BF16;
     const bool leader = (threadIdx.x & 31) == 0;
-    uint32_t g = 0, nq = 0;
+    uint32_t g = 0;
     bool ok = true;
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
@@ -254,18 +254,11 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
             ah_ok = ah.next(apg, antok);
             if (ah_ok) prefetch(apg);
         }
-        /* the rope dims of this CTA's half of Q, once the previous chunk's
-         * GEMM1s are done (the latent dims go to TMEM) */
-        if (leader) {
-            ok = wait_bar(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 1);
-            if (ok) {
-                mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
-                tma_load_2d(c.s + kOffQ, q_rope, 512 + rank * 32, ch.seq * kH, bar(c, B_Q_FULL));
-            }
-        }
-        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        if (!ok) break;
-        nq++;
+        /* the chunk's queries (128 heads x 576 values) into L2, a few tiles
+         * before the staging warps load them; the staging warps also issue
+         * the rope dims' TMA load, so this loop never waits for the previous
+         * chunk's GEMM1s */
+        if (leader) bulk_prefetch_l2(p.q + (size_t)ch.seq * kH * kE, kH * kE * 2);
         do {
             const uint32_t st = g % kStages;
             if (leader) {
@@ -304,10 +297,6 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
         const uint32_t st = last % kStages;
         long long t0 = clock64();
         while (!mbar_try(bar(c, B_KV_FULL + st), (last / kStages) & 1) && clock64() - t0 < kWaitCycles) {}
-    }
-    if (nq) {
-        long long t0 = clock64();
-        while (!mbar_try(bar(c, B_Q_FULL), (nq - 1) & 1) && clock64() - t0 < kWaitCycles) {}
     }
 }
 
@@ -662,7 +651,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
  * quadrant and slot), so that the exchange of tile t+1 runs while tile t is
  * being finished.  The quadrant's out rows are rewritten only after its
  * previous copy has read them (the issuing lane's bulk group). */
-__device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, int wend, uint32_t rank) {
+__device__ void stager(const Ctx &c, const Params &p, const CUtensorMap *q_rope, uint32_t tmem, int wbeg, int wend,
+                       uint32_t rank) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t quad = warp & 3, row = quad * 32 + lane, lane_base = (quad * 32) << 16;
     uint32_t t = 0, nq = 0;
@@ -675,13 +665,26 @@ __device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, i
         if (n == 0) continue;
         /* this CTA's 256 latent dims of the chunk's Q (this thread: head
          * `row`) into TMEM as soon as the previous chunk's GEMM1s are done,
-         * while the softmax warps may still be finishing that chunk */
+         * while the softmax warps may still be finishing that chunk: the
+         * first half is loaded before that wait (the producer prefetched the
+         * chunk's queries into L2), the second half after it; quadrant 0
+         * issues the rope dims' TMA load into shared memory */
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)ch.seq * kH + row) * kE + rank * 256);
+        uint32_t u[32];
+        #pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const uint4 v = __ldg(src + k);
+            u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
+        }
         if (!(ok = wait_warp(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 17))) break;
         tc_fence_after();
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)ch.seq * kH + row) * kE + rank * 256);
+        if (quad == 0 && lane == 0) {
+            mbar_expect_tx(bar(c, B_Q_FULL), kQBytes);
+            tma_load_2d(c.s + kOffQ, q_rope, 512 + rank * 32, ch.seq * kH, bar(c, B_Q_FULL));
+        }
+        tmem_st32(tmem + lane_base + kTmemQ, u);
         #pragma unroll 1
-        for (int q64 = 0; q64 < 4; q64++) {
-            uint32_t u[32];
+        for (int q64 = 1; q64 < 4; q64++) {
             #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const uint4 v = __ldg(src + q64 * 8 + k);
@@ -728,6 +731,11 @@ __device__ void stager(const Ctx &c, const Params &p, uint32_t tmem, int wbeg, i
         if (quad == 0)
             for (uint32_t u = t >= 2 ? t - 2 : 0; u < t && ok; u++)
                 ok = wait_bar(c, bar(c, B_X_EMPTY + (u & 1)), (u >> 1) & 1, true, 20);
+        /* and the last rope load this warp issued has landed */
+        if (quad == 0 && nq) {
+            long long t0 = clock64();
+            while (!mbar_try(bar(c, B_Q_FULL), (nq - 1) & 1) && clock64() - t0 < kWaitCycles) {}
+        }
     }
 }
 
@@ -934,7 +942,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     c.abort = &s_abort;
     const uint32_t warp = threadIdx.x >> 5;
     const int w = blockIdx.x >> 1;
-    const int wbeg = p.worker_begin[w], wend = p.worker_begin[w + 1];
 
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -970,6 +977,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     cluster_sync();                                 /* both CTAs' barriers exist before any remote arrive or copy */
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(c.smem + kOffTmem);
+    const int wbeg = p.worker_begin[w], wend = p.worker_begin[w + 1];
 
     if (warp == 0) {
         producer<KV>(c, p, &kv_lat, &kv_rope, &q_rope, wbeg, wend, rank);
@@ -984,7 +992,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV == CT_KV_BF16 ? k
     } else if (warp < (uint32_t)kFirstStageWarp) {
         softmax_warps<KV>(c, p, tmem, wbeg, wend, rank);
     } else if (warp < (uint32_t)kFirstConvWarp) {
-        stager(c, p, tmem, wbeg, wend, rank);
+        stager(c, p, &q_rope, tmem, wbeg, wend, rank);
     } else if (KV != CT_KV_BF16) {
         converter<KV>(c, p, wbeg, wend);
     }

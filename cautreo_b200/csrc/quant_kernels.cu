@@ -9,7 +9,13 @@
  * operation individually rounded, and decode with the fp16-rounded scale.
  * Block layout: u16 scale followed by the packed codes (34 / 18 / 10 / 6 B).
  *
- * Per-token codecs: one warp per token, absmax by warp shuffle.
+ * The block codecs and the per-token encoders run on the paged cache's
+ * append and gather kernels where the shapes allow (kv_kernels.cu:
+ * ct__launch_encode_blocks / _decode_blocks / _quant_tokens: the same
+ * arithmetic, coalesced); the kernels here cover the rest.
+ *
+ * Per-token codecs: one warp per token, absmax by warp shuffle; decode by
+ * 16-code vectors when the entry is a multiple of 16 codes.
  */
 #include "../../include/hal.h"
 #include "../../include/quant.h"
@@ -61,6 +67,30 @@ __global__ void __launch_bounds__(256) k_quant_tokens(const void *x, uint32_t n_
     if (lane == 0) scales[t] = d;
 }
 
+/* 16 codes (one 16-byte vector) of a token per thread -> four float4. */
+template <bool Int8>
+__global__ void __launch_bounds__(256) k_dequant_tokens16(const uint8_t *codes, const float *scales, uint32_t n_tok,
+                                                          uint32_t dim, float *x) {
+    const uint32_t per = dim / 16;
+    const size_t total = (size_t)n_tok * per;
+    for (size_t c = blockIdx.x * (size_t)blockDim.x + threadIdx.x; c < total; c += (size_t)gridDim.x * blockDim.x) {
+        const float sc = __ldg(scales + (total <= 0xFFFFFFFFu ? (size_t)((uint32_t)c / per) : c / per));
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(codes) + c);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        float4 *o = reinterpret_cast<float4 *>(x) + 4 * c;
+        #pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float f[4];
+            #pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const uint8_t u = (uint8_t)(w[j] >> (8 * b));
+                f[b] = __fmul_rn(Int8 ? (float)(int8_t)u : ct_e4m3_to_f32(u), sc);
+            }
+            __stcs(o + j, make_float4(f[0], f[1], f[2], f[3]));
+        }
+    }
+}
+
 template <bool Int8>
 __global__ void k_dequant_tokens(const uint8_t *codes, const float *scales, uint32_t n_tok, uint32_t dim, float *x) {
     const size_t total = (size_t)n_tok * dim;
@@ -75,6 +105,9 @@ __global__ void k_dequant_tokens(const uint8_t *codes, const float *scales, uint
 
 extern "C" int ct__launch_q_blocks(int type, const float *x, void *blocks, int64_t n, void *stream) {
     if (n <= 0) return CT_OK;
+    if (type < CT_QUANT_Q8_0 || type > CT_QUANT_Q1_0) return CT_ERR_ARG;
+    const int fast = ct__launch_encode_blocks(type, x, blocks, n, stream);
+    if (fast != CT_ERR_UNSUPPORTED) return fast;
     const int64_t nb = n / 32;
     const int grid = ct__grid_for((size_t)nb, 128, 148 * 8);
     cudaStream_t st = (cudaStream_t)stream;
@@ -92,6 +125,9 @@ extern "C" int ct__launch_q_blocks(int type, const float *x, void *blocks, int64
 
 extern "C" int ct__launch_deq_blocks(int type, const void *blocks, float *x, int64_t n, void *stream) {
     if (n <= 0) return CT_OK;
+    if (type < CT_QUANT_Q8_0 || type > CT_QUANT_Q1_0) return CT_ERR_ARG;
+    const int fast = ct__launch_decode_blocks(type, blocks, x, n, stream);
+    if (fast != CT_ERR_UNSUPPORTED) return fast;
     const int64_t nb = n / 32;
     const int grid = ct__grid_for((size_t)nb, 128, 148 * 8);
     cudaStream_t st = (cudaStream_t)stream;
@@ -121,6 +157,11 @@ static int quant_tokens(bool int8, const void *x, int src_is_bf16, uint32_t n_to
                         uint8_t *codes, float *scales, void *stream) {
     if (!x || !codes || !scales || dim == 0) return CT_ERR_ARG;
     if (n_tok == 0) return CT_OK;
+    const bool aligned = ((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 15) == 0;
+    if (aligned) {
+        const int fast = ct__launch_quant_tokens(int8, x, src_is_bf16, n_tok, dim, codes, scales, stream);
+        if (fast != CT_ERR_UNSUPPORTED) return fast;
+    }
     const int grid = (int)((n_tok + 7) / 8);
     cudaStream_t st = (cudaStream_t)stream;
     if (int8) {
@@ -148,6 +189,13 @@ extern "C" int ct_dequant_kv_int8(const int8_t *codes, const float *scales, uint
                                   float *x, void *stream) {
     if (!codes || !scales || !x) return CT_ERR_ARG;
     if ((size_t)n_tok * dim == 0) return CT_OK;
+    if (dim % 16 == 0 && ((uintptr_t)codes & 15) == 0 && ((uintptr_t)x & 15) == 0) {
+        const int g16 = ct__grid_for((size_t)n_tok * (dim / 16), 256, 148 * 16);
+        k_dequant_tokens16<true><<<g16, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint8_t *>(codes), scales,
+                                                                         n_tok, dim, x);
+        ct__count_launches(1);
+        return ct__cuda_status(cudaGetLastError(), "dequant_int8");
+    }
     const int grid = ct__grid_for((size_t)n_tok * dim, 256, 148 * 8);
     k_dequant_tokens<true><<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint8_t *>(codes), scales, n_tok, dim, x);
     ct__count_launches(1);
@@ -158,6 +206,12 @@ extern "C" int ct_dequant_kv_e4m3(const uint8_t *codes, const float *scales, uin
                                   float *x, void *stream) {
     if (!codes || !scales || !x) return CT_ERR_ARG;
     if ((size_t)n_tok * dim == 0) return CT_OK;
+    if (dim % 16 == 0 && ((uintptr_t)codes & 15) == 0 && ((uintptr_t)x & 15) == 0) {
+        const int g16 = ct__grid_for((size_t)n_tok * (dim / 16), 256, 148 * 16);
+        k_dequant_tokens16<false><<<g16, 256, 0, (cudaStream_t)stream>>>(codes, scales, n_tok, dim, x);
+        ct__count_launches(1);
+        return ct__cuda_status(cudaGetLastError(), "dequant_e4m3");
+    }
     const int grid = ct__grid_for((size_t)n_tok * dim, 256, 148 * 8);
     k_dequant_tokens<false><<<grid, 256, 0, (cudaStream_t)stream>>>(codes, scales, n_tok, dim, x);
     ct__count_launches(1);

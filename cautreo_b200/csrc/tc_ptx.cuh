@@ -73,6 +73,10 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, i
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y) : "memory");
 }
+/* L2 prefetch of a contiguous global range (16-B aligned, size a multiple of 16). */
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 /* Bulk copy of this CTA's shared memory into the peer's, completing on the
  * peer's barrier (both peer addresses from mapa). */
 __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {

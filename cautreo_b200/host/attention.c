@@ -35,7 +35,7 @@ bool ct_attn_forward(const float *q, const float *k, const float *v, uint32_t n_
     if (n_kv_heads == 0 || head_dim == 0) return true;
     const size_t qb = (size_t)n_kv_heads * head_dim * sizeof(float);
     const size_t kb = (size_t)n_tokens * head_dim * sizeof(float);
-    const size_t sb = (size_t)n_kv_heads * n_tokens * sizeof(float);
+    const size_t sb = ct__attn_scratch_bytes(n_tokens, n_kv_heads, head_dim);
     char *buf = NULL;
     const size_t total = 2 * qb + 2 * kb + sb;
     if (ct__scratch_alloc((void **)&buf, total, NULL)) return false;
@@ -60,9 +60,11 @@ void ct_attn_softmax(float *x, uint32_t n) {
     if (!x || n == 0) return;
     float *d = NULL;
     const size_t b = (size_t)n * sizeof(float);
-    if (ct__scratch_alloc((void **)&d, b, NULL)) return;
+    const size_t extra = ct__softmax_scratch_bytes(n);
+    if (ct__scratch_alloc((void **)&d, b + extra + 16, NULL)) return;
+    void *sx = (char *)d + ((b + 15) & ~(size_t)15);
     int rc = ct__cuda_status(cudaMemcpyAsync(d, x, b, cudaMemcpyHostToDevice, 0), "ct_attn_softmax");
-    if (!rc) rc = ct__launch_softmax(d, n, NULL);
+    if (!rc) rc = ct__launch_softmax(d, n, sx, NULL);
     if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(x, d, b, cudaMemcpyDeviceToHost, 0), "ct_attn_softmax");
     ct__scratch_free(d, NULL);
     cudaStreamSynchronize(0);

@@ -41,6 +41,39 @@ def test_attn_forward_matches_reference_golden():
     np.testing.assert_allclose(y, g["sm_y"], rtol=ATTN_TOL, atol=1e-9)
 
 
+@pytest.mark.parametrize("n,H,D", [(20000, 4, 64), (5000, 3, 200), (4096, 2, 1)])
+def test_attn_forward_long_contexts_match_reference(n, H, D):
+    """From 4096 tokens ct_attn_forward runs split over many CTAs (per-tile
+    maxima, sums and value sums in fp64, merged per head); the result stays
+    within the tolerance of the reference's own ct_attn_forward."""
+    R, L = oracle.ref(), ct.lib()
+    rng = np.random.default_rng(n * 7 + H * 3 + D)
+    q = rng.standard_normal(H * D).astype(np.float32)
+    k = rng.standard_normal(n * D).astype(np.float32)
+    v = rng.standard_normal(n * D).astype(np.float32)
+    want = np.zeros(H * D, np.float32)
+    got = np.zeros(H * D, np.float32)
+    assert R.ct_attn_forward(q.ctypes.data, k.ctypes.data, v.ctypes.data, n, H, D, 0.0, want.ctypes.data)
+    assert L.ct_attn_forward(q.ctypes.data, k.ctypes.data, v.ctypes.data, n, H, D, 0.0, got.ctypes.data)
+    np.testing.assert_allclose(got, want, rtol=ATTN_TOL, atol=ATTN_TOL)
+
+
+@pytest.mark.parametrize("n", [65536, 300000])
+def test_softmax_long_inputs_match_reference(n):
+    """From 65536 values ct_attn_softmax runs split over many CTAs; also with
+    a NaN after the first value, which the reference's maximum skips but its
+    sum does not (the values are then left unnormalised)."""
+    R, L = oracle.ref(), ct.lib()
+    x = (np.random.default_rng(n).standard_normal(n) * 4).astype(np.float32)
+    for case in (x, np.where(np.arange(n) == 70001 % n, np.float32(np.nan), x).astype(np.float32)):
+        want, got = case.copy(), case.copy()
+        R.ct_attn_softmax(want.ctypes.data, n)
+        L.ct_attn_softmax(got.ctypes.data, n)
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        ok = ~np.isnan(want)
+        np.testing.assert_allclose(got[ok], want[ok], rtol=ATTN_TOL, atol=1e-9)
+
+
 def test_attention_test_known_answers():
     """attention_test.c:17-39 through the device path."""
     L = ct.lib()

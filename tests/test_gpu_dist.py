@@ -72,3 +72,25 @@ def test_nccl_gather_rows_and_stats_two_processes():
         res = json.load(open(outs[0]))
     assert res["rows_ok"]
     assert res["stats"] == res["want_stats"]
+
+
+@pytest.mark.parametrize("row_bytes", [131072, 10244, 100])
+def test_gather_rows_one_rank_places_rows(row_bytes):
+    """A one-rank NCCL context (one GPU): ct_dist_gather_rows places the
+    rank's own rows at their global positions through the scatter kernel;
+    long rows spread over many warps, rows that are not a multiple of 16
+    bytes go as 4-byte words."""
+    import cautreo_b200 as ct
+    from gpu_util import dev, empty, host, stream
+    n = 300
+    ctx = ct.NcclContext(0, 1, ct.nccl_unique_id(), 0)
+    try:
+        src = np.random.default_rng(row_bytes).integers(0, 2**32, n * row_bytes // 4, dtype=np.uint64).astype(np.uint32)
+        ids = np.random.default_rng(row_bytes + 1).permutation(n).astype(np.uint32)
+        out = empty((n * row_bytes // 4,), np.uint32)
+        src_d = dev(src)
+        ctx.gather_rows(src_d.data_ptr(), n, row_bytes, ids, n, out.data_ptr(), stream())
+        got = host(out, np.uint32).reshape(n, row_bytes // 4)
+        assert np.array_equal(got[ids], src.reshape(n, row_bytes // 4))
+    finally:
+        ctx.close()

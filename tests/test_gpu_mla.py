@@ -258,6 +258,50 @@ def test_mla_plan_follows_device_lengths():
         assert np.all(got[lens == 0] == 0)
 
 
+def test_mla_decode_graph_replay_follows_appends():
+    """A serving loop: the decode (plan, decode kernel, combine) is captured
+    once into a CUDA graph; between replays the sequences grow through
+    ct_kv_paged_append, some across page boundaries.  Each replay equals an
+    ordinary decode of the same state, bit for bit."""
+    S, E, NP, MP = 6, MLA_E, 80, 40
+    lens0 = [70, 1, 300, 64, 129, 2000]
+    grow = [1, 63, 1, 1, 64, 5]
+    steps = 3
+    x = oracle.normal_bf16(oracle.key(8, 3), 0, (sum(lens0) + steps * sum(grow)) * E).reshape(-1, E)
+    h = ct.PagedKV(S, MP, NP, PAGE, E, 0, ct.CT_KV_BF16, 0, stream())
+    h.set_free_order(oracle.permutation(oracle.key(8, 4), NP))
+    xd = dev(x)
+    h.append(list(range(S)), lens0, xd.data_ptr(), ct.CT_KV_BF16)
+    qd = dev(oracle.normal_bf16(oracle.key(8, 5), 0, S * MLA_H * E))
+    plan = ct.MlaPlan(np.array(lens0, np.int32), NP, max_pages_per_seq=MP)
+    out_g = empty((S, MLA_H, MLA_DV), np.uint16)
+    out_e = empty((S, MLA_H, MLA_DV), np.uint16)
+    side = torch.cuda.Stream()
+
+    def decode(out, st):
+        plan.decode(qd.data_ptr(), h.pool, None, h.block_table_dev, h.seq_lens_dev, out.data_ptr(), None, st)
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        decode(out_g, side.cuda_stream)                  # first call outside the capture (attributes, maps)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        decode(out_g, side.cuda_stream)
+    off = sum(lens0)
+    for _ in range(steps):
+        h.append(list(range(S)), grow, xd.data_ptr() + off * E * 2, ct.CT_KV_BF16)
+        off += sum(grow)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        decode(out_e, stream())
+        assert np.array_equal(host(out_g, np.uint16), host(out_e, np.uint16))
+    assert h.seq_lens().tolist() == [l + steps * d for l, d in zip(lens0, grow)]
+    del g
+    h.close()
+
+
 def test_mla_through_paged_handle():
     """Append through ct_kv_paged_append, then decode the handle's pool."""
     S, E = 3, MLA_E
