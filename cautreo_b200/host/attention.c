@@ -74,9 +74,9 @@ void ct_attn_softmax(float *x, uint32_t n) {
 
 /* ct_attn_mla_decode_step_host splits a step into up to this many sequence
  * groups, so that the copies of one group overlap the decode of another.
- * Each group costs one more decode launch (~20-30 us of pipeline fill and
- * drain), worth it while the group's copies (~3 MB, ~60 us over PCIe) are
- * longer; so a step gets one group per CT_STEP_GROUP_BYTES of copies. */
+ * Each group costs one more set of decode launches, worth it while the
+ * group's copies (~3 MB, ~60 us over PCIe) are longer than their fill and
+ * drain; so a step gets one group per CT_STEP_GROUP_BYTES of copies. */
 #define CT_STEP_GROUPS 8
 #define CT_STEP_GROUP_BYTES (3u << 20)
 
@@ -102,12 +102,13 @@ struct ct_mla_plan {
     int32_t *lens_h;
     /* ct_attn_mla_decode_step_host's pipeline: sequence groups
      * [group_begin[g], group_begin[g + 1]) with one sub-plan each, a copy-in
-     * and a copy-out stream, and the events that order them. */
+     * and a copy-out stream, a second decode stream for the odd groups, and
+     * the events that order them. */
     uint32_t n_groups;
     uint32_t group_begin[CT_STEP_GROUPS + 1];
     ct_mla_plan_t *group_plan[CT_STEP_GROUPS];
-    cudaStream_t copy_in, copy_out;
-    cudaEvent_t ev_in[CT_STEP_GROUPS], ev_dec[CT_STEP_GROUPS];
+    cudaStream_t copy_in, copy_out, dec2;
+    cudaEvent_t ev_in[CT_STEP_GROUPS], ev_dec[CT_STEP_GROUPS], ev_go, ev_done2;
 };
 
 /* Declared in mla_tc.cu: whether the tensor-core kernel takes these dims on
@@ -124,8 +125,11 @@ void ct_mla_plan_destroy(ct_mla_plan_t *p) {
         if (p->ev_in[g]) cudaEventDestroy(p->ev_in[g]);
         if (p->ev_dec[g]) cudaEventDestroy(p->ev_dec[g]);
     }
+    if (p->ev_go) cudaEventDestroy(p->ev_go);
+    if (p->ev_done2) cudaEventDestroy(p->ev_done2);
     if (p->copy_in) cudaStreamDestroy(p->copy_in);
     if (p->copy_out) cudaStreamDestroy(p->copy_out);
+    if (p->dec2) cudaStreamDestroy(p->dec2);
     free(p->rows_h); free(p->lens_h);
     free(p);
 }
@@ -243,29 +247,44 @@ int ct_attn_mla_decode_paged(const ct_mla_plan_t *plan, const void *q, const voi
 }
 
 /* Split p's sequences into contiguous groups and give each its own plan,
- * copy streams and events.  Called once per plan.  The copy-in of the first
- * group and the copy-out of the last overlap no decode, so those two groups
- * get half the KV tokens of the others: with G groups the cuts fall at
- * (g + 1/2) / (G - 1) of the step's tokens. */
+ * copy streams and events.  Called once per plan.  Nothing overlaps the
+ * copy-in of the first groups or the copy-out of the last ones (the two
+ * decode streams finish their last groups together), so the groups at
+ * either end are smaller: group g of G gets a share of the step's KV tokens
+ * proportional to min(1, 2^(min(g, G-1-g) - 2)), i.e. 1/4, 1/2, 1, ..., 1,
+ * 1/2, 1/4; a group's copy time follows its sequence count, its decode time
+ * its tokens. */
 static int step_host_pipeline(ct_mla_plan_t *p, size_t step_bytes) {
     uint32_t G = (uint32_t)(step_bytes / CT_STEP_GROUP_BYTES);
     if (G > CT_STEP_GROUPS) G = CT_STEP_GROUPS;
     if (G > p->n_seq / 2) G = p->n_seq / 2;             /* at least two sequences a group */
     if (G < 1) G = 1;
+    uint32_t w4[CT_STEP_GROUPS], wsum = 0;             /* weights in quarters */
+    for (uint32_t g = 0; g < G; g++) {
+        const uint32_t e = g < G - 1 - g ? g : G - 1 - g;
+        w4[g] = e >= 2 ? 4 : 1u << e;
+        wsum += w4[g];
+    }
     uint64_t total = 0;
     for (uint32_t s = 0; s < p->n_seq; s++) total += (uint64_t)p->lens_h[s];
     p->group_begin[0] = 0;
-    uint32_t g = 0;
+    uint32_t g = 0, wacc = w4[0];
     uint64_t acc = 0;
     for (uint32_t s = 0; s < p->n_seq && g + 1 < G; s++) {
         acc += (uint64_t)p->lens_h[s];
-        if (acc * 2 * (G - 1) >= total * (2 * g + 1)) p->group_begin[++g] = s + 1;
+        if (acc * wsum >= total * wacc) {               /* group g holds its share of the tokens */
+            p->group_begin[++g] = s + 1;
+            wacc += w4[g];
+        }
     }
     while (g < G) p->group_begin[++g] = p->n_seq;
     p->n_groups = G;
     if (G == 1) return CT_OK;
     int rc = ct__cuda_status(cudaStreamCreateWithFlags(&p->copy_in, cudaStreamNonBlocking), "step_host streams");
     if (!rc) rc = ct__cuda_status(cudaStreamCreateWithFlags(&p->copy_out, cudaStreamNonBlocking), "step_host streams");
+    if (!rc) rc = ct__cuda_status(cudaStreamCreateWithFlags(&p->dec2, cudaStreamNonBlocking), "step_host streams");
+    if (!rc) rc = ct__cuda_status(cudaEventCreateWithFlags(&p->ev_go, cudaEventDisableTiming), "step_host events");
+    if (!rc) rc = ct__cuda_status(cudaEventCreateWithFlags(&p->ev_done2, cudaEventDisableTiming), "step_host events");
     for (g = 0; g < G && !rc; g++) {
         const uint32_t a = p->group_begin[g], b = p->group_begin[g + 1];
         rc = ct__cuda_status(cudaEventCreateWithFlags(&p->ev_in[g], cudaEventDisableTiming), "step_host events");
@@ -316,7 +335,12 @@ int ct_attn_mla_decode_step_host(ct_mla_plan_t *p, const void *q_host, const voi
     /* Groups: the copy-in of group g+1 runs during the decode of group g, and
      * the copy-out of group g during the decode of group g+1.  All new tokens
      * (n_seq x entry_dim bf16, small) are copied and appended before the
-     * first decode, as in the one-group order. */
+     * first decode, as in the one-group order.  The groups' decodes are
+     * independent (own sub-plan, own rows of the staging buffers), so even
+     * groups run on the caller's stream and odd ones on a second stream: the
+     * next group's kernels take the SMs its predecessor's last workers leave,
+     * and the planning and combine launches of one group overlap the decode
+     * of its neighbour. */
     uint32_t launches = 0;
     char *oh = (char *)out_host, *sq = (char *)p->stage_q, *so = (char *)p->stage_o;
     const char *qh = (const char *)q_host;
@@ -331,30 +355,40 @@ int ct_attn_mla_decode_step_host(ct_mla_plan_t *p, const void *q_host, const voi
         if (!rc) rc = ct_kv_paged_write_slots(pool, scales, p->dims.kv_dtype, p->stage_e, CT_KV_BF16, dest_slot,
                                               (uint32_t)n, (uint32_t)E, stream);
     }
+    /* the second decode stream starts after the append (and everything
+     * queued before this call) */
+    if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_go, st), "step_host");
+    if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(p->dec2, p->ev_go, 0), "step_host");
     uint32_t g = 0;
     for (; g < p->n_groups && !rc; g++) {
         const size_t a = p->group_begin[g], m = p->group_begin[g + 1] - a;
         if (m == 0) continue;
+        cudaStream_t sg = (g & 1) ? p->dec2 : st;
         rc = ct__cuda_status(cudaMemcpyAsync(sq + a * qr, qh + a * qr, m * qr, cudaMemcpyHostToDevice, p->copy_in),
                              "step_host q");
         if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_in[g], p->copy_in), "step_host");
-        if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(st, p->ev_in[g], 0), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(sg, p->ev_in[g], 0), "step_host");
         if (!rc) {
             rc = ct_attn_mla_decode_paged(p->group_plan[g], sq + a * qr, pool, scales, block_table, seq_lens,
-                                          so + a * orow, NULL, stream);
+                                          so + a * orow, NULL, (void *)sg);
             launches += p->group_plan[g]->last_launches;
         }
-        if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_dec[g], st), "step_host");
+        if (!rc) rc = ct__cuda_status(cudaEventRecord(p->ev_dec[g], sg), "step_host");
         if (!rc) rc = ct__cuda_status(cudaStreamWaitEvent(p->copy_out, p->ev_dec[g], 0), "step_host");
         if (!rc) rc = ct__cuda_status(cudaMemcpyAsync(oh + a * orow, so + a * orow, m * orow, cudaMemcpyDeviceToHost,
                                                       p->copy_out), "step_host out");
     }
+    /* the caller's stream ends after the second stream's work too */
+    int rj = ct__cuda_status(cudaEventRecord(p->ev_done2, p->dec2), "step_host");
+    if (!rj) rj = ct__cuda_status(cudaStreamWaitEvent(st, p->ev_done2, 0), "step_host");
+    if (!rc) rc = rj;
     p->last_launches = launches;
     /* On an error part of the work may be queued: wait for all of it, so no
      * copy is still reading or writing the caller's buffers on return. */
     int rs = ct__cuda_status(cudaStreamSynchronize(p->copy_in), "step_host sync");
+    int r2 = ct__cuda_status(cudaStreamSynchronize(p->dec2), "step_host sync");
     int rt = ct__cuda_status(cudaStreamSynchronize(st), "step_host sync");
     int ro = ct__cuda_status(cudaStreamSynchronize(p->copy_out), "step_host sync");
-    if (!rc) rc = rs ? rs : rt ? rt : ro;
+    if (!rc) rc = rs ? rs : r2 ? r2 : rt ? rt : ro;
     return rc;
 }
