@@ -43,8 +43,9 @@
  *
  * Shared memory (per CTA): Q rope dims 8 KB (SW64 [128x32]), 3 page stages of
  * 36 KB, an exchange out buffer and two in slots of 32 KB (partial scores,
- * then P), a 6 KB row-statistics buffer, barriers.  TMEM: S at columns 0 and
- * 64, Q at 128, O at 256..511.
+ * then P), a 3 KB row-statistics buffer, per stage the token scales (256 B)
+ * and rope codes (2 KB) of quantised pools, barriers.  TMEM: S at columns 0
+ * and 64, Q at 128, O at 256..511.
  *
  * Every wait is bounded (about two seconds of clock); on expiry the kernel
  * records an error word, drains its own TMA loads, copies and MMAs, frees
@@ -85,13 +86,15 @@ constexpr uint32_t kOffIn = kOffOut + kXBytes;         /* two receive slots */
 constexpr uint32_t kOffRed = kOffIn + 2 * kXBytes;
 constexpr uint32_t kRedBytes = 3 * kParts * kH * 4;     /* row max [2 parities][parts], row sum [parts] */
 constexpr uint32_t kOffScale = kOffRed + kRedBytes;    /* per stage: 64 fp32 token scales (quantised pools) */
-constexpr uint32_t kOffBar = kOffScale + kStages * 256;
+constexpr uint32_t kOffRc = kOffScale + kStages * 256;  /* per stage: the rope codes, 64 x 32 bytes (quantised pools) */
+constexpr uint32_t kOffBar = kOffRc + kStages * 2048;
 constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffTmem = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemUsed = kOffTmem + 16;
 constexpr uint32_t kSmemAlloc = kSmemUsed + 1024;       /* slack to align the base to 1024 B */
 static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
 static_assert(kOffKv % 1024 == 0 && kOffOut % 1024 == 0 && kOffIn % 1024 == 0, "swizzle atoms need 1 KB alignment");
+static_assert(kOffRc % 128 == 0, "TMA destination alignment");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;      /* 2 x 64 columns: fp32 scores */
 constexpr uint32_t kTmemQ = 128;    /* 128 columns, bf16 query latent dims of the half */
@@ -271,12 +274,13 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
                         for (int b = 0; b < 4; b++) tma_load_2d(dst + b * 8192, kv_lat, rank * 256 + b * 64, y, fb);
                         tma_load_2d(dst + 4 * 8192, kv_rope, 512 + rank * 32, y, fb);
                     } else {
-                        /* 8-bit codes into the upper half of each bf16 box (the
-                         * converter widens them in place), and the page's scales */
+                        /* 8-bit latent codes into the upper half of each bf16 box
+                         * (the converter widens them in place), the rope codes
+                         * beside the stages, and the page's scales */
                         mbar_expect_tx(fb, kCodeBytes);
                         for (int b = 0; b < 4; b++)
                             tma_load_2d(dst + b * 8192 + 4096, kv_lat, rank * 256 + b * 64, y, fb);
-                        tma_load_2d(dst + 4 * 8192 + 2048, kv_rope, 512 + rank * 32, y, fb);
+                        tma_load_2d(c.s + kOffRc + st * 2048, kv_rope, 512 + rank * 32, y, fb);
                         bulk_load(c.s + kOffScale + st * 256, p.scales + (size_t)pg * kP, 256, fb);
                     }
                 }
@@ -842,37 +846,45 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
 /* ---- warps 15-18 (int8 / e4m3 pools): codes -> bf16 in place -------------- */
 
 /* 16 codes (one 16-byte chunk) -> 16 bf16 values as two 16-byte chunks.
- * Every int8 and e4m3 value is exactly representable in bf16. */
+ * Every int8 and e4m3 value is exactly representable in bf16, so a value's
+ * bf16 is the upper half of its fp32.  int8 without a conversion
+ * instruction: the code + 128 (its byte xor 0x80) becomes the low byte of
+ * the fp32 2^23 (bits 0x4B000000), and subtracting 2^23 + 128 leaves the
+ * code exactly (integers below 2^24).  e4m3 by the paired conversion to
+ * f16x2 and f32. */
 template <int KV>
 __device__ __forceinline__ void widen16(const uint4 &c, uint4 &lo, uint4 &hi) {
-    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
     uint32_t o[8];
-    #pragma unroll
-    for (int i = 0; i < 8; i++) {                      /* codes 2i, 2i+1 */
-        const uint32_t pair = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
-        float f0, f1;
-        if (KV == CT_KV_INT8) {
-            f0 = (float)(int8_t)(pair & 0xFF);
-            f1 = (float)(int8_t)(pair >> 8);
-        } else {
-            const float2 f = ct_e4m3x2_to_f32x2((uint16_t)pair);
-            f0 = f.x;
-            f1 = f.y;
+    if (KV == CT_KV_INT8) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        #pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t pair = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+            const float f0 = (float)(int8_t)(pair & 0xFF), f1 = (float)(int8_t)(pair >> 8);
+            o[i] = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632u);
         }
-        o[i] = bf16x2_rn(f0, f1);
+    } else {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        #pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float2 f = ct_e4m3x2_to_f32x2((uint16_t)((w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu));
+            o[i] = __byte_perm(__float_as_uint(f.x), __float_as_uint(f.y), 0x7632u);
+        }
     }
     lo = make_uint4(o[0], o[1], o[2], o[3]);
     hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-/* The TMA put each box's codes in the upper half of its bf16 box (latent:
- * 64 rows x 64 codes at +4 KB of an 8 KB SW128 box; rope: 64 x 32 at +2 KB of
- * a 4 KB SW64 box).  A warp owns whole boxes (latent box w, the rope box
- * for the last warp): it loads all of a box's codes into registers, then
- * writes the bf16 rows over them, so no other warp's codes are overwritten.
- * Latent rows past the page's tokens become zeros (they are V rows of GEMM2). */
+/* The TMA put each latent box's codes in the upper half of its bf16 box
+ * (64 rows x 64 codes at +4 KB of an 8 KB SW128 box) and the rope codes
+ * (64 rows x 32) in a 2 KB area of their own.  Warp w owns latent box w: it
+ * loads all of the box's codes into registers, then writes the bf16 rows
+ * over them, so no other warp's codes are overwritten; it also converts rope
+ * rows [16w, 16w+16) into the SW64 rope box.  Latent rows past the page's
+ * tokens become zeros (they are V rows of GEMM2). */
 template <int KV>
 __device__ void converter(const Ctx &c, const Params &p, int wbeg, int wend) {
+    static_assert(kConvWarps == 4, "one latent box and a quarter of the rope box per warp");
     const uint32_t lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - kFirstConvWarp;
     uint32_t g = 0;
     bool ok = true;
@@ -885,37 +897,27 @@ __device__ void converter(const Ctx &c, const Params &p, int wbeg, int wend) {
             const uint32_t st = g % kStages;
             if (!wait_warp(c, bar(c, B_KV_FULL + st), (g / kStages) & 1, false, 19)) { ok = false; break; }
             uint8_t *kv = c.smem + kOffKv + st * kKvBytes;
-            #pragma unroll 1
-            for (int bi = 0; bi < 4 / kConvWarps; bi++) {
-                uint8_t *box = kv + (cw + kConvWarps * bi) * 8192;
-                uint4 code[8];
-                #pragma unroll
-                for (int k = 0; k < 8; k++) code[k] = reinterpret_cast<const uint4 *>(box + 4096)[lane + 32 * k];
-                __syncwarp();
-                #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    const uint32_t idx = lane + 32 * k, row = idx >> 2, cc = idx & 3;
-                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                    if ((int32_t)row < ntok) widen16<KV>(code[k], lo, hi);
-                    *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc) ^ (row & 7)) << 4)) = lo;
-                    *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc + 1) ^ (row & 7)) << 4)) = hi;
-                }
-                __syncwarp();
+            uint8_t *box = kv + cw * 8192;
+            uint4 code[8];
+            #pragma unroll
+            for (int k = 0; k < 8; k++) code[k] = reinterpret_cast<const uint4 *>(box + 4096)[lane + 32 * k];
+            const uint4 rc = reinterpret_cast<const uint4 *>(c.smem + kOffRc + st * 2048)[32 * cw + lane];
+            __syncwarp();
+            #pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t idx = lane + 32 * k, row = idx >> 2, cc = idx & 3;
+                uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                if ((int32_t)row < ntok) widen16<KV>(code[k], lo, hi);
+                *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc) ^ (row & 7)) << 4)) = lo;
+                *reinterpret_cast<uint4 *>(box + row * 128 + (((2 * cc + 1) ^ (row & 7)) << 4)) = hi;
             }
-            if (cw == kConvWarps - 1) {
-                uint8_t *box = kv + 4 * 8192;
-                uint4 code[4];
-                #pragma unroll
-                for (int k = 0; k < 4; k++) code[k] = reinterpret_cast<const uint4 *>(box + 2048)[lane + 32 * k];
-                __syncwarp();
-                #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const uint32_t idx = lane + 32 * k, row = idx >> 1, cc = idx & 1, sw = (row >> 1) & 3;
-                    uint4 lo, hi;
-                    widen16<KV>(code[k], lo, hi);
-                    *reinterpret_cast<uint4 *>(box + row * 64 + (((2 * cc) ^ sw) << 4)) = lo;
-                    *reinterpret_cast<uint4 *>(box + row * 64 + (((2 * cc + 1) ^ sw) << 4)) = hi;
-                }
+            {
+                uint8_t *rbox = kv + 4 * 8192;
+                const uint32_t idx = 32 * cw + lane, row = idx >> 1, cc = idx & 1, sw = (row >> 1) & 3;
+                uint4 lo, hi;
+                widen16<KV>(rc, lo, hi);
+                *reinterpret_cast<uint4 *>(rbox + row * 64 + (((2 * cc) ^ sw) << 4)) = lo;
+                *reinterpret_cast<uint4 *>(rbox + row * 64 + (((2 * cc + 1) ^ sw) << 4)) = hi;
             }
             proxy_fence();                             /* generic writes -> the tensor core's view */
             warp_arrive(bar(c, B_CONV_FULL + st));
