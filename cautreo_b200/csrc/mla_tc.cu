@@ -162,6 +162,7 @@ struct Params {
     uint32_t maxp;
     uint32_t n_pages;
     float qk_scale;          /* scale * log2(e) */
+    int out32;               /* out is 32-B aligned: the epilogue writes whole sectors */
 };
 
 /* Warp-cooperative walk over the pages of a chunk that hold tokens: lanes
@@ -215,14 +216,24 @@ __device__ __forceinline__ ct_mla_chunk_t load_chunk(const Params &p, int ci) {
     return ch;
 }
 
-/* Tiles of a chunk (warp-collective). */
+/* Tiles of a chunk (warp-collective): the pages WarpTiles would hand out,
+ * counted with all of the chunk's block-table loads in flight at once (16
+ * per lane), so that a role starting a chunk of hundreds of pages does not
+ * wait for one load per 32 pages in turn. */
 __device__ __forceinline__ uint32_t count_tiles(const ct_mla_chunk_t &ch, const Params &p) {
-    WarpTiles it;
-    it.init(ch, p);
-    int32_t pg, ntok;
-    uint32_t n = 0;
-    while (it.next(pg, ntok)) n++;
-    return n;
+    const int32_t *row = p.bt + (size_t)ch.row * p.maxp;
+    const int32_t len = p.lens[ch.row];
+    const int32_t lim = len > 0 ? min(ch.page_end, (len + kP - 1) / kP) : 0;
+    const int32_t lane = (int32_t)(threadIdx.x & 31);
+    uint32_t cnt = 0;
+    for (int32_t b = ch.page_begin + lane; b < lim; b += 32 * 16) {
+        int32_t v[16];
+        #pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = b + 32 * k < lim ? __ldg(row + b + 32 * k) : -1;
+        #pragma unroll
+        for (int k = 0; k < 16; k++) cnt += (v[k] >= 0 && (uint32_t)v[k] < p.n_pages) ? 1u : 0u;
+    }
+    return __reduce_add_sync(0xFFFFFFFFu, cnt);
 }
 
 /* ---- warp 0: TMA producer (lane 0 issues) -------------------------------- */
@@ -234,6 +245,10 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
     const bool leader = (threadIdx.x & 31) == 0;
     uint32_t g = 0;
     bool ok = true;
+    /* The queries of a chunk (128 heads x 576 values) go into L2 ahead of
+     * the staging warps, which load them into TMEM when the previous chunk's
+     * GEMM1s are done; the first chunk's as early as possible. */
+    if (leader && wbeg < wend) bulk_prefetch_l2(p.q + (size_t)load_chunk(p, wbeg).seq * kH * kE, kH * kE * 2);
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
         WarpTiles it;
@@ -257,11 +272,19 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
             ah_ok = ah.next(apg, antok);
             if (ah_ok) prefetch(apg);
         }
-        /* the chunk's queries (128 heads x 576 values) into L2, a few tiles
-         * before the staging warps load them; the staging warps also issue
-         * the rope dims' TMA load, so this loop never waits for the previous
-         * chunk's GEMM1s */
-        if (leader) bulk_prefetch_l2(p.q + (size_t)ch.seq * kH * kE, kH * kE * 2);
+        /* the next chunk's queries when the look-ahead reaches the end of
+         * this chunk, ~6 tiles before the staging warps load them: earlier,
+         * a long chunk's page stream would evict them from L2 again (the
+         * staging warps also issue the rope dims' TMA load, so this loop
+         * never waits for the previous chunk's GEMM1s) */
+        bool q_next = ci + 1 < wend;
+        auto prefetch_q_next = [&]() {
+            if (!q_next) return;
+            const int32_t nseq = load_chunk(p, ci + 1).seq;
+            if (leader) bulk_prefetch_l2(p.q + (size_t)nseq * kH * kE, kH * kE * 2);
+            q_next = false;
+        };
+        if (!ah_ok) prefetch_q_next();
         do {
             const uint32_t st = g % kStages;
             if (leader) {
@@ -290,6 +313,7 @@ __device__ void producer(const Ctx &c, const Params &p, const CUtensorMap *kv_la
             if (ah_ok) {
                 ah_ok = ah.next(apg, antok);
                 if (ah_ok) prefetch(apg);
+                else prefetch_q_next();
             }
             g++;
         } while (it.next(pg, ntok));
@@ -665,21 +689,26 @@ __device__ void stager(const Ctx &c, const Params &p, const CUtensorMap *q_rope,
     const uint32_t xf_peer = mapa(bar(c, B_X_FULL), c.peer);
     for (int ci = wbeg; ci < wend && ok; ci++) {
         const ct_mla_chunk_t ch = load_chunk(p, ci);
-        const uint32_t n = count_tiles(ch, p);
-        if (n == 0) continue;
         /* this CTA's 256 latent dims of the chunk's Q (this thread: head
          * `row`) into TMEM as soon as the previous chunk's GEMM1s are done,
-         * while the softmax warps may still be finishing that chunk: the
-         * first half is loaded before that wait (the producer prefetched the
-         * chunk's queries into L2), the second half after it; quadrant 0
-         * issues the rope dims' TMA load into shared memory */
+         * while the softmax warps may still be finishing that chunk.  The
+         * producer prefetched the chunk's queries into L2; the first quarter
+         * is loaded before the chunk's pages are counted (a block-table walk)
+         * and before that wait.  Quadrant 0 issues the rope dims' TMA load
+         * into shared memory. */
         const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)ch.seq * kH + row) * kE + rank * 256);
         uint32_t u[32];
-        #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const uint4 v = __ldg(src + k);
-            u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
-        }
+        auto load8 = [&](int q64) {
+            if (q64 < 3) prefetch_l1(src + (q64 + 1) * 8);     /* the next quarter's 128 bytes */
+            #pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint4 x = __ldg(src + q64 * 8 + k);
+                u[4 * k] = x.x; u[4 * k + 1] = x.y; u[4 * k + 2] = x.z; u[4 * k + 3] = x.w;
+            }
+        };
+        load8(0);
+        const uint32_t n = count_tiles(ch, p);
+        if (n == 0) continue;
         if (!(ok = wait_warp(c, bar(c, B_Q_EMPTY), (nq & 1) ^ 1, false, 17))) break;
         tc_fence_after();
         if (quad == 0 && lane == 0) {
@@ -689,11 +718,7 @@ __device__ void stager(const Ctx &c, const Params &p, const CUtensorMap *q_rope,
         tmem_st32(tmem + lane_base + kTmemQ, u);
         #pragma unroll 1
         for (int q64 = 1; q64 < 4; q64++) {
-            #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint4 v = __ldg(src + q64 * 8 + k);
-                u[4 * k] = v.x; u[4 * k + 1] = v.y; u[4 * k + 2] = v.z; u[4 * k + 3] = v.w;
-            }
+            load8(q64);
             tmem_st32(tmem + lane_base + kTmemQ + q64 * 32, u);
         }
         tmem_wait_st();
@@ -809,21 +834,26 @@ __device__ void softmax_warps(const Ctx &c, const Params &p, uint32_t tmem, int 
             tmem_ld32(tmem + r.lane_base + kTmemO + r.part * kOCols + cc * 32, o);
             tmem_wait_ld();
             const uint32_t d0 = d_base + cc * 32;
+            /* a lane writes 32 consecutive values of its head row: whole
+             * 32-byte sectors (the split-KV partials always, the bf16 output
+             * when it is 32-B aligned) */
             if (ch.part < 0) {
-                uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d0);
+                uint32_t w[16];
                 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    uint32_t w[4];
+                for (int e = 0; e < 16; e++)
+                    w[e] = (uint32_t)ct_f32_to_bf16(o[2 * e] * inv) | ((uint32_t)ct_f32_to_bf16(o[2 * e + 1] * inv) << 16);
+                uint4 *dst = reinterpret_cast<uint4 *>(p.out + oh * kDv + d0);
+                if (p.out32) {
+                    st_global_v8(dst, w);
+                    st_global_v8(dst + 2, w + 8);
+                } else {
                     #pragma unroll
-                    for (int e = 0; e < 4; e++)
-                        w[e] = (uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e] * inv) |
-                               ((uint32_t)ct_f32_to_bf16(o[8 * k + 2 * e + 1] * inv) << 16);
-                    dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int k = 0; k < 4; k++) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
                 }
             } else {
-                float4 *dst = reinterpret_cast<float4 *>(p.part_o + ((size_t)ch.part * kH + r.row) * kDv + d0);
+                float *dst = p.part_o + ((size_t)ch.part * kH + r.row) * kDv + d0;
                 #pragma unroll
-                for (int k = 0; k < 8; k++) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                for (int k = 0; k < 4; k++) st_global_v8(dst + 8 * k, reinterpret_cast<const uint32_t *>(o + 8 * k));
             }
         }
         tc_fence_before();
@@ -1145,6 +1175,7 @@ extern "C" int ct__launch_mla_tc(const ct_mla_dims_t *dims, const ct_mla_chunk_t
     p.maxp = dims->max_pages_per_seq;
     p.n_pages = dims->n_pages;
     p.qk_scale = dims->scale * kLog2e;
+    p.out32 = ((uintptr_t)out & 31u) == 0;
     static bool attr_set[4] = {false, false, false, false};
     if (!attr_set[kv]) {
         int rc = ct__cuda_status(cudaFuncSetAttribute(kernel_for(kv), cudaFuncAttributeMaxDynamicSharedMemorySize,

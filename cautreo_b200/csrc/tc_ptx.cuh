@@ -73,6 +73,16 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, i
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y) : "memory");
 }
+/* 32-byte global store (address 32-B aligned): a lane writes a whole sector. */
+__device__ __forceinline__ void st_global_v8(void *dst, const uint32_t *w) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+}
+/* L1 prefetch of the global cache line holding addr. */
+__device__ __forceinline__ void prefetch_l1(const void *addr) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(addr));
+}
 /* L2 prefetch of a contiguous global range (16-B aligned, size a multiple of 16). */
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
