@@ -102,6 +102,29 @@ def test_mla_lse_and_splits():
         np.testing.assert_allclose(lse[s], ref, rtol=0, atol=5e-3)
 
 
+def test_mla_output_16_byte_aligned_equals_32_byte_aligned():
+    """An output that starts 16 bytes past a 32-byte boundary takes the
+    epilogue's 16-byte stores instead of its 32-byte ones: same bytes."""
+    lens = [700, 64, 2500, 1]
+    pool, bt, q = mla_case(lens, seed=6)
+    L = np.asarray(lens, np.int32)
+    plan = ct.MlaPlan(L, pool.shape[0], max_pages_per_seq=bt.shape[1], scale=MLA_SCALE)
+    n_out = len(lens) * MLA_H * MLA_DV
+    buf = empty((n_out + 16,), np.uint16)                 # 256-B aligned base
+    pd, qd, btd, ld = dev(pool), dev(q), dev(bt), dev(L)
+    outs = []
+    for off in (0, 8):                                    # 0 and 16 bytes in
+        buf.zero_()
+        plan.decode(qd.data_ptr(), pd.data_ptr(), None, btd.data_ptr(), ld.data_ptr(), buf.data_ptr() + 2 * off,
+                    None, stream())
+        outs.append(host(buf, np.uint16)[off:off + n_out].copy())
+    assert plan.tensor_cores
+    np.testing.assert_array_equal(outs[0], outs[1])
+    want = oracle.mla_decode_paged(pool, bt, lens, q, MLA_H, MLA_E, MLA_DV, PAGE, MLA_SCALE)
+    ok, mx, rel = close(oracle.bf16_to_f32(outs[1]).reshape(len(lens), MLA_H, MLA_DV), want)
+    assert ok, (mx, rel)
+
+
 def test_mla_evicted_pages_are_skipped():
     lens = [300, 300]
     pool, bt, q = mla_case(lens, seed=4)
