@@ -103,8 +103,8 @@ def mla_case(lens, seed=1, H=MLA_H, E=MLA_E, page=PAGE, extra_pages=0, outlier_b
 
 def close(got, want, atol=ATOL, rtol=RTOL):
     """Attention parity, elementwise: |got - want| <= atol + rtol * |want|
-    (2e-2 absolute, 1e-2 relative), the combined absolute/relative bound of
-    the north-star tolerance.  A pure 2e-2 absolute bound cannot hold for
+    (2e-2 absolute, 1e-2 relative), the combined absolute/relative bound the
+    decode path is held to.  A pure 2e-2 absolute bound cannot hold for
     bf16 outputs beyond 8 in magnitude, whose rounding step alone is 2^-4
     (outlier-heavy caches produce such outputs), hence the relative term.
     Returns (ok, max |err|, max excess over the bound)."""
