@@ -575,9 +575,14 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
     /* arm this quadrant's barrier of the slot for tile t + 2 (8 KB) */
     if (r.part == 0 && (r.tid & 31) == 0) mbar_expect_tx(bar(c, B_X_FULL + slot * 4 + r.quad), kXBytes / 4);
     /* quantised pages: the scores are code dot products; times the token's scale */
-    if (kQuant) {
+    if constexpr (kQuant) {                         /* packed pairs (f32x2), same roundings */
+        const float2 *sc2 = reinterpret_cast<const float2 *>(tok_scale);
         #pragma unroll
-        for (int i = 0; i < kTPT; i++) s[i] *= tok_scale[i];
+        for (int k = 0; k < kTPT / 2; k++) {
+            const float2 m = __fmul2_rn(make_float2(s[2 * k], s[2 * k + 1]), sc2[k]);
+            s[2 * k] = m.x;
+            s[2 * k + 1] = m.y;
+        }
     }
     /* the last page of a sequence masks the slots past its end (warp-uniform) */
     const bool partial = ntok < kP;
@@ -638,7 +643,8 @@ __device__ bool finish_tile(const Ctx &c, const Params &p, uint32_t tmem, Row &r
             w[k] = bf16x2_rn(p0, p1);
         } else if (!partial) {
             /* V = scale x codes: the scale folds into P */
-            w[k] = bf16x2_rn(p0 * tok_scale[2 * k], p1 * tok_scale[2 * k + 1]);
+            const float2 ps = __fmul2_rn(make_float2(p0, p1), reinterpret_cast<const float2 *>(tok_scale)[k]);
+            w[k] = bf16x2_rn(ps.x, ps.y);
         } else {
             const bool in0 = (int32_t)(r.part * kTPT + 2 * k) < ntok, in1 = (int32_t)(r.part * kTPT + 2 * k + 1) < ntok;
             w[k] = bf16x2_rn(in0 ? p0 * tok_scale[2 * k] : 0.0f, in1 ? p1 * tok_scale[2 * k + 1] : 0.0f);
