@@ -223,7 +223,7 @@ __device__ __forceinline__ ct_mla_chunk_t load_chunk(const Params &p, int ci) {
 __device__ __forceinline__ uint32_t count_tiles(const ct_mla_chunk_t &ch, const Params &p) {
     const int32_t *row = p.bt + (size_t)ch.row * p.maxp;
     const int32_t len = p.lens[ch.row];
-    const int32_t lim = len > 0 ? min(ch.page_end, (len + kP - 1) / kP) : 0;
+    const int32_t lim = len > 0 ? (int32_t)min((int64_t)ch.page_end, ((int64_t)len + kP - 1) / kP) : 0;
     const int32_t lane = (int32_t)(threadIdx.x & 31);
     uint32_t cnt = 0;
     for (int32_t b = ch.page_begin + lane; b < lim; b += 32 * 16) {
