@@ -132,7 +132,11 @@ int ct_mla_tc_error(int clear);
  * ct_kv_paged_write_slots; NULL skips the append), decodes, and copies
  * out_host ([n_seq][n_heads][v_dim] bf16) back.  Returns when out_host is
  * filled.  The plan keeps the device staging buffers between calls; pinned
- * host buffers give the fastest copies. */
+ * host buffers give the fastest copies.  Large steps are cut into sequence
+ * groups whose copies overlap the decode of other groups, on streams the
+ * plan owns (ordered after the work already queued on `stream`); all of
+ * them have finished when the call returns.  Calls on one plan must not
+ * overlap. */
 int ct_attn_mla_decode_step_host(ct_mla_plan_t *plan, const void *q_host, const void *entries_host,
                                  const int32_t *dest_slot, void *pool, float *scales,
                                  const int32_t *block_table, const int32_t *seq_lens, void *out_host,
