@@ -395,3 +395,45 @@ def test_mla_step_host(n_seq):
     oh2 = torch.empty_like(oh).pin_memory()
     plan.step_host(qh, None, None, pd, None, btd, ld, oh2, stream())
     assert torch.equal(oh, oh2)
+
+
+@pytest.mark.parametrize("dtype", [ct.CT_KV_INT8, ct.CT_KV_E4M3])
+def test_mla_step_host_quantised_pool(dtype):
+    """The host-buffer step over an int8 / e4m3 pool: the new tokens are
+    quantised on append exactly as the oracle codes them (codes and scales
+    bit-exact), and the decode, cut into sequence groups on two streams,
+    matches the oracle on the dequantised pool (a sample of the sequences)."""
+    n_seq = 40                                                  # ~11 MB of copies: three sequence groups
+    lens = oracle.lengths_loguniform(oracle.key(23, 1), n_seq, 64, 2000).astype(np.int32)
+    lens_after = lens + 1
+    pool16, bt, q = mla_case(lens_after, seed=23, outlier_bp=100, outlier_mul=20.0)
+    NP = pool16.shape[0]
+    xf = np.ascontiguousarray(oracle.bf16_to_f32(pool16.reshape(-1)).reshape(NP * PAGE, MLA_E))
+    codes = np.zeros(NP * PAGE * MLA_E, np.uint8)
+    sc = np.zeros(NP * PAGE, np.float32)
+    quant = O.orc_kv_quant_int8 if dtype == ct.CT_KV_INT8 else O.orc_kv_quant_e4m3
+    quant(xf.ctypes.data, NP * PAGE, MLA_E, codes.ctypes.data, sc.ctypes.data)
+    codes = codes.reshape(NP * PAGE, MLA_E)
+    slots = np.array([bt[s, n // PAGE] * PAGE + n % PAGE for s, n in enumerate(lens)], np.int32)
+    new = pool16.reshape(NP * PAGE, MLA_E)[slots]
+    codes_before, sc_before = codes.copy(), sc.copy()
+    codes_before[slots] = 0x7F if dtype == ct.CT_KV_E4M3 else 0x80   # stale until the step writes the token
+    sc_before[slots] = np.nan
+    plan = ct.MlaPlan(lens_after, NP, max_pages_per_seq=bt.shape[1], kv_dtype=dtype, scale=MLA_SCALE)
+    pd, sd_, btd, ld, slotd = dev(codes_before), dev(sc_before), dev(bt), dev(lens_after), dev(slots)
+    qh, eh = _pinned(q), _pinned(new)
+    oh = torch.empty((n_seq, MLA_H, MLA_DV), dtype=torch.int16).pin_memory()
+    plan.step_host(qh, eh, slotd, pd, sd_, btd, ld, oh, stream())
+    assert np.array_equal(host(pd, np.uint8).reshape(NP * PAGE, MLA_E), codes)
+    assert np.array_equal(host(sd_, np.float32), sc)
+    got = oracle.bf16_to_f32(oh.numpy().view(np.uint16)).reshape(n_seq, MLA_H, MLA_DV)
+    back = np.zeros(NP * PAGE * MLA_E, np.float32)
+    dequant = O.orc_kv_dequant_int8 if dtype == ct.CT_KV_INT8 else O.orc_kv_dequant_e4m3
+    cc = np.ascontiguousarray(codes.reshape(-1))
+    dequant(cc.ctypes.data, sc.ctypes.data, NP * PAGE, MLA_E, back.ctypes.data)
+    sub = sorted(set(np.argsort(lens)[[0, 1, n_seq // 3, n_seq // 2, n_seq - 2, n_seq - 1]].tolist()))
+    qf = oracle.bf16_to_f32(q.reshape(-1)).reshape(q.shape)
+    want = oracle_decode_f32(back.reshape(NP, PAGE, MLA_E), bt[sub], lens_after[sub], qf[sub], MLA_H, MLA_E, MLA_DV,
+                             PAGE)
+    ok, mx, rel = close(got[sub], want)
+    assert ok, (mx, rel)
